@@ -1,0 +1,497 @@
+#!/usr/bin/env python3
+"""Attention-forward benchmark on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
+
+Headline (`value`): prefill, non-causal, H_q=32, H_kv=8 (GQA 4:1), D=128,
+S_q=S_kv=4096, fp16 in / fp32 out, one sequence per GPU (global batch = N,
+batch-sharded, no communication): whole-job TFLOP/s with
+FLOPs = 4*B*H_q*S_q*S_kv*D (the reference benchmark's formula,
+tests/bench_flash_attn.cu:125-127).  A step is one attention forward of the
+rank's batch; inputs are resident in HBM and rotate over 4 buffer sets
+(448 MiB > 2x the 126 MB L2).  `e2e` is the same metric through the public
+API (flash_attn_fwd) with the step's Q/K/V copied from pinned host memory and
+O copied back inside the timed region.  `extra` holds the decode configs
+(HBM GB/s with bytes = 2*B*H_kv*S_kv*D*2 + 2*B*H_q*D + 4*B*H_q*D), MQA D=64,
+prefill S=512 and, for N > 1, the KV-split long decode across the N GPUs.
+
+--impl reference times the reference's CPU path for the same workload: the
+NumPy reference_attn of kernel_models/flash_attn.py (restated in oracle/, the
+reference tree does not travel), fp32, BLAS threads = host cores, each step a
+bounded sample of query heads; rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from datetime import timedelta
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "prefill TFLOP/s & decode HBM GB/s (H_q32/H_kv8/D128) at 1/2/4/8 B200"
+H_Q, H_KV, D, S = 32, 8, 128, 4096
+ROTATE = 4
+MIB = 1 << 20
+
+
+def prefill_flops(B, H_q, S_q, S_kv, D_):
+    return 4.0 * B * H_q * S_q * S_kv * D_
+
+
+def decode_bytes(B, H_q, H_kv, S_kv, D_):
+    return 2.0 * B * H_kv * S_kv * D_ * 2 + 2.0 * B * H_q * D_ + 4.0 * B * H_q * D_
+
+
+def workload_config(world):
+    return {
+        "workload": "prefill non-causal H_q=32 H_kv=8 D=128 S_q=S_kv=4096, fp16 in / fp32 out, "
+                    "1 sequence per GPU (batch-sharded)",
+        "global_batch": world,
+        "seq_len": S,
+        "heads_q": H_Q,
+        "heads_kv": H_KV,
+        "head_dim": D,
+        "parallelism": f"batch-shard x{world} (no collective)",
+        "l2": f"inputs rotate over {ROTATE} HBM-resident sets ({ROTATE * 112} MiB > 2x L2)",
+    }
+
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained"), "src": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "src": "fallback"}
+
+
+def profile_traffic(name):
+    """dram bytes per launch from a committed ncu summary line 'traffic_bytes_per_launch: N'."""
+    path = os.path.join(REPO, "profiles", name)
+    try:
+        for line in open(path):
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------- clocks
+_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+            0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+            0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+BAD_REASONS = {"hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown"}
+
+
+class ClockSampler:
+    """Polls this rank's GPU (NVML) every few ms while the timed region runs."""
+
+    def __init__(self, cuda_index, period_s=0.005):
+        self.period = period_s
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._h = None
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            uuid = str(torch.cuda.get_device_properties(cuda_index).uuid)
+            try:
+                self._h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            except Exception:
+                self._h = pynvml.nvmlDeviceGetHandleByIndex(cuda_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._h = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._h is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._h is not None:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        names = sorted(n for bit, n in _REASONS.items() if self.reasons & bit and n != "gpu_idle")
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------- helpers
+def rand_f16(shape, gen, device):
+    import torch
+
+    return torch.randn(shape, generator=gen, device=device, dtype=torch.float32).to(torch.float16)
+
+
+def time_loop(fn, iters, warmup, stream):
+    """Mean ms per call over `iters` back-to-back calls (CUDA events on `stream`)."""
+    import torch
+
+    for i in range(warmup):
+        fn(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(iters):
+        fn(i)
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def max_over_ranks(vals, world, device):
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor(vals, dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+# ---------------------------------------------------------------- our arm
+def run_prefill_headline(args, rank, world, dev):
+    import torch
+    import torch.distributed as dist
+
+    from kernelfoundry_b200 import flash_attn_fwd, plan
+
+    stream = torch.cuda.current_stream(dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1002 + 7919 * rank)
+    qs = [rand_f16((1, H_Q, S, D), gen, dev) for _ in range(ROTATE)]
+    ks = [rand_f16((1, H_KV, S, D), gen, dev) for _ in range(ROTATE)]
+    vs = [rand_f16((1, H_KV, S, D), gen, dev) for _ in range(ROTATE)]
+    os_ = [torch.empty((1, H_Q, S, D), dtype=torch.float32, device=dev) for _ in range(ROTATE)]
+    assert plan(1, H_Q, H_KV, S, S, D)["path"] == "prefill"
+
+    def step(i):
+        j = i % ROTATE
+        flash_attn_fwd(qs[j], ks[j], vs[j], out=os_[j])
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+
+    def timed():
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier(device_ids=[dev.index])
+        torch.cuda.synchronize()
+        with ClockSampler(dev.index) as cs:
+            t0.record(stream)
+            for i in range(args.steps):
+                ev[i][0].record(stream)
+                step(i)
+                ev[i][1].record(stream)
+            t1.record(stream)
+            torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier(device_ids=[dev.index])
+        total_ms = t0.elapsed_time(t1)
+        kern_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+        return total_ms, kern_ms, cs.summary()
+
+    total_ms, kern_ms, clocks = timed()
+    if set(clocks["reasons"]) & BAD_REASONS:           # rejected clocks: measure once more
+        total_ms, kern_ms, clocks = timed()
+    total_ms, kern_ms = max_over_ranks([total_ms, kern_ms], world, dev)
+    if world > 1:
+        all_clocks = [None] * world
+        dist.all_gather_object(all_clocks, clocks)
+    else:
+        all_clocks = [clocks]
+    ms_per_step = total_ms / args.steps
+    del qs, ks, vs, os_
+    torch.cuda.empty_cache()
+    return ms_per_step, kern_ms, all_clocks
+
+
+def run_prefill_e2e(args, rank, world, dev):
+    """Same workload through the public API with host buffers; H2D + kernel + D2H per step."""
+    import torch
+    import torch.distributed as dist
+
+    from kernelfoundry_b200 import flash_attn_fwd
+
+    stream = torch.cuda.current_stream(dev)
+    g = torch.Generator().manual_seed(2002 + rank)
+    hq = torch.randn((1, H_Q, S, D), generator=g).to(torch.float16).pin_memory()
+    hk = torch.randn((1, H_KV, S, D), generator=g).to(torch.float16).pin_memory()
+    hv = torch.randn((1, H_KV, S, D), generator=g).to(torch.float16).pin_memory()
+    ho = torch.empty((1, H_Q, S, D), dtype=torch.float32).pin_memory()
+    dq, dk, dv = (torch.empty_like(x, device=dev) for x in (hq, hk, hv))
+    do = torch.empty((1, H_Q, S, D), dtype=torch.float32, device=dev)
+
+    def step(_):
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        flash_attn_fwd(dq, dk, dv, out=do)
+        ho.copy_(do, non_blocking=True)
+
+    if world > 1:
+        dist.barrier(device_ids=[dev.index])
+    ms = time_loop(step, args.steps, args.warmup, stream)
+    (ms,) = max_over_ranks([ms], world, dev)
+    h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv))
+    d2h = ho.numel() * ho.element_size()
+    return ms, h2d, d2h
+
+
+def run_extras(args, rank, world, dev, peaks):
+    """Decode (C3), long decode (C5), MQA (C4), short prefill (C1) on this rank's GPU."""
+    import torch
+
+    from kernelfoundry_b200 import flash_attn_fwd, plan
+
+    stream = torch.cuda.current_stream(dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4242)
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    iters = max(10, min(args.steps, 50))
+    out = {}
+
+    def bench_cfg(B, Hq, Hkv, Sq, Skv, Dh):
+        one = (B * Hq * Sq * Dh * 2 + 2 * B * Hkv * Skv * Dh * 2 + B * Hq * Sq * Dh * 4)
+        rot = max(1, min(16, -(-2 * l2 // one) + 1)) if one < 2 * l2 else 1
+        qs = [rand_f16((B, Hq, Sq, Dh), gen, dev) for _ in range(rot)]
+        ks = [rand_f16((B, Hkv, Skv, Dh), gen, dev) for _ in range(rot)]
+        vs = [rand_f16((B, Hkv, Skv, Dh), gen, dev) for _ in range(rot)]
+        os_ = [torch.empty((B, Hq, Sq, Dh), dtype=torch.float32, device=dev) for _ in range(rot)]
+
+        def f(i):
+            j = i % rot
+            flash_attn_fwd(qs[j], ks[j], vs[j], out=os_[j])
+
+        ms = time_loop(f, iters, 3, stream)
+        pl = plan(B, Hq, Hkv, Sq, Skv, Dh)
+        del qs, ks, vs, os_
+        return ms, rot, pl
+
+    for B in (1, 16, 64):
+        ms, rot, pl = bench_cfg(B, H_Q, H_KV, 1, 4096, D)
+        gbs = decode_bytes(B, H_Q, H_KV, 4096, D) / (ms * 1e-3) / 1e9
+        out[f"decode_kv4096_B{B}"] = {"us": round(ms * 1e3, 2), "GB/s": round(gbs, 1),
+                                      "frac_hbm": round(gbs / peaks["hbm_gbs"], 3), "n_split": pl["n_split"],
+                                      "rotated_sets": rot}
+    ms, rot, pl = bench_cfg(1, H_Q, H_KV, 1, 131072, D)
+    gbs = decode_bytes(1, H_Q, H_KV, 131072, D) / (ms * 1e-3) / 1e9
+    out["long_decode_kv131072_1gpu"] = {"us": round(ms * 1e3, 2), "GB/s": round(gbs, 1),
+                                        "frac_hbm": round(gbs / peaks["hbm_gbs"], 3), "n_split": pl["n_split"]}
+    ms, rot, pl = bench_cfg(4, 32, 1, 2048, 2048, 64)
+    tf = prefill_flops(4, 32, 2048, 2048, 64) / (ms * 1e-3) / 1e12
+    out["mqa_d64_B4_S2048"] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 1),
+                               "frac_tensor": round(tf / peaks["bf16_tflops"], 3)}
+    ms, rot, pl = bench_cfg(1, H_Q, H_KV, 512, 512, D)
+    tf = prefill_flops(1, H_Q, 512, 512, D) / (ms * 1e-3) / 1e12
+    out["prefill_S512_B1"] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 1)}
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_long_decode_split(args, rank, world, dev, peaks):
+    """C5 across the N GPUs: KV split by ranges, partials + one all-gather + LSE merge."""
+    import torch
+    import torch.distributed as dist
+
+    from kernelfoundry_b200.multi_gpu import kv_shard, long_decode_forward
+
+    S_kv = 131072
+    lo, hi = kv_shard(S_kv, world, rank)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5005)
+    q = rand_f16((1, H_Q, 1, D), gen, dev)
+    gen.manual_seed(6006 + rank)
+    k = rand_f16((1, H_KV, hi - lo, D), gen, dev)
+    v = rand_f16((1, H_KV, hi - lo, D), gen, dev)
+    buf = torch.empty(world * (H_Q * D + 2 * H_Q), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    dist.barrier(device_ids=[dev.index])
+    ms = time_loop(lambda i: long_decode_forward(q, k, v, gather_buf=buf), max(10, min(args.steps, 50)), 3, stream)
+    (ms,) = max_over_ranks([ms], world, dev)
+    gbs = decode_bytes(1, H_Q, H_KV, S_kv, D) / (ms * 1e-3) / 1e9
+    return {"us": round(ms * 1e3, 2), "GB/s_total": round(gbs, 1), "GB/s_per_gpu": round(gbs / world, 1),
+            "frac_hbm_per_gpu": round(gbs / world / peaks["hbm_gbs"], 3), "collective": "1x all_gather (NCCL)"}
+
+
+def cpu_baseline_sample(budget_s=12.0):
+    """The reference's NumPy path (reference_attn restated), fp32, on a bounded sample of heads."""
+    import numpy as np
+
+    from oracle.attn_oracle import reference_attn
+
+    try:
+        from threadpoolctl import threadpool_info
+
+        threads = max((i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"), default=1)
+    except Exception:
+        threads = os.cpu_count() or 1
+    rng = np.random.default_rng(7)
+    K = rng.standard_normal((1, 1, S, D), dtype=np.float32).astype(np.float16).astype(np.float32)
+    V = rng.standard_normal((1, 1, S, D), dtype=np.float32).astype(np.float16).astype(np.float32)
+    done = 0
+    t0 = time.perf_counter()
+    while done < H_Q and time.perf_counter() - t0 < budget_s:
+        Qh = rng.standard_normal((1, 1, S, D), dtype=np.float32).astype(np.float16).astype(np.float32)
+        reference_attn(Qh, K, V)
+        done += 1
+    dt = time.perf_counter() - t0
+    tf = prefill_flops(1, done, S, S, D) / dt / 1e12
+    return {"value": round(tf, 5), "unit": "TFLOP/s", "cores": int(threads), "kind": "port",
+            "sample": f"{done} of {H_Q} query heads of one S=4096 D=128 sequence, fp32 NumPy "
+                      f"reference_attn (oracle restatement), {dt:.1f} s"}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus and "RANK" in os.environ:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    peaks = load_peaks()
+
+    ms_step, kern_ms, clocks = run_prefill_headline(args, rank, world, dev)
+    flops_rank = prefill_flops(1, H_Q, S, S, D)
+    value = world * flops_rank / (ms_step * 1e-3) / 1e12
+    e2e_ms, h2d, d2h = run_prefill_e2e(args, rank, world, dev)
+    e2e_value = world * flops_rank / (e2e_ms * 1e-3) / 1e12
+
+    achieved = flops_rank / (kern_ms * 1e-3) / 1e12
+    traffic = profile_traffic("prefill_sm100_C2.md")
+    roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": traffic,
+                "kernel": "kf::prefill_fwd_kernel<128>", "kernel_ms": round(kern_ms, 5),
+                "flops_per_launch": flops_rank, "peak_src": f"{peaks['src']} bf16 dense (burst)"}
+
+    extra = {}
+    if not args.no_extras:
+        if rank == 0:
+            extra = run_extras(args, rank, world, dev, peaks)
+        if world > 1:
+            ld = run_long_decode_split(args, rank, world, dev, peaks)
+            if rank == 0:
+                extra[f"long_decode_kv131072_split_{world}gpu"] = ld
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded N(0,1) fp16)",
+        "config": workload_config(world),
+        "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
+        "gpu_launches": args.steps,
+        "roofline": roofline,
+        "clocks": {"sm_mhz": clocks[0]["sm_mhz"], "sm_max_mhz": clocks[0]["sm_max_mhz"],
+                   "reasons": sorted({r for c in clocks for r in c["reasons"]}),
+                   "per_gpu_median_mhz": [c["sm_mhz"] for c in clocks]},
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_sample()
+    if extra:
+        line["extra"] = extra
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[dev.index])
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------- reference arm
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    import numpy as np
+
+    from oracle.attn_oracle import reference_attn
+
+    try:
+        from threadpoolctl import threadpool_info
+
+        threads = max((i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"), default=1)
+    except Exception:
+        threads = os.cpu_count() or 1
+    heads = 2     # bounded sample per step: 2 of the 32 query heads (1/16 of the per-GPU work)
+    rng = np.random.default_rng(11)
+    Q = rng.standard_normal((1, heads, S, D), dtype=np.float32).astype(np.float16).astype(np.float32)
+    K = rng.standard_normal((1, 1, S, D), dtype=np.float32).astype(np.float16).astype(np.float32)
+    V = rng.standard_normal((1, 1, S, D), dtype=np.float32).astype(np.float16).astype(np.float32)
+    for _ in range(args.warmup):
+        reference_attn(Q, K, V)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        reference_attn(Q, K, V)
+    dt = (time.perf_counter() - t0) / args.steps
+    value = prefill_flops(1, heads, S, S, D) / dt / 1e12
+    sample = (f"{heads} of {H_Q} query heads (GQA group of one KV head) of one S=4096 D=128 sequence per step, "
+              f"fp32 NumPy reference_attn (restated from kernel_models/flash_attn.py:250-265)")
+    line = {
+        "metric": METRIC, "value": round(value, 5), "unit": "TFLOP/s", "impl": "reference", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) fp16-rounded)",
+        "config": workload_config(world),
+        "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": int(threads), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-extras", action="store_true", help="headline only (skip decode/MQA/long-decode lines)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

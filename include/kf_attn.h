@@ -1,0 +1,139 @@
+/*
+ * kf_attn.h -- C ABI of the B200 (sm_100a) attention forward.
+ *
+ * Drop-in boundary for the host launchers of sviraaj/kernelfoundry's
+ * flash-attention kernel.  Tensor layout and numerics are the reference's:
+ *   Q  [B, H_q,  S_q,  D]  fp16 (IEEE binary16 bits), row-major, device memory
+ *   K  [B, H_kv, S_kv, D]  fp16
+ *   V  [B, H_kv, S_kv, D]  fp16
+ *   O  [B, H_q,  S_q,  D]  fp32 output
+ *   Mi [B, H_q, S_q] fp32  row max of the scaled scores  (optional)
+ *   Li [B, H_q, S_q] fp32  sum of exp(score - Mi)         (optional)
+ *   score = (q . k) / sqrt(D); query head h uses KV head h / (H_q / H_kv).
+ * D must be 16, 64, 128 or 256 (the reference's instantiations,
+ * kernels/flash_attn.cu:589-600).  All pointers are device pointers (16-byte
+ * aligned for Q, K, V, O); `stream` is a cudaStream_t (NULL = legacy default
+ * stream).  Plain C types only: no CUDA or torch types in any signature.
+ *
+ * Every call returns KF_OK (0) or a KF_ERR_* code; none calls exit().
+ * kf_attn_* calls are asynchronous on `stream` and allocate nothing.
+ */
+#ifndef KF_ATTN_H_
+#define KF_ATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define KF_OK 0
+#define KF_ERR_INVALID_ARG 1          /* bad shape, null pointer, H_q % H_kv != 0, ... */
+#define KF_ERR_UNSUPPORTED_HEAD_DIM 2 /* D not in {16, 64, 128, 256} */
+#define KF_ERR_MISALIGNED 3           /* Q/K/V/O not 16-byte aligned */
+#define KF_ERR_CUDA 4                 /* a CUDA runtime call failed: kf_last_cuda_error() */
+#define KF_ERR_DEVICE_TIMEOUT 5       /* a bounded in-kernel wait expired */
+#define KF_ERR_UNSUPPORTED_DEVICE 6   /* the current device is not sm_100 */
+#define KF_ERR_WORKSPACE 7            /* workspace too small for an explicit request */
+
+/* Human-readable text for a status code (static storage, never NULL). */
+const char* kf_strerror(int code);
+
+/* cudaError_t value (as int) of the most recent failing CUDA call on this thread. */
+int kf_last_cuda_error(void);
+
+/* Library version string. */
+const char* kf_version(void);
+
+/* ---- attention forward --------------------------------------------------
+ * Replaces: launch_flash_attn(Q, K, V, O, B, S, H_q, H_kv, D, stream)
+ *           (tests/test_flash_attn.cu:52-113) and the general q_len/kv_len
+ *           launch of flash_attn_kernel<D> (tests/bench_flash_attn.cu:39-54,
+ *           raw kernel signature kernels/flash_attn.cu:384-398).
+ * Differences, by design: asynchronous (no stream synchronize), no per-call
+ * cudaMalloc of Mi/Li scratch (the softmax state stays on chip; short-query
+ * split-KV partials go to the caller's workspace).
+ *
+ * workspace: optional device buffer used by the split-KV decode path.  Size it
+ * with kf_attn_workspace_bytes(); zero-fill it once before its first use
+ * (kf_attn_workspace_init); every successful call leaves it ready for the
+ * next.  Two calls that overlap on the GPU must not share a workspace.
+ * workspace == NULL (or too small) is valid: the decode path then uses fewer
+ * KV splits (slower for small batches, same results).
+ */
+int kf_attn_fwd(const void* Q, const void* K, const void* V, float* O,
+                int B, int H_q, int H_kv, int S_q, int S_kv, int D,
+                void* workspace, size_t workspace_bytes, void* stream);
+
+/* Same, also writing the reference kernel's softmax state Mi/Li
+ * (kernels/flash_attn.cu:575-578).  Mi and/or Li may be NULL. */
+int kf_attn_fwd_lse(const void* Q, const void* K, const void* V, float* O,
+                    float* Mi, float* Li,
+                    int B, int H_q, int H_kv, int S_q, int S_kv, int D,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* Partial attention over the given K/V (e.g. one GPU's slice of a long KV
+ * cache): O_u = sum_j exp(s_j - m) v_j (un-normalised), m = max_j s_j,
+ * l = sum_j exp(s_j - m), with s_j the scaled scores.  Merge partials of
+ * disjoint KV slices with kf_attn_combine.  m and l must be non-NULL.
+ * No reference counterpart: the reference has no split-KV; this is the
+ * (Mi, Li, un-normalised O) state of its online softmax
+ * (kernels/flash_attn.cu:261-294) exported for a cross-GPU merge. */
+int kf_attn_fwd_partial(const void* Q, const void* K, const void* V,
+                        float* O_u, float* m, float* l,
+                        int B, int H_q, int H_kv, int S_q, int S_kv, int D,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* Log-sum-exp merge of n_parts partials stacked as
+ *   O_parts [n_parts][B*H_q*S_q][D], m_parts/l_parts [n_parts][B*H_q*S_q]
+ * into O [B,H_q,S_q,D] (normalised) and optional Mi/Li of the union.
+ * No reference counterpart (see kf_attn_fwd_partial). */
+int kf_attn_combine(const float* O_parts, const float* m_parts, const float* l_parts,
+                    int n_parts, float* O, float* Mi, float* Li,
+                    int B, int H_q, int S_q, int D, void* stream);
+
+/* Bytes of workspace the call with these arguments would use (0 if none). */
+size_t kf_attn_workspace_bytes(int B, int H_q, int H_kv, int S_q, int S_kv, int D);
+
+/* Zero-fill a workspace before its first use (cudaMemsetAsync on stream). */
+int kf_attn_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
+
+/* Execution plan the call would use, for tests and benchmarks:
+ *   *path = 0 prefill (tcgen05 kernel) or 1 decode (split-KV kernel);
+ *   *n_split = KV splits per (b, h_kv) (decode), *grid_ctas = CTAs launched. */
+int kf_attn_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t workspace_bytes,
+                 int* path, int* n_split, int* grid_ctas);
+
+/* Blocking, reference-compatible launcher: same arguments and semantics as
+ * launch_flash_attn (tests/test_flash_attn.cu:52-113): S_q = S_kv = S,
+ * synchronizes `stream` before returning, returns KF_* codes (the C++
+ * header kf_attn_compat.h maps them to cudaError_t).  Allocates nothing. */
+int kf_launch_flash_attn(const uint16_t* Q, const uint16_t* K, const uint16_t* V, float* O,
+                         int B, int S, int H_q, int H_kv, int D, void* stream);
+
+/* ---- device error word / bounded waits ----------------------------------
+ * Kernels never spin forever: each wait gives up after a wall-clock limit
+ * (default 1 s), records the failure in a per-device error word and unwinds.
+ * No reference counterpart (the reference has no waits that can time out). */
+
+/* Synchronizes the current device, returns KF_ERR_DEVICE_TIMEOUT if any
+ * kernel recorded an expired wait since the last clear (else KF_OK).
+ * clear != 0 resets the word.  *raw (nullable) receives the raw bits. */
+int kf_device_error(int clear, unsigned* raw);
+
+/* Set the in-kernel wait limit in nanoseconds (0 restores the default). */
+void kf_set_wait_timeout_ns(unsigned long long ns);
+
+/* Launch a one-CTA kernel that waits on a barrier nothing ever signals, with
+ * limit timeout_ns, then synchronizes.  Returns KF_ERR_DEVICE_TIMEOUT when the
+ * bounded wait expired as designed (and clears the error word): it proves
+ * the unwind path without faulting or hanging the GPU. */
+int kf_selftest_wait_timeout(unsigned long long timeout_ns, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* KF_ATTN_H_ */

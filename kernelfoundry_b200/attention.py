@@ -1,0 +1,190 @@
+"""Host API of the attention forward (torch tensors in, CUDA kernels underneath).
+
+Mirrors the reference's launcher interface (sviraaj/kernelfoundry,
+tests/test_flash_attn.cu:52-113 and tests/bench_flash_attn.cu:39-54):
+
+* :func:`launch_flash_attn` -- same name, arguments and meaning as the
+  reference's C++ launcher (raw device pointers, B, S, H_q, H_kv, D, stream),
+  blocking, returning a status code (0 = success) instead of raising, like the
+  reference's ``cudaError_t`` return.
+* :func:`flash_attn_fwd` -- the general q_len/kv_len form on torch tensors
+  ``[B, H, S, D]`` fp16 -> fp32, asynchronous on the current stream, with the
+  reference kernel's optional softmax state (Mi, Li).
+* :func:`flash_attn_partial` / :func:`combine_partials` -- (m, l, O_u) partials
+  over a KV slice and their log-sum-exp merge (cross-GPU split decode).
+
+torch only supplies device memory and the current stream; the arithmetic runs
+in libkf_attn.so (sm_100a).  Nothing here falls back to a CPU path.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import torch
+
+from ._lib import KFError, check, lib
+
+__all__ = [
+    "launch_flash_attn",
+    "flash_attn_fwd",
+    "flash_attn_partial",
+    "combine_partials",
+    "plan",
+    "workspace_bytes",
+    "device_error",
+    "KFError",
+]
+
+_ws_lock = threading.Lock()
+_ws_cache: dict[int, torch.Tensor] = {}
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _stream_handle(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _check_qkv(q, k, v):
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if not t.is_cuda:
+            raise ValueError(f"{name} must be a CUDA tensor (no CPU path)")
+        if t.dtype != torch.float16:
+            raise ValueError(f"{name} must be float16")
+        if t.dim() != 4 or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous [B, H, S, D] tensor")
+    B, H_q, S_q, D = q.shape
+    Bk, H_kv, S_kv, Dk = k.shape
+    if v.shape != k.shape or Bk != B or Dk != D:
+        raise ValueError("k/v shape mismatch with q")
+    if not (q.device == k.device == v.device):
+        raise ValueError("q, k, v must be on one device")
+    return B, H_q, H_kv, S_q, S_kv, D
+
+
+def workspace_bytes(B, H_q, H_kv, S_q, S_kv, D) -> int:
+    return int(lib().kf_attn_workspace_bytes(B, H_q, H_kv, S_q, S_kv, D))
+
+
+def _workspace(device: torch.device, nbytes: int):
+    """Per-device zero-initialised workspace, grown on demand.
+
+    Calls that overlap on the GPU (different streams) must not share it; use
+    the ``workspace=`` argument to give each stream its own.
+    """
+    if nbytes == 0:
+        return None
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    with _ws_lock:
+        ws = _ws_cache.get(idx)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+            _ws_cache[idx] = ws
+        return ws
+
+
+def new_workspace(nbytes: int, device=None) -> torch.Tensor:
+    """A private zero-filled workspace (for concurrent streams)."""
+    return torch.zeros(max(int(nbytes), 16), dtype=torch.uint8, device=device or torch.device("cuda"))
+
+
+def plan(B, H_q, H_kv, S_q, S_kv, D, workspace_bytes=2**62):
+    """Kernel selection for a call: {'path': 'prefill'|'decode', 'n_split', 'ctas'}."""
+    path, ns, ctas = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
+    check(lib().kf_attn_plan(B, H_q, H_kv, S_q, S_kv, D, workspace_bytes,
+                             ctypes.byref(path), ctypes.byref(ns), ctypes.byref(ctas)), "kf_attn_plan")
+    return {"path": "prefill" if path.value == 0 else "decode", "n_split": ns.value, "ctas": ctas.value}
+
+
+def flash_attn_fwd(q, k, v, *, out=None, return_lse=False, workspace=None):
+    """O = softmax(Q K^T / sqrt(D)) V per head; GQA head map h_kv = h_q // (H_q // H_kv).
+
+    q [B,H_q,S_q,D] fp16, k/v [B,H_kv,S_kv,D] fp16 (CUDA, contiguous) ->
+    O [B,H_q,S_q,D] fp32.  With ``return_lse`` also returns (Mi, Li), the
+    reference kernel's row max of the scaled scores and sum of exp(s - Mi).
+    """
+    B, H_q, H_kv, S_q, S_kv, D = _check_qkv(q, k, v)
+    dev = q.device
+    if out is None:
+        out = torch.empty((B, H_q, S_q, D), dtype=torch.float32, device=dev)
+    Mi = Li = None
+    if return_lse:
+        Mi = torch.empty((B, H_q, S_q), dtype=torch.float32, device=dev)
+        Li = torch.empty_like(Mi)
+    with torch.cuda.device(dev):
+        if workspace is None:
+            workspace = _workspace(dev, workspace_bytes(B, H_q, H_kv, S_q, S_kv, D))
+        wsb = workspace.numel() if workspace is not None else 0
+        rc = lib().kf_attn_fwd_lse(_ptr(q), _ptr(k), _ptr(v), _ptr(out), _ptr(Mi), _ptr(Li),
+                                   B, H_q, H_kv, S_q, S_kv, D, _ptr(workspace), wsb, _stream_handle(dev))
+    check(rc, "kf_attn_fwd_lse")
+    return (out, Mi, Li) if return_lse else out
+
+
+def flash_attn_partial(q, k, v, *, workspace=None):
+    """(O_u, m, l) over the given K/V: O_u = sum exp(s - m) v, m = max s, l = sum exp(s - m)."""
+    B, H_q, H_kv, S_q, S_kv, D = _check_qkv(q, k, v)
+    dev = q.device
+    O_u = torch.empty((B, H_q, S_q, D), dtype=torch.float32, device=dev)
+    m = torch.empty((B, H_q, S_q), dtype=torch.float32, device=dev)
+    l = torch.empty_like(m)
+    with torch.cuda.device(dev):
+        if workspace is None:
+            workspace = _workspace(dev, workspace_bytes(B, H_q, H_kv, S_q, S_kv, D))
+        wsb = workspace.numel() if workspace is not None else 0
+        rc = lib().kf_attn_fwd_partial(_ptr(q), _ptr(k), _ptr(v), _ptr(O_u), _ptr(m), _ptr(l),
+                                       B, H_q, H_kv, S_q, S_kv, D, _ptr(workspace), wsb, _stream_handle(dev))
+    check(rc, "kf_attn_fwd_partial")
+    return O_u, m, l
+
+
+def combine_partials(O_parts, m_parts, l_parts, *, out=None, return_lse=False):
+    """Merge stacked partials O_parts [G,B,H,S,D], m/l_parts [G,B,H,S] by log-sum-exp."""
+    if not (O_parts.is_cuda and m_parts.is_cuda and l_parts.is_cuda):
+        raise ValueError("partials must be CUDA tensors (no CPU path)")
+    G, B, H_q, S_q, D = O_parts.shape
+    O_parts = O_parts.contiguous()
+    m_parts = m_parts.contiguous()
+    l_parts = l_parts.contiguous()
+    dev = O_parts.device
+    if out is None:
+        out = torch.empty((B, H_q, S_q, D), dtype=torch.float32, device=dev)
+    Mi = Li = None
+    if return_lse:
+        Mi = torch.empty((B, H_q, S_q), dtype=torch.float32, device=dev)
+        Li = torch.empty_like(Mi)
+    with torch.cuda.device(dev):
+        rc = lib().kf_attn_combine(_ptr(O_parts), _ptr(m_parts), _ptr(l_parts), G, _ptr(out), _ptr(Mi), _ptr(Li),
+                                   B, H_q, S_q, D, _stream_handle(dev))
+    check(rc, "kf_attn_combine")
+    return (out, Mi, Li) if return_lse else out
+
+
+def launch_flash_attn(Q, K, V, O, B, S, H_q, H_kv, D, stream=0) -> int:
+    """Reference-compatible blocking launcher on raw device pointers (ints).
+
+    Same arguments as tests/test_flash_attn.cu:52-58; returns 0 on success or a
+    KF_* status (the reference returns cudaError_t; kf_attn_compat.h maps ours
+    onto it).  Prefill only: S_q = S_kv = S.
+    """
+    return int(lib().kf_launch_flash_attn(ctypes.c_void_p(Q), ctypes.c_void_p(K), ctypes.c_void_p(V),
+                                          ctypes.c_void_p(O), B, S, H_q, H_kv, D, ctypes.c_void_p(stream)))
+
+
+def device_error(clear: bool = True):
+    """(status, raw bits) of the device error word; synchronizes the device."""
+    raw = ctypes.c_uint(0)
+    rc = lib().kf_device_error(1 if clear else 0, ctypes.byref(raw))
+    return rc, raw.value
+
+
+def selftest_wait_timeout(timeout_ns: int = 20_000_000) -> int:
+    """Run the bounded-wait self-test kernel; returns KF_ERR_DEVICE_TIMEOUT when the wait expired as designed."""
+    return int(lib().kf_selftest_wait_timeout(timeout_ns, _stream_handle(torch.device("cuda"))))
+
+
+def set_wait_timeout_ns(ns: int) -> None:
+    lib().kf_set_wait_timeout_ns(int(ns))

@@ -1,0 +1,431 @@
+// decode_sm100.cuh -- short-query (decode) attention forward, split-KV.
+//
+// Replaces the reference's flash_attn_kernel<D> launched with q_len = 1
+// (tests/bench_flash_attn.cu:39-54, :153-159).  The reference gives each
+// (b, h_q) one CTA that uses 1 of its 64 query rows and streams the head's
+// whole KV serially, re-reading each KV head H_q/H_kv times.  Here:
+//   * rows: the G = H_q/H_kv query heads sharing one KV head (times the S_q
+//     query positions, S_q small) are packed as the M rows of the MMA, so
+//     every K/V byte is read from HBM once per (b, h_kv);
+//   * split-KV: the KV sequence of each (b, h_kv) is cut into n_split chunks,
+//     one CTA each, sized by the host to fill all SMs;
+//   * a producer warp streams K and V tiles (64 rows) into a shared-memory
+//     ring with TMA (3-D tensor maps, swizzled boxes, zero fill past S_kv);
+//     four consumer warps each take 16 rows of every tile: S = Q K^T and
+//     O += P V with mma.sync m16n8k16 (the contraction is tiny; the kernel is
+//     HBM-bound) and an online softmax in registers;
+//   * the CTA merges its warps' (m, l, O) in shared memory, writes one
+//     partial per split, and the last CTA of each (b, h_kv) to finish
+//     (atomic ticket) merges the splits by log-sum-exp and writes O (and
+//     Mi/Li) -- one launch, no second combine kernel.  The ticket counter is
+//     reset by that CTA, so the workspace stays zeroed between calls.
+// Softmax state uses the reference's convention (kernels/flash_attn.cu:
+// 261-294, 575-578): m = max of scaled scores, l = sum exp(s - m), O
+// un-normalised until the end.
+#pragma once
+
+#include <math_constants.h>
+
+#include "kf_ptx.cuh"
+
+namespace kf {
+
+template <int D, int MT>
+struct DecodeCfg {
+    static constexpr int TK = 64;                        // KV rows per stage
+    static constexpr int NW = 4;                         // consumer warps, 16 rows each
+    static constexpr int SWB = (D >= 64) ? 128 : 2 * D;
+    static constexpr int SWE = SWB / 2;
+    static constexpr int NSPAN = D / SWE;
+    static constexpr int TILE_BYTES = TK * D * 2;        // one K or V tile
+    static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
+    static constexpr int NSTAGE_RAW = 98304 / STAGE_BYTES;
+    static constexpr int NSTAGE = NSTAGE_RAW < 2 ? 2 : (NSTAGE_RAW > 8 ? 8 : NSTAGE_RAW);
+    static constexpr int QROWS = MT * 16;
+    static constexpr int QPITCH = D + 8;                 // halfs; +16 B breaks bank conflicts
+    static constexpr int Q_BYTES = (QROWS * QPITCH * 2 + 15) / 16 * 16;
+    static constexpr int MAX_SPLIT = 256;
+    static constexpr int RED_BYTES = NW * QROWS * (D + 2) * 4;
+    static constexpr int CMB_BYTES = (MAX_SPLIT + 2) * QROWS * 4;
+    static constexpr int STAGES_BYTES = NSTAGE * STAGE_BYTES;
+    static constexpr int BIG0 = STAGES_BYTES > RED_BYTES ? STAGES_BYTES : RED_BYTES;
+    static constexpr int BIG = BIG0 > CMB_BYTES ? BIG0 : CMB_BYTES;
+    static constexpr int SMEM_BYTES = 1024 + BIG + Q_BYTES + 256;
+    static constexpr int THREADS = 32 * (NW + 1);
+    static_assert(NW * 16 == TK, "each consumer warp owns 16 rows of a stage");
+    static_assert(SMEM_BYTES <= 232448, "shared memory over budget");
+};
+
+struct DecodeParams {
+    const uint16_t* Q;
+    float* O;
+    float* Mi;             // nullable
+    float* Li;             // nullable
+    float* part_O;         // [rows][n_split][D]   (n_split > 1)
+    float* part_ml;        // [rows][n_split][2]
+    unsigned* counters;    // [B*H_kv*n_rg], zero between calls
+    int H_q, H_kv, S_q, S_kv, G, R, n_rg, n_split, chunk;
+    float scale_log2, scale;
+    int unnormalized;
+    unsigned long long timeout_ns;
+};
+
+template <int D, int MT>
+__global__ void __launch_bounds__(DecodeCfg<D, MT>::THREADS)
+decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                  const DecodeParams p) {
+    using C = DecodeCfg<D, MT>;
+    constexpr int TK = C::TK, NW = C::NW, SWB = C::SWB, SWE = C::SWE, NSPAN = C::NSPAN;
+    constexpr int NSTAGE = C::NSTAGE, QROWS = C::QROWS, QPITCH = C::QPITCH;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sBig = smem;                       // stages, later reduction scratch
+    uint16_t* sQ = reinterpret_cast<uint16_t*>(smem + C::BIG);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BIG + C::Q_BYTES);
+    uint64_t* empty = full + NSTAGE;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + NSTAGE);
+    volatile int* is_last = abort_flag + 1;
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int split = blockIdx.x;
+    const int hk = blockIdx.y / p.n_rg;
+    const int rg = blockIdx.y % p.n_rg;
+    const int b = blockIdx.z;
+    const int r0 = rg * QROWS;
+    const int nrows = min(QROWS, p.R - r0);
+    // Global row index (over B*H_q*S_q) of this CTA's local row 0.
+    const size_t row_base = (static_cast<size_t>(b) * p.H_q + static_cast<size_t>(hk) * p.G) * p.S_q + r0;
+    const int kv_lo = split * p.chunk;
+    const int kv_hi = min(p.S_kv, kv_lo + p.chunk);
+    const int n_st = (kv_hi - kv_lo + TK - 1) / TK;
+    const float c = p.scale_log2;
+
+    if (tid == 0) {
+        for (int s = 0; s < NSTAGE; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], NW);
+        }
+        *abort_flag = 0;
+        *is_last = 0;
+        fence_mbar_init();
+    }
+    // Q rows of this (b, h_kv, row group) -> padded shared tile (rows >= nrows are zero).
+    for (int idx = tid; idx < QROWS * (D / 8); idx += C::THREADS) {
+        const int row = idx / (D / 8), ch = idx % (D / 8);
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (row < nrows) v = *reinterpret_cast<const uint4*>(p.Q + (row_base + row) * D + ch * 8);
+        *reinterpret_cast<uint4*>(sQ + row * QPITCH + ch * 8) = v;
+    }
+    __syncthreads();
+
+    float o[MT][D / 8][4];
+    float mrow[MT][2], lsum[MT][2];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+        mrow[mt][0] = mrow[mt][1] = -CUDART_INF_F;
+        lsum[mt][0] = lsum[mt][1] = 0.f;
+#pragma unroll
+        for (int n = 0; n < D / 8; ++n) o[mt][n][0] = o[mt][n][1] = o[mt][n][2] = o[mt][n][3] = 0.f;
+    }
+
+    if (warp == NW) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            tma_prefetch_desc(&tmK);
+            tma_prefetch_desc(&tmV);
+            const uint64_t pol = l2_policy_evict_first();   // KV is streamed once
+            const int bh = b * p.H_kv + hk;
+            int issued = 0;
+            for (int i = 0; i < n_st; ++i) {
+                const int slot = i % NSTAGE, round = i / NSTAGE;
+                if (round > 0 && !mbar_wait_bounded(&empty[slot], (round - 1) & 1, abort_flag, p.timeout_ns)) {
+                    atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_SOFTMAX);
+                    break;
+                }
+                mbar_arrive_expect_tx(&full[slot], C::STAGE_BYTES);
+                uint8_t* dK = sBig + slot * C::STAGE_BYTES;
+                uint8_t* dV = dK + C::TILE_BYTES;
+                const int row = kv_lo + i * TK;
+#pragma unroll
+                for (int s = 0; s < NSPAN; ++s) {
+                    tma_load_3d_hint(dK + s * TK * SWB, &tmK, &full[slot], s * SWE, row, bh, pol);
+                    tma_load_3d_hint(dV + s * TK * SWB, &tmV, &full[slot], s * SWE, row, bh, pol);
+                }
+                issued = i + 1;
+            }
+            if (*abort_flag) {
+                const int first = issued > NSTAGE ? issued - NSTAGE : 0;
+                int dummy = 0;
+                for (int i = first; i < issued; ++i)
+                    mbar_wait_bounded(&full[i % NSTAGE], (i / NSTAGE) & 1, &dummy, p.timeout_ns);
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ consumer warps
+        const int cq = lane & 3;
+        const int lm = lane >> 3, lr = lane & 7;
+        const uint32_t sQa = smem_u32(sQ);
+        for (int i = 0; i < n_st; ++i) {
+            const int slot = i % NSTAGE;
+            bool ok = mbar_wait_bounded(&full[slot], (i / NSTAGE) & 1, abort_flag, p.timeout_ns);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) { atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_TMA); break; }
+            const uint32_t sK = smem_u32(sBig + slot * C::STAGE_BYTES);
+            const uint32_t sV = sK + C::TILE_BYTES;
+
+            // S = Q K^T for this warp's 16 KV rows.
+            float s[MT][2][4];
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt) s[mt][nt][0] = s[mt][nt][1] = s[mt][nt][2] = s[mt][nt][3] = 0.f;
+#pragma unroll
+            for (int ks = 0; ks < D / 16; ++ks) {
+                uint32_t b00, b01, b10, b11;
+                const int krow = warp * 16 + lr + ((lm >> 1) << 3);
+                const int kcol = ks * 16 + ((lm & 1) << 3);
+                ldmatrix_x4(sK + swz_offset<SWB>(TK, krow, kcol), b00, b01, b10, b11);
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) {
+                    uint32_t a0, a1, a2, a3;
+                    const int qrow = mt * 16 + lr + ((lm & 1) << 3);
+                    const int qcol = ks * 16 + ((lm >> 1) << 3);
+                    ldmatrix_x4(sQa + (qrow * QPITCH + qcol) * 2, a0, a1, a2, a3);
+                    mma_16816(s[mt][0], a0, a1, a2, a3, b00, b01);
+                    mma_16816(s[mt][1], a0, a1, a2, a3, b10, b11);
+                }
+            }
+            // Mask keys past the end of this split (only the last stage can hold them).
+            if (i == n_st - 1) {
+                const int kv0 = kv_lo + i * TK + warp * 16 + 2 * cq;
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            if (kv0 + nt * 8 + (e & 1) >= kv_hi) s[mt][nt][e] = -CUDART_INF_F;
+            }
+            // Online softmax (raw-score units; c folds in 1/sqrt(D) and log2 e).
+            uint32_t pa[MT][4];
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    float mx = fmaxf(fmaxf(s[mt][0][2 * hh], s[mt][0][2 * hh + 1]),
+                                     fmaxf(s[mt][1][2 * hh], s[mt][1][2 * hh + 1]));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                    const float m_new = fmaxf(mrow[mt][hh], mx);
+                    const float m_use = (m_new == -CUDART_INF_F) ? 0.f : m_new;
+                    const float f = ex2_approx((mrow[mt][hh] - m_use) * c);
+                    mrow[mt][hh] = m_new;
+                    const float neg = -m_use * c;
+                    float ps = 0.f;
+#pragma unroll
+                    for (int nt = 0; nt < 2; ++nt) {
+                        s[mt][nt][2 * hh] = ex2_approx(fmaf(s[mt][nt][2 * hh], c, neg));
+                        s[mt][nt][2 * hh + 1] = ex2_approx(fmaf(s[mt][nt][2 * hh + 1], c, neg));
+                        ps += s[mt][nt][2 * hh] + s[mt][nt][2 * hh + 1];
+                    }
+                    lsum[mt][hh] = lsum[mt][hh] * f + ps;
+#pragma unroll
+                    for (int n = 0; n < D / 8; ++n) {
+                        o[mt][n][2 * hh] *= f;
+                        o[mt][n][2 * hh + 1] *= f;
+                    }
+                }
+                pa[mt][0] = pack_half2(s[mt][0][0], s[mt][0][1]);
+                pa[mt][1] = pack_half2(s[mt][0][2], s[mt][0][3]);
+                pa[mt][2] = pack_half2(s[mt][1][0], s[mt][1][1]);
+                pa[mt][3] = pack_half2(s[mt][1][2], s[mt][1][3]);
+            }
+            // O += P V
+#pragma unroll
+            for (int dp = 0; dp < D / 16; ++dp) {
+                uint32_t b0a, b1a, b0b, b1b;
+                const int vrow = warp * 16 + lr + ((lm & 1) << 3);
+                const int vcol = dp * 16 + ((lm >> 1) << 3);
+                ldmatrix_x4_trans(sV + swz_offset<SWB>(TK, vrow, vcol), b0a, b1a, b0b, b1b);
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) {
+                    mma_16816(o[mt][2 * dp], pa[mt][0], pa[mt][1], pa[mt][2], pa[mt][3], b0a, b1a);
+                    mma_16816(o[mt][2 * dp + 1], pa[mt][0], pa[mt][1], pa[mt][2], pa[mt][3], b0b, b1b);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+    }
+    __syncthreads();   // every stage consumed: the ring memory becomes reduction scratch
+    if (*abort_flag) return;
+
+    float* red_m = reinterpret_cast<float*>(sBig);            // [NW][QROWS]
+    float* red_l = red_m + NW * QROWS;                         // [NW][QROWS]
+    float* red_o = red_l + NW * QROWS;                         // [NW][QROWS][D]
+    if (warp < NW) {
+        const int g = lane >> 2, cq = lane & 3;
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                float l = lsum[mt][hh];
+                l += __shfl_xor_sync(0xffffffffu, l, 1);
+                l += __shfl_xor_sync(0xffffffffu, l, 2);
+                const int row = mt * 16 + g + 8 * hh;
+                if (cq == 0) {
+                    red_m[warp * QROWS + row] = mrow[mt][hh];
+                    red_l[warp * QROWS + row] = l;
+                }
+#pragma unroll
+                for (int n = 0; n < D / 8; ++n)
+                    *reinterpret_cast<float2*>(red_o + (warp * QROWS + row) * D + n * 8 + 2 * cq) =
+                        make_float2(o[mt][n][2 * hh], o[mt][n][2 * hh + 1]);
+            }
+    }
+    __syncthreads();
+    // Per-row weights of each warp, the merged max and sum.
+    float* wts = red_o + NW * QROWS * D;                       // [NW][QROWS]
+    float* Mrow = wts + NW * QROWS;                            // [QROWS]
+    float* Lrow = Mrow + QROWS;                                // [QROWS]
+    if (tid < QROWS) {
+        float M = -CUDART_INF_F;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, red_m[w * QROWS + tid]);
+        const float Mu = (M == -CUDART_INF_F) ? 0.f : M;
+        float L = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+            const float wt = ex2_approx((red_m[w * QROWS + tid] - Mu) * c);
+            wts[w * QROWS + tid] = wt;
+            L += wt * red_l[w * QROWS + tid];
+        }
+        Mrow[tid] = M;
+        Lrow[tid] = L;
+    }
+    __syncthreads();
+
+    if (p.n_split == 1) {
+        for (int idx = tid; idx < nrows * (D / 4); idx += C::THREADS) {
+            const int row = idx / (D / 4), d = (idx % (D / 4)) * 4;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int w = 0; w < NW; ++w) {
+                const float wt = wts[w * QROWS + row];
+                const float4 v = *reinterpret_cast<const float4*>(red_o + (w * QROWS + row) * D + d);
+                acc.x += wt * v.x; acc.y += wt * v.y; acc.z += wt * v.z; acc.w += wt * v.w;
+            }
+            const float sc = p.unnormalized ? 1.f : 1.f / Lrow[row];
+            acc.x *= sc; acc.y *= sc; acc.z *= sc; acc.w *= sc;
+            *reinterpret_cast<float4*>(p.O + (row_base + row) * D + d) = acc;
+        }
+        if (tid < nrows) {
+            if (p.Mi) p.Mi[row_base + tid] = Mrow[tid] * p.scale;
+            if (p.Li) p.Li[row_base + tid] = Lrow[tid];
+        }
+        return;
+    }
+
+    // ---- split partial: (m, l, O_u) relative to this split's max
+    const int ns = p.n_split;
+    for (int idx = tid; idx < nrows * (D / 4); idx += C::THREADS) {
+        const int row = idx / (D / 4), d = (idx % (D / 4)) * 4;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+            const float wt = wts[w * QROWS + row];
+            const float4 v = *reinterpret_cast<const float4*>(red_o + (w * QROWS + row) * D + d);
+            acc.x += wt * v.x; acc.y += wt * v.y; acc.z += wt * v.z; acc.w += wt * v.w;
+        }
+        *reinterpret_cast<float4*>(p.part_O + ((row_base + row) * ns + split) * D + d) = acc;
+    }
+    if (tid < nrows) {
+        *reinterpret_cast<float2*>(p.part_ml + ((row_base + tid) * ns + split) * 2) = make_float2(Mrow[tid], Lrow[tid]);
+    }
+    __threadfence();
+    __syncthreads();
+    const size_t cidx = (static_cast<size_t>(b) * p.H_kv + hk) * p.n_rg + rg;
+    if (tid == 0) {
+        const unsigned ticket = atomicAdd(&p.counters[cidx], 1u);
+        *is_last = (ticket == static_cast<unsigned>(ns - 1)) ? 1 : 0;
+    }
+    __syncthreads();
+    if (!*is_last) return;
+    __threadfence();
+
+    // ---- last CTA of this (b, h_kv, row group): merge all splits
+    float* swt = reinterpret_cast<float*>(sBig);               // [ns][QROWS]
+    float* sM = swt + ns * QROWS;
+    float* sL = sM + QROWS;
+    if (tid < nrows) {
+        const float* ml = p.part_ml + (row_base + tid) * ns * 2;
+        float M = -CUDART_INF_F;
+        for (int s2 = 0; s2 < ns; ++s2) M = fmaxf(M, __ldcg(ml + 2 * s2));
+        const float Mu = (M == -CUDART_INF_F) ? 0.f : M;
+        float L = 0.f;
+        for (int s2 = 0; s2 < ns; ++s2) {
+            const float wt = ex2_approx((__ldcg(ml + 2 * s2) - Mu) * c);
+            swt[s2 * QROWS + tid] = wt;
+            L += wt * __ldcg(ml + 2 * s2 + 1);
+        }
+        sM[tid] = M;
+        sL[tid] = L;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < nrows * (D / 4); idx += C::THREADS) {
+        const int row = idx / (D / 4), d = (idx % (D / 4)) * 4;
+        const float4* src = reinterpret_cast<const float4*>(p.part_O + (row_base + row) * ns * D + d);
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s2 = 0; s2 < ns; ++s2) {
+            const float wt = swt[s2 * QROWS + row];
+            const float4 v = __ldcg(src + s2 * (D / 4));
+            acc.x += wt * v.x; acc.y += wt * v.y; acc.z += wt * v.z; acc.w += wt * v.w;
+        }
+        const float sc = p.unnormalized ? 1.f : 1.f / sL[row];
+        acc.x *= sc; acc.y *= sc; acc.z *= sc; acc.w *= sc;
+        *reinterpret_cast<float4*>(p.O + (row_base + row) * D + d) = acc;
+    }
+    if (tid < nrows) {
+        if (p.Mi) p.Mi[row_base + tid] = sM[tid] * p.scale;
+        if (p.Li) p.Li[row_base + tid] = sL[tid];
+    }
+    if (tid == 0) p.counters[cidx] = 0u;
+}
+
+// Merge G partial results (m in natural-log units of the scaled scores, l,
+// un-normalised O) by log-sum-exp: M = max_g m_g,
+// O = sum_g e^{m_g - M} O_g / sum_g e^{m_g - M} l_g.  Parts are stacked
+// [G][rows] and [G][rows][D].  Used after the cross-GPU all-gather.
+__global__ void combine_partials_kernel(const float* __restrict__ O_parts, const float* __restrict__ m_parts,
+                                        const float* __restrict__ l_parts, int n_parts, long long rows, int D,
+                                        float* __restrict__ O, float* __restrict__ Mi, float* __restrict__ Li) {
+    const long long n4 = rows * (D / 4);
+    constexpr float LOG2E = 1.4426950408889634f;
+    for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < n4;
+         idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long row = idx / (D / 4);
+        const int d = static_cast<int>(idx % (D / 4)) * 4;
+        float M = -CUDART_INF_F;
+        for (int g = 0; g < n_parts; ++g) M = fmaxf(M, m_parts[g * rows + row]);
+        const float Mu = (M == -CUDART_INF_F) ? 0.f : M;
+        float L = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int g = 0; g < n_parts; ++g) {
+            const float wt = ex2_approx((m_parts[g * rows + row] - Mu) * LOG2E);
+            L += wt * l_parts[g * rows + row];
+            const float4 v = *reinterpret_cast<const float4*>(O_parts + (g * rows + row) * D + d);
+            acc.x += wt * v.x; acc.y += wt * v.y; acc.z += wt * v.z; acc.w += wt * v.w;
+        }
+        const float inv = 1.f / L;
+        acc.x *= inv; acc.y *= inv; acc.z *= inv; acc.w *= inv;
+        *reinterpret_cast<float4*>(O + row * D + d) = acc;
+        if (d == 0) {
+            if (Mi) Mi[row] = M;
+            if (Li) Li[row] = L;
+        }
+    }
+}
+
+}  // namespace kf

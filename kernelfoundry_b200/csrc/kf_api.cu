@@ -1,0 +1,483 @@
+// kf_api.cu -- the C ABI (include/kf_attn.h) over the sm_100a kernels.
+//
+// One translation unit: the kernels are included here so device code can
+// name the library's device error word directly.  Host side: argument
+// validation, the execution plan (tcgen05 prefill kernel vs. split-KV decode
+// kernel, split count from the SM count and occupancy), TMA tensor-map
+// encoding through the driver entry point (the library links the static
+// CUDA runtime only, so it loads on machines without a GPU driver), launches.
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/kf_attn.h"
+#include "decode_sm100.cuh"
+#include "kf_ptx.cuh"
+#include "prefill_sm100.cuh"
+
+namespace kf {
+
+// Waits on a barrier that nothing signals; the bounded wait must expire.
+__global__ void selftest_wait_kernel(unsigned long long timeout_ns) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (!mbar_wait_bounded(&bar, 0, &abort_flag, timeout_ns)) atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_SELFTEST);
+    }
+}
+
+}  // namespace kf
+
+namespace {
+
+constexpr unsigned long long kDefaultTimeoutNs = 1000000000ull;   // 1 s
+std::atomic<unsigned long long> g_timeout_ns{kDefaultTimeoutNs};
+thread_local int t_last_cuda_error = 0;
+
+constexpr int kMaxDevices = 64;
+constexpr int kCounterSlots = 16384;          // split-KV ticket counters at the workspace head
+constexpr size_t kCounterBytes = kCounterSlots * sizeof(unsigned);
+
+int cuda_fail(cudaError_t e) {
+    t_last_cuda_error = static_cast<int>(e);
+    return KF_ERR_CUDA;
+}
+
+struct DeviceInfo {
+    bool ready = false;
+    int sm_count = 0;
+    int cc_major = 0, cc_minor = 0;
+};
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+int device_info(DeviceInfo** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (dev < 0 || dev >= kMaxDevices) return KF_ERR_UNSUPPORTED_DEVICE;
+    DeviceInfo& di = g_dev[dev];
+    if (!di.ready) {
+        std::lock_guard<std::mutex> lk(g_dev_mu);
+        if (!di.ready) {
+            if ((e = cudaDeviceGetAttribute(&di.sm_count, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return cuda_fail(e);
+            if ((e = cudaDeviceGetAttribute(&di.cc_major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess) return cuda_fail(e);
+            if ((e = cudaDeviceGetAttribute(&di.cc_minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess) return cuda_fail(e);
+            di.ready = true;
+        }
+    }
+    if (di.cc_major != 10 || di.cc_minor != 0) return KF_ERR_UNSUPPORTED_DEVICE;
+    *out = &di;
+    return KF_OK;
+}
+
+// Sets the dynamic shared-memory opt-in of a kernel once per device and
+// returns how many of its CTAs fit on one SM.
+template <typename Kern>
+int kernel_setup(Kern kern, int smem_bytes, int threads, int* blocks_per_sm) {
+    struct Slot { std::atomic<int> bps{0}; };
+    static Slot slots[kMaxDevices];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e);
+    int v = slots[dev].bps.load(std::memory_order_acquire);
+    if (v == 0) {
+        if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes)) != cudaSuccess)
+            return cuda_fail(e);
+        int n = 0;
+        if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, threads, smem_bytes)) != cudaSuccess)
+            return cuda_fail(e);
+        v = n > 0 ? n : 1;
+        slots[dev].bps.store(v, std::memory_order_release);
+    }
+    *blocks_per_sm = v;
+    return KF_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 3-D map over a [BH][S][D] fp16 tensor; boxes of (swizzle span) x box_rows x 1.
+int make_map(CUtensorMap* map, const void* base, int D, int S, long long BH, int box_rows, int swb) {
+    auto enc = encode_fn();
+    if (!enc) return cuda_fail(cudaErrorNotSupported);
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(BH)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2, static_cast<cuuint64_t>(S) * D * 2};
+    cuuint32_t box[3] = {static_cast<cuuint32_t>(swb / 2), static_cast<cuuint32_t>(box_rows), 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    const CUtensorMapSwizzle sw = swb == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : swb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return cuda_fail(cudaErrorInvalidValue);
+    return KF_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int validate(const void* Q, const void* K, const void* V, const float* O, int B, int H_q, int H_kv, int S_q,
+             int S_kv, int D) {
+    if (B < 0 || S_q < 0 || H_q <= 0 || H_kv <= 0 || H_q % H_kv != 0) return KF_ERR_INVALID_ARG;
+    if (!(D == 16 || D == 64 || D == 128 || D == 256)) return KF_ERR_UNSUPPORTED_HEAD_DIM;
+    if (B == 0 || S_q == 0) return KF_OK;
+    if (S_kv <= 0) return KF_ERR_INVALID_ARG;
+    if (B > 65535 || H_q > 65535) return KF_ERR_INVALID_ARG;
+    if (static_cast<long long>(B) * H_q * S_q > (1ll << 40) || static_cast<long long>(B) * H_kv > (1ll << 31))
+        return KF_ERR_INVALID_ARG;
+    if (!Q || !K || !V || !O) return KF_ERR_INVALID_ARG;
+    if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O)) return KF_ERR_MISALIGNED;
+    return KF_OK;
+}
+
+// ------------------------------------------------------------------ planning
+struct Plan {
+    int path = 0;        // 0 prefill, 1 decode
+    int mt = 1;          // decode: 16-row MMA tiles per CTA
+    int n_rg = 1;        // decode: row groups per (b, h_kv)
+    int n_split = 1;     // decode: KV splits
+    int chunk = 0;       // decode: KV rows per split
+    size_t ws_bytes = 0; // workspace the plan uses
+    long long ctas = 0;
+};
+
+int decode_max_mt(int D) { return D <= 128 ? 2 : 1; }
+
+// Decode (packed-rows) path when G * S_q rows fit in two row groups.
+bool use_decode(int G, int S_q, int D) {
+    const long long R = static_cast<long long>(G) * S_q;
+    return R <= 2ll * 16 * decode_max_mt(D);
+}
+
+size_t split_ws_bytes(long long rows, int n_split, int D) {
+    const size_t part = static_cast<size_t>(rows) * n_split * (static_cast<size_t>(D) + 2) * sizeof(float);
+    return kCounterBytes + ((part + 255) / 256) * 256;
+}
+
+template <int D, int MT>
+int decode_blocks_per_sm(int* bps) {
+    using C = kf::DecodeCfg<D, MT>;
+    return kernel_setup(kf::decode_fwd_kernel<D, MT>, C::SMEM_BYTES, C::THREADS, bps);
+}
+
+int decode_bps(int D, int mt, int* bps) {
+    switch (D) {
+        case 16: return mt == 2 ? decode_blocks_per_sm<16, 2>(bps) : decode_blocks_per_sm<16, 1>(bps);
+        case 64: return mt == 2 ? decode_blocks_per_sm<64, 2>(bps) : decode_blocks_per_sm<64, 1>(bps);
+        case 128: return mt == 2 ? decode_blocks_per_sm<128, 2>(bps) : decode_blocks_per_sm<128, 1>(bps);
+        default: return decode_blocks_per_sm<256, 1>(bps);
+    }
+}
+
+int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_bytes, int sm_count,
+              int blocks_per_sm, Plan* pl) {
+    const int G = H_q / H_kv;
+    if (!use_decode(G, S_q, D)) {
+        pl->path = 0;
+        const int rows_per_cta = (D <= 128 ? 2 : 1) * 128;
+        pl->ctas = static_cast<long long>((S_q + rows_per_cta - 1) / rows_per_cta) * H_q * B;
+        return KF_OK;
+    }
+    pl->path = 1;
+    const int R = G * S_q;
+    const int maxmt = decode_max_mt(D);
+    pl->mt = R <= 16 ? 1 : maxmt;
+    const int qrows = 16 * pl->mt;
+    pl->n_rg = (R + qrows - 1) / qrows;
+    const long long units = static_cast<long long>(B) * H_kv * pl->n_rg;
+    const int TK = 64;
+    const int total_stages = (S_kv + TK - 1) / TK;
+    const double cap = static_cast<double>(sm_count) * blocks_per_sm;
+    const double ovh = 2.0;   // per-CTA fixed cost in stage-equivalents
+    int best_s = 1;
+    double best_cost = 1e300;
+    const int max_s = total_stages < kf::DecodeCfg<128, 1>::MAX_SPLIT ? total_stages : kf::DecodeCfg<128, 1>::MAX_SPLIT;
+    const long long rows = static_cast<long long>(B) * H_q * S_q;
+    for (int s = 1; s <= max_s; ++s) {
+        const int nst = (total_stages + s - 1) / s;
+        const int s_eff = (total_stages + nst - 1) / nst;
+        if (s_eff != s) continue;
+        if (s > 1 && (units > kCounterSlots || split_ws_bytes(rows, s, D) > ws_bytes)) break;
+        const double cost = units * s * (nst + ovh) / cap + (nst + ovh) + (s > 1 ? 1.0 : 0.0);
+        if (cost < best_cost) {
+            best_cost = cost;
+            best_s = s;
+        }
+    }
+    const int nst = (total_stages + best_s - 1) / best_s;
+    pl->n_split = best_s;
+    pl->chunk = nst * TK;
+    pl->ws_bytes = best_s > 1 ? split_ws_bytes(rows, best_s, D) : 0;
+    pl->ctas = units * best_s;
+    return KF_OK;
+}
+
+int plan_for_call(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_bytes, Plan* pl) {
+    DeviceInfo* di = nullptr;
+    int rc = device_info(&di);
+    if (rc != KF_OK) return rc;
+    const int G = H_q / H_kv;
+    int bps = 1;
+    if (use_decode(G, S_q, D)) {
+        const int R = G * S_q;
+        const int mt = R <= 16 ? 1 : decode_max_mt(D);
+        rc = decode_bps(D, mt, &bps);
+        if (rc != KF_OK) return rc;
+    }
+    return make_plan(B, H_q, H_kv, S_q, S_kv, D, ws_bytes, di->sm_count, bps, pl);
+}
+
+// ------------------------------------------------------------------ launches
+template <int D>
+int launch_prefill(const void* Q, const void* K, const void* V, float* O, float* Mi, float* Li, int unnorm, int B,
+                   int H_q, int H_kv, int S_q, int S_kv, cudaStream_t s) {
+    using C = kf::PrefillCfg<D>;
+    int bps = 0;
+    int rc = kernel_setup(kf::prefill_fwd_kernel<D>, C::SMEM_BYTES, C::THREADS, &bps);
+    if (rc != KF_OK) return rc;
+    CUtensorMap mq, mk, mv;
+    if ((rc = make_map(&mq, Q, D, S_q, static_cast<long long>(B) * H_q, C::BM, C::SWB)) != KF_OK) return rc;
+    if ((rc = make_map(&mk, K, D, S_kv, static_cast<long long>(B) * H_kv, C::BC, C::SWB)) != KF_OK) return rc;
+    if ((rc = make_map(&mv, V, D, S_kv, static_cast<long long>(B) * H_kv, C::BC, C::SWB)) != KF_OK) return rc;
+    kf::PrefillParams p;
+    p.O = O;
+    p.Mi = Mi;
+    p.Li = Li;
+    p.H_q = H_q;
+    p.H_kv = H_kv;
+    p.S_q = S_q;
+    p.S_kv = S_kv;
+    p.G = H_q / H_kv;
+    p.scale = 1.0f / std::sqrt(static_cast<float>(D));
+    p.scale_log2 = p.scale * 1.4426950408889634f;
+    p.unnormalized = unnorm;
+    p.timeout_ns = g_timeout_ns.load();
+    const int rows_per_cta = C::NQ * C::BM;
+    dim3 grid((S_q + rows_per_cta - 1) / rows_per_cta, H_q, B);
+    kf::prefill_fwd_kernel<D><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, p);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? KF_OK : cuda_fail(e);
+}
+
+template <int D, int MT>
+int launch_decode_t(const Plan& pl, const void* Q, const void* K, const void* V, float* O, float* Mi, float* Li,
+                    int unnorm, int B, int H_q, int H_kv, int S_q, int S_kv, void* ws, cudaStream_t s) {
+    using C = kf::DecodeCfg<D, MT>;
+    int bps = 0;
+    int rc = kernel_setup(kf::decode_fwd_kernel<D, MT>, C::SMEM_BYTES, C::THREADS, &bps);
+    if (rc != KF_OK) return rc;
+    CUtensorMap mk, mv;
+    if ((rc = make_map(&mk, K, D, S_kv, static_cast<long long>(B) * H_kv, C::TK, C::SWB)) != KF_OK) return rc;
+    if ((rc = make_map(&mv, V, D, S_kv, static_cast<long long>(B) * H_kv, C::TK, C::SWB)) != KF_OK) return rc;
+    kf::DecodeParams p;
+    p.Q = static_cast<const uint16_t*>(Q);
+    p.O = O;
+    p.Mi = Mi;
+    p.Li = Li;
+    p.counters = static_cast<unsigned*>(ws);
+    p.part_O = ws ? reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kCounterBytes) : nullptr;
+    const long long rows = static_cast<long long>(B) * H_q * S_q;
+    p.part_ml = p.part_O ? p.part_O + rows * pl.n_split * D : nullptr;
+    p.H_q = H_q;
+    p.H_kv = H_kv;
+    p.S_q = S_q;
+    p.S_kv = S_kv;
+    p.G = H_q / H_kv;
+    p.R = p.G * S_q;
+    p.n_rg = pl.n_rg;
+    p.n_split = pl.n_split;
+    p.chunk = pl.chunk;
+    p.scale = 1.0f / std::sqrt(static_cast<float>(D));
+    p.scale_log2 = p.scale * 1.4426950408889634f;
+    p.unnormalized = unnorm;
+    p.timeout_ns = g_timeout_ns.load();
+    dim3 grid(pl.n_split, H_kv * pl.n_rg, B);
+    kf::decode_fwd_kernel<D, MT><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? KF_OK : cuda_fail(e);
+}
+
+int launch_decode(const Plan& pl, int D, const void* Q, const void* K, const void* V, float* O, float* Mi,
+                  float* Li, int unnorm, int B, int H_q, int H_kv, int S_q, int S_kv, void* ws, cudaStream_t s) {
+#define KF_DEC(DV, MTV) \
+    return launch_decode_t<DV, MTV>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s)
+    switch (D) {
+        case 16: if (pl.mt == 2) KF_DEC(16, 2); KF_DEC(16, 1);
+        case 64: if (pl.mt == 2) KF_DEC(64, 2); KF_DEC(64, 1);
+        case 128: if (pl.mt == 2) KF_DEC(128, 2); KF_DEC(128, 1);
+        default: KF_DEC(256, 1);
+    }
+#undef KF_DEC
+}
+
+int attn_core(const void* Q, const void* K, const void* V, float* O, float* Mi, float* Li, int unnorm, int B,
+              int H_q, int H_kv, int S_q, int S_kv, int D, void* ws, size_t ws_bytes, void* stream) {
+    int rc = validate(Q, K, V, O, B, H_q, H_kv, S_q, S_kv, D);
+    if (rc != KF_OK) return rc;
+    if (B == 0 || S_q == 0) return KF_OK;
+    if (!ws) ws_bytes = 0;
+    if (ws && !aligned16(ws)) return KF_ERR_MISALIGNED;
+    Plan pl;
+    if ((rc = plan_for_call(B, H_q, H_kv, S_q, S_kv, D, ws_bytes, &pl)) != KF_OK) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (pl.path == 0) {
+        switch (D) {
+            case 16: return launch_prefill<16>(Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, s);
+            case 64: return launch_prefill<64>(Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, s);
+            case 128: return launch_prefill<128>(Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, s);
+            default: return launch_prefill<256>(Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, s);
+        }
+    }
+    return launch_decode(pl, D, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, pl.n_split > 1 ? ws : nullptr, s);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* kf_strerror(int code) {
+    switch (code) {
+        case KF_OK: return "ok";
+        case KF_ERR_INVALID_ARG: return "invalid argument (shape, null pointer or H_q % H_kv != 0)";
+        case KF_ERR_UNSUPPORTED_HEAD_DIM: return "unsupported head dimension (D must be 16, 64, 128 or 256)";
+        case KF_ERR_MISALIGNED: return "pointer not 16-byte aligned";
+        case KF_ERR_CUDA: return "CUDA runtime error (see kf_last_cuda_error)";
+        case KF_ERR_DEVICE_TIMEOUT: return "a bounded in-kernel wait expired";
+        case KF_ERR_UNSUPPORTED_DEVICE: return "current device is not an sm_100 (B200) GPU";
+        case KF_ERR_WORKSPACE: return "workspace too small";
+        default: return "unknown status";
+    }
+}
+
+int kf_last_cuda_error(void) { return t_last_cuda_error; }
+
+const char* kf_version(void) { return "kernelfoundry-b200 0.1.0 (sm_100a)"; }
+
+int kf_attn_fwd(const void* Q, const void* K, const void* V, float* O, int B, int H_q, int H_kv, int S_q, int S_kv,
+                int D, void* workspace, size_t workspace_bytes, void* stream) {
+    return attn_core(Q, K, V, O, nullptr, nullptr, 0, B, H_q, H_kv, S_q, S_kv, D, workspace, workspace_bytes, stream);
+}
+
+int kf_attn_fwd_lse(const void* Q, const void* K, const void* V, float* O, float* Mi, float* Li, int B, int H_q,
+                    int H_kv, int S_q, int S_kv, int D, void* workspace, size_t workspace_bytes, void* stream) {
+    return attn_core(Q, K, V, O, Mi, Li, 0, B, H_q, H_kv, S_q, S_kv, D, workspace, workspace_bytes, stream);
+}
+
+int kf_attn_fwd_partial(const void* Q, const void* K, const void* V, float* O_u, float* m, float* l, int B, int H_q,
+                        int H_kv, int S_q, int S_kv, int D, void* workspace, size_t workspace_bytes, void* stream) {
+    if (B > 0 && S_q > 0 && (!m || !l)) return KF_ERR_INVALID_ARG;
+    return attn_core(Q, K, V, O_u, m, l, 1, B, H_q, H_kv, S_q, S_kv, D, workspace, workspace_bytes, stream);
+}
+
+int kf_attn_combine(const float* O_parts, const float* m_parts, const float* l_parts, int n_parts, float* O,
+                    float* Mi, float* Li, int B, int H_q, int S_q, int D, void* stream) {
+    if (n_parts <= 0 || B < 0 || H_q <= 0 || S_q < 0) return KF_ERR_INVALID_ARG;
+    if (!(D == 16 || D == 64 || D == 128 || D == 256)) return KF_ERR_UNSUPPORTED_HEAD_DIM;
+    const long long rows = static_cast<long long>(B) * H_q * S_q;
+    if (rows == 0) return KF_OK;
+    if (!O_parts || !m_parts || !l_parts || !O) return KF_ERR_INVALID_ARG;
+    if (!aligned16(O_parts) || !aligned16(O)) return KF_ERR_MISALIGNED;
+    DeviceInfo* di = nullptr;
+    int rc = device_info(&di);
+    if (rc != KF_OK) return rc;
+    const long long n4 = rows * (D / 4);
+    const int threads = 256;
+    long long blocks = (n4 + threads - 1) / threads;
+    const long long maxb = static_cast<long long>(di->sm_count) * 8;
+    if (blocks > maxb) blocks = maxb;
+    kf::combine_partials_kernel<<<static_cast<unsigned>(blocks), threads, 0, static_cast<cudaStream_t>(stream)>>>(
+        O_parts, m_parts, l_parts, n_parts, rows, D, O, Mi, Li);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? KF_OK : cuda_fail(e);
+}
+
+size_t kf_attn_workspace_bytes(int B, int H_q, int H_kv, int S_q, int S_kv, int D) {
+    if (validate(reinterpret_cast<const void*>(16), reinterpret_cast<const void*>(16),
+                 reinterpret_cast<const void*>(16), reinterpret_cast<const float*>(16), B, H_q, H_kv, S_q, S_kv,
+                 D) != KF_OK || B == 0 || S_q == 0)
+        return 0;
+    Plan pl;
+    if (plan_for_call(B, H_q, H_kv, S_q, S_kv, D, static_cast<size_t>(-1), &pl) != KF_OK) return 0;
+    return pl.ws_bytes;
+}
+
+int kf_attn_workspace_init(void* workspace, size_t workspace_bytes, void* stream) {
+    if (!workspace || workspace_bytes == 0) return KF_OK;
+    cudaError_t e = cudaMemsetAsync(workspace, 0, workspace_bytes, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? KF_OK : cuda_fail(e);
+}
+
+int kf_attn_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t workspace_bytes, int* path, int* n_split,
+                 int* grid_ctas) {
+    int rc = validate(reinterpret_cast<const void*>(16), reinterpret_cast<const void*>(16),
+                      reinterpret_cast<const void*>(16), reinterpret_cast<const float*>(16), B, H_q, H_kv, S_q, S_kv,
+                      D);
+    if (rc != KF_OK) return rc;
+    Plan pl;
+    if (B > 0 && S_q > 0 && (rc = plan_for_call(B, H_q, H_kv, S_q, S_kv, D, workspace_bytes, &pl)) != KF_OK) return rc;
+    if (path) *path = pl.path;
+    if (n_split) *n_split = pl.n_split;
+    if (grid_ctas) *grid_ctas = static_cast<int>(pl.ctas);
+    return KF_OK;
+}
+
+int kf_launch_flash_attn(const uint16_t* Q, const uint16_t* K, const uint16_t* V, float* O, int B, int S, int H_q,
+                         int H_kv, int D, void* stream) {
+    int rc = attn_core(Q, K, V, O, nullptr, nullptr, 0, B, H_q, H_kv, S, S, D, nullptr, 0, stream);
+    if (rc != KF_OK) return rc;
+    cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e);
+    unsigned raw = 0;
+    e = cudaMemcpyFromSymbol(&raw, kf::g_kf_dev_error, sizeof(raw));
+    if (e != cudaSuccess) return cuda_fail(e);
+    return raw ? KF_ERR_DEVICE_TIMEOUT : KF_OK;
+}
+
+int kf_device_error(int clear, unsigned* raw) {
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e);
+    unsigned v = 0;
+    if ((e = cudaMemcpyFromSymbol(&v, kf::g_kf_dev_error, sizeof(v))) != cudaSuccess) return cuda_fail(e);
+    if (raw) *raw = v;
+    if (clear && v) {
+        const unsigned zero = 0;
+        if ((e = cudaMemcpyToSymbol(kf::g_kf_dev_error, &zero, sizeof(zero))) != cudaSuccess) return cuda_fail(e);
+    }
+    return v ? KF_ERR_DEVICE_TIMEOUT : KF_OK;
+}
+
+void kf_set_wait_timeout_ns(unsigned long long ns) { g_timeout_ns.store(ns ? ns : kDefaultTimeoutNs); }
+
+int kf_selftest_wait_timeout(unsigned long long timeout_ns, void* stream) {
+    DeviceInfo* di = nullptr;
+    int rc = device_info(&di);
+    if (rc != KF_OK) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    kf::selftest_wait_kernel<<<1, 32, 0, s>>>(timeout_ns);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e);
+    if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return cuda_fail(e);
+    return kf_device_error(1, nullptr);
+}
+
+}  // extern "C"

@@ -1,0 +1,379 @@
+// prefill_sm100.cuh -- non-causal attention forward on tcgen05 tensor cores.
+//
+// Replaces the reference's flash_attn_kernel<D> (kernels/flash_attn.cu:384-585)
+// for query blocks of many rows (prefill).  Same math and layout contract:
+// Q [B,H_q,S_q,D] fp16, K/V [B,H_kv,S_kv,D] fp16, O [B,H_q,S_q,D] fp32,
+// optional Mi/Li [B,H_q,S_q] fp32 (row max of the scaled scores, sum of
+// exp(score - Mi): kernels/flash_attn.cu:575-578), softmax scale 1/sqrt(D),
+// GQA head map h_kv = h_q / (H_q/H_kv) (kernels/flash_attn.cu:406).
+//
+// One CTA owns NQ query tiles of 128 rows of one (b, h_q) and streams all of
+// that head's K/V through a ring of shared-memory slots:
+//   warp 0      TMA producer: Q tiles once, then K_0, V_0, K_1, V_1, ... into
+//               the ring (3-D tensor maps, 128-B (or 32-B) swizzle, zero fill
+//               past S_q / S_kv).
+//   warp 1      TMEM owner + single-thread MMA issuer:
+//                 S_t  = Q_t K_j^T        (tcgen05.mma, M=128, N=BC, fp32 in TMEM)
+//                 O_t += P_t V_j          (tcgen05.mma, M=128, N=D,  fp32 in TMEM)
+//               in the order PV_A(j-1), QK_A(j), PV_B(j-1), QK_B(j), so the tensor
+//               core works on one tile while the other tile's softmax runs.
+//   warps 4..   one softmax warpgroup per Q tile, one thread per query row:
+//               tcgen05.ld of the S row, row max in registers, exp2 with the
+//               scale folded in, P (fp16) written to swizzled shared memory,
+//               lazy rescale of the O row in TMEM only when the running max
+//               grows by more than 2^8; epilogue O /= l straight from TMEM.
+// All waits are bounded (kf_ptx.cuh); a timeout raises a device error word
+// and every role unwinds, drains its in-flight copies/MMAs, frees TMEM.
+#pragma once
+
+#include <math_constants.h>
+
+#include "kf_ptx.cuh"
+
+namespace kf {
+
+template <int D>
+struct PrefillCfg {
+    static constexpr int BM = 128;                     // query rows per tile (UMMA M)
+    static constexpr int NQ = (D <= 128) ? 2 : 1;      // query tiles per CTA
+    static constexpr int BC = (D <= 128) ? 128 : 64;   // KV rows per tile (UMMA N of QK^T)
+    static constexpr int SWB = (D >= 64) ? 128 : 2 * D;  // swizzle span in bytes
+    static constexpr int SWE = SWB / 2;                // fp16 elements per span
+    static constexpr int NSPAN = D / SWE;              // spans (TMA boxes) per row
+    static constexpr int Q_BYTES = BM * D * 2;
+    static constexpr int KV_BYTES = BC * D * 2;
+    static constexpr int P_BYTES = BM * BC * 2;
+    static constexpr int SMEM_LIMIT = 232448;          // 227 KB opt-in per CTA
+    static constexpr int BAR_BYTES = 1024;
+    static constexpr int FIXED = NQ * (Q_BYTES + P_BYTES);
+    static constexpr int NSLOT_RAW = (SMEM_LIMIT - 1024 - BAR_BYTES - FIXED) / KV_BYTES;
+    static constexpr int NSLOT = NSLOT_RAW > 8 ? 8 : NSLOT_RAW;
+    static constexpr int SMEM_BYTES = 1024 + FIXED + NSLOT * KV_BYTES + BAR_BYTES;
+    static constexpr int TMEM_USED = NQ * (BC + D);
+    static constexpr int TMEM_COLS = TMEM_USED <= 32 ? 32 : TMEM_USED <= 64 ? 64 : TMEM_USED <= 128 ? 128
+                                   : TMEM_USED <= 256 ? 256 : 512;
+    static constexpr int THREADS = 128 * (1 + NQ);
+    static_assert(NSLOT >= 2, "K/V ring needs at least two slots");
+    static_assert(SMEM_BYTES <= SMEM_LIMIT, "shared memory over budget");
+    static_assert(TMEM_USED <= 512, "TMEM over budget");
+};
+
+struct PrefillParams {
+    float* O;
+    float* Mi;   // nullable
+    float* Li;   // nullable
+    int H_q, H_kv, S_q, S_kv, G;
+    float scale_log2;   // (1/sqrt(D)) * log2(e)
+    float scale;        // 1/sqrt(D)
+    int unnormalized;   // 1: write O_u = sum exp(s - Mi) v (partial form), Mi/Li required
+    unsigned long long timeout_ns;
+};
+
+template <int N>
+__device__ __forceinline__ void tmem_ld_chunk(uint32_t taddr, uint32_t (&r)[N]) {
+    if constexpr (N == 32) tmem_ld32(taddr, r); else tmem_ld16(taddr, r);
+}
+template <int N>
+__device__ __forceinline__ void tmem_st_chunk(uint32_t taddr, const uint32_t (&r)[N]) {
+    if constexpr (N == 32) tmem_st32(taddr, r); else tmem_st16(taddr, r);
+}
+
+// Bounded wait that ignores the abort flag (used while draining).
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, uint64_t timeout_ns) {
+    int dummy = 0;
+    return mbar_wait_bounded(bar, parity, &dummy, timeout_ns);
+}
+
+template <int D>
+__global__ void __launch_bounds__(PrefillCfg<D>::THREADS, 1)
+prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const PrefillParams p) {
+    using C = PrefillCfg<D>;
+    constexpr int BM = C::BM, BC = C::BC, NQ = C::NQ, SWB = C::SWB, SWE = C::SWE, NSPAN = C::NSPAN;
+    constexpr int NSLOT = C::NSLOT;
+    constexpr int OCH = D < 32 ? D : 32;   // TMEM columns per O chunk
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sQ = smem;
+    uint8_t* sP = sQ + NQ * C::Q_BYTES;
+    uint8_t* sKV = sP + NQ * C::P_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + NSLOT * C::KV_BYTES);
+    uint64_t* q_full = bars;
+    uint64_t* s_full = q_full + NQ;
+    uint64_t* p_full = s_full + NQ;
+    uint64_t* o_full = p_full + NQ;
+    uint64_t* kv_full = o_full + NQ;
+    uint64_t* kv_empty = kv_full + NSLOT;
+    uint64_t* mma_done = kv_empty + NSLOT;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int h = blockIdx.y;
+    const int b = blockIdx.z;
+    const int h_kv = h / p.G;
+    const int q_row0 = blockIdx.x * NQ * BM;
+    const int rows_left = p.S_q - q_row0;
+    const int nq_active = rows_left >= NQ * BM ? NQ : (rows_left + BM - 1) / BM;
+    const int n_kv = (p.S_kv + BC - 1) / BC;
+
+    if (threadIdx.x == 0) {
+        for (int t = 0; t < NQ; ++t) {
+            mbar_init(&q_full[t], 1);
+            mbar_init(&s_full[t], 1);
+            mbar_init(&p_full[t], 128);
+            mbar_init(&o_full[t], 1);
+        }
+        for (int s = 0; s < NSLOT; ++s) {
+            mbar_init(&kv_full[s], 1);
+            mbar_init(&kv_empty[s], 1);
+        }
+        mbar_init(mma_done, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            tma_prefetch_desc(&tmQ);
+            tma_prefetch_desc(&tmK);
+            tma_prefetch_desc(&tmV);
+            const int bh_q = b * p.H_q + h;
+            const int bh_kv = b * p.H_kv + h_kv;
+            for (int t = 0; t < nq_active; ++t) {
+                mbar_arrive_expect_tx(&q_full[t], C::Q_BYTES);
+                for (int s = 0; s < NSPAN; ++s)
+                    tma_load_3d(sQ + t * C::Q_BYTES + s * BM * SWB, &tmQ, &q_full[t], s * SWE, q_row0 + t * BM, bh_q);
+            }
+            const int n_loads = 2 * n_kv;
+            int issued = 0;
+            for (int i = 0; i < n_loads; ++i) {
+                const int slot = i % NSLOT;
+                const int round = i / NSLOT;
+                if (round > 0 && !mbar_wait_bounded(&kv_empty[slot], (round - 1) & 1, abort_flag, p.timeout_ns)) {
+                    atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_MMA);
+                    break;
+                }
+                mbar_arrive_expect_tx(&kv_full[slot], C::KV_BYTES);
+                const CUtensorMap* map = (i & 1) ? &tmV : &tmK;
+                uint8_t* dst = sKV + slot * C::KV_BYTES;
+                for (int s = 0; s < NSPAN; ++s)
+                    tma_load_3d(dst + s * BC * SWB, map, &kv_full[slot], s * SWE, (i >> 1) * BC, bh_kv);
+                issued = i + 1;
+            }
+            if (*abort_flag) {
+                // Drain: every copy this thread issued must land before the CTA exits.
+                for (int t = 0; t < nq_active; ++t) mbar_wait_drain(&q_full[t], 0, p.timeout_ns);
+                const int first = issued > NSLOT ? issued - NSLOT : 0;
+                for (int i = first; i < issued; ++i)
+                    mbar_wait_drain(&kv_full[i % NSLOT], (i / NSLOT) & 1, p.timeout_ns);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc_qk = umma_idesc_f16_f32(BM, BC, false, false);
+            constexpr uint32_t idesc_pv = umma_idesc_f16_f32(BM, D, false, true);
+            constexpr uint32_t lay_qk = umma_layout_code(SWB);
+            constexpr uint32_t lay_p = umma_layout_code(128);
+            const uint32_t sQa = smem_u32(sQ), sPa = smem_u32(sP), sKVa = smem_u32(sKV);
+            bool ok = true;
+            for (int t = 0; t < nq_active && ok; ++t) ok = mbar_wait_bounded(&q_full[t], 0, abort_flag, p.timeout_ns);
+            if (!ok) atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_TMA);
+            for (int j = 0; j <= n_kv && ok; ++j) {
+                const int iK = 2 * j, iV = 2 * (j - 1) + 1;
+                const int slotK = iK % NSLOT, slotV = (iV + NSLOT) % NSLOT;
+                if (j < n_kv && !mbar_wait_bounded(&kv_full[slotK], (iK / NSLOT) & 1, abort_flag, p.timeout_ns)) {
+                    atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_TMA); ok = false; break;
+                }
+                if (j > 0 && !mbar_wait_bounded(&kv_full[slotV], (iV / NSLOT) & 1, abort_flag, p.timeout_ns)) {
+                    atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_TMA); ok = false; break;
+                }
+                tc_fence_after();
+                for (int t = 0; t < nq_active; ++t) {
+                    const uint32_t tS = tmem + t * BC;
+                    const uint32_t tO = tmem + NQ * BC + t * D;
+                    if (j > 0) {
+                        if (!mbar_wait_bounded(&p_full[t], (j - 1) & 1, abort_flag, p.timeout_ns)) {
+                            atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_SOFTMAX); ok = false; break;
+                        }
+                        tc_fence_after();
+                        const uint32_t pbase = sPa + t * C::P_BYTES;
+                        const uint32_t vbase = sKVa + slotV * C::KV_BYTES;
+#pragma unroll
+                        for (int kk = 0; kk < BC / 16; ++kk) {
+                            // P: K-major, 64-element spans of BM rows; V: MN-major spans of SWE columns.
+                            const uint32_t pa = pbase + (kk * 16 / 64) * (BM * 128) + ((kk * 16) % 64) * 2;
+                            const uint64_t adesc = umma_desc(pa, 16, 8 * 128, lay_p);
+                            const uint64_t bdesc = umma_desc(vbase + kk * 16 * SWB, BC * SWB, 8 * SWB, lay_qk);
+                            umma_ss(tO, adesc, bdesc, idesc_pv, (j > 1 || kk > 0) ? 1u : 0u);
+                        }
+                        if (j == n_kv) umma_commit(&o_full[t]);
+                    }
+                    if (j < n_kv) {
+                        const uint32_t qbase = sQa + t * C::Q_BYTES;
+                        const uint32_t kbase = sKVa + slotK * C::KV_BYTES;
+#pragma unroll
+                        for (int kk = 0; kk < D / 16; ++kk) {
+                            const int span = (kk * 16) / SWE;
+                            const int off = ((kk * 16) % SWE) * 2;
+                            const uint64_t adesc = umma_desc(qbase + span * BM * SWB + off, 16, 8 * SWB, lay_qk);
+                            const uint64_t bdesc = umma_desc(kbase + span * BC * SWB + off, 16, 8 * SWB, lay_qk);
+                            umma_ss(tS, adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
+                        }
+                        umma_commit(&s_full[t]);
+                    }
+                }
+                if (!ok) break;
+                if (j > 0) umma_commit(&kv_empty[slotV]);
+                if (j < n_kv) umma_commit(&kv_empty[slotK]);
+            }
+            // Every MMA issued above must complete before TMEM is released.
+            umma_commit(mma_done);
+            mbar_wait_drain(mma_done, 0, p.timeout_ns);
+        }
+    } else if (warp >= 4) {
+        // ------------------------------------------------------------ softmax warpgroups
+        const int t = (warp - 4) >> 2;
+        const int wq = warp & 3;                 // TMEM sub-partition of this warp
+        const int row = wq * 32 + lane;          // query row within the tile
+        if (t < nq_active) {
+            const uint32_t tl = tmem + (static_cast<uint32_t>(wq * 32) << 16);
+            const uint32_t tS = tl + t * BC;
+            const uint32_t tO = tl + NQ * BC + t * D;
+            uint8_t* sPt = sP + t * C::P_BYTES;
+            const float c = p.scale_log2;
+            float m_ref = -CUDART_INF_F, m_true = -CUDART_INF_F, l = 0.f;
+            bool ok = true;
+            for (int j = 0; j < n_kv; ++j) {
+                ok = mbar_wait_bounded(&s_full[t], j & 1, abort_flag, p.timeout_ns);
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) { atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_MMA); break; }
+                tc_fence_after();
+                uint32_t sr[BC];
+#pragma unroll
+                for (int cc = 0; cc < BC / 32; ++cc)
+                    tmem_ld32(tS + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[cc * 32]));
+                tmem_wait_ld();
+                const int kv_valid = p.S_kv - j * BC;
+                if (kv_valid < BC) {
+#pragma unroll
+                    for (int cc = 0; cc < BC; ++cc)
+                        if (cc >= kv_valid) sr[cc] = __float_as_uint(-CUDART_INF_F);
+                }
+                float mx0 = __uint_as_float(sr[0]), mx1 = __uint_as_float(sr[1]);
+                float mx2 = __uint_as_float(sr[2]), mx3 = __uint_as_float(sr[3]);
+#pragma unroll
+                for (int cc = 4; cc < BC; cc += 4) {
+                    mx0 = fmaxf(mx0, __uint_as_float(sr[cc]));
+                    mx1 = fmaxf(mx1, __uint_as_float(sr[cc + 1]));
+                    mx2 = fmaxf(mx2, __uint_as_float(sr[cc + 2]));
+                    mx3 = fmaxf(mx3, __uint_as_float(sr[cc + 3]));
+                }
+                const float m_new = fmaxf(m_true, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)));
+                m_true = m_new;
+                // Lazy rescale: keep the reference max unless the row max grew by
+                // more than 2^8 (P <= 256 stays exact enough in fp16, l and O in fp32).
+                bool rescale = false;
+                float f = 1.0f;
+                if (j == 0) {
+                    m_ref = m_new;
+                } else {
+                    const bool need = (m_new - m_ref) * c > 8.0f;
+                    rescale = __any_sync(0xffffffffu, need);
+                    if (need) {
+                        f = ex2_approx((m_ref - m_new) * c);
+                        m_ref = m_new;
+                        l *= f;
+                    }
+                }
+                const float neg = -m_ref * c;
+                float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+                for (int ch = 0; ch < BC / 8; ++ch) {
+                    float e[8];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) e[k] = ex2_approx(fmaf(__uint_as_float(sr[ch * 8 + k]), c, neg));
+                    s0 += (e[0] + e[1]) + (e[2] + e[3]);
+                    s1 += (e[4] + e[5]) + (e[6] + e[7]);
+                    uint4 v;
+                    v.x = pack_half2(e[0], e[1]);
+                    v.y = pack_half2(e[2], e[3]);
+                    v.z = pack_half2(e[4], e[5]);
+                    v.w = pack_half2(e[6], e[7]);
+                    const int span = ch >> 3, chunk = ch & 7;
+                    *reinterpret_cast<uint4*>(sPt + span * (BM * 128) + row * 128 + ((chunk ^ (row & 7)) << 4)) = v;
+                }
+                l += s0 + s1;
+                if (rescale) {
+                    // O_t is stable here: PV_t(j-1) completed before S_t(j) was committed.
+#pragma unroll
+                    for (int dc = 0; dc < D / OCH; ++dc) {
+                        uint32_t o[OCH];
+                        tmem_ld_chunk<OCH>(tO + dc * OCH, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int k = 0; k < OCH; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * f);
+                        tmem_st_chunk<OCH>(tO + dc * OCH, o);
+                    }
+                    tmem_wait_st();
+                }
+                fence_proxy_async_smem();
+                tc_fence_before();
+                mbar_arrive(&p_full[t]);
+            }
+            if (ok) {
+                ok = mbar_wait_bounded(&o_full[t], 0, abort_flag, p.timeout_ns);
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_MMA);
+            }
+            if (ok) {
+                tc_fence_after();
+                const float f = ex2_approx((m_ref - m_true) * c);   // rebase to the true max
+                const float l_true = l * f;
+                const float osc = p.unnormalized ? f : 1.0f / l;
+                const int qrow = q_row0 + t * BM + row;
+                const bool store = qrow < p.S_q;
+                float* orow = p.O + ((static_cast<size_t>(b) * p.H_q + h) * p.S_q + (store ? qrow : 0)) * D;
+#pragma unroll
+                for (int dc = 0; dc < D / OCH; ++dc) {
+                    uint32_t o[OCH];
+                    tmem_ld_chunk<OCH>(tO + dc * OCH, o);
+                    tmem_wait_ld();
+                    if (store) {
+#pragma unroll
+                        for (int k = 0; k < OCH; k += 4) {
+                            float4 v = make_float4(__uint_as_float(o[k]) * osc, __uint_as_float(o[k + 1]) * osc,
+                                                   __uint_as_float(o[k + 2]) * osc, __uint_as_float(o[k + 3]) * osc);
+                            *reinterpret_cast<float4*>(orow + dc * OCH + k) = v;
+                        }
+                    }
+                }
+                if (store) {
+                    const size_t mi = (static_cast<size_t>(b) * p.H_q + h) * p.S_q + qrow;
+                    if (p.Mi) p.Mi[mi] = m_true * p.scale;
+                    if (p.Li) p.Li[mi] = l_true;
+                }
+            }
+            tc_fence_before();
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+}  // namespace kf

@@ -1,0 +1,119 @@
+"""The C-ABI library loads, exports what include/kf_attn.h declares, and
+validates arguments before touching a GPU (no compute calls here)."""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from conftest import REPO
+
+HEADER = os.path.join(REPO, "include", "kf_attn.h")
+
+
+def _declared():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(kf_[a-z_0-9]+)\s*\(", text)))
+
+
+def test_header_symbols_exported(kf_lib):
+    from kernelfoundry_b200 import _lib
+    from kernelfoundry_b200.build import LIB_PATH
+
+    declared = _declared()
+    assert len(declared) >= 14
+    assert sorted(declared) == sorted(_lib.EXPORTED)
+    out = subprocess.run(["nm", "-D", "--defined-only", LIB_PATH], capture_output=True, text=True, check=True).stdout
+    exported = set(re.findall(r"\bT (kf_\w+)", out))
+    missing = [s for s in declared if s not in exported]
+    assert not missing, missing
+    for s in declared:
+        assert hasattr(kf_lib, s)
+
+
+def test_library_is_product_only(kf_lib):
+    """The product library contains no oracle / reference code."""
+    from kernelfoundry_b200.build import LIB_PATH
+
+    out = subprocess.run(["nm", "-D", LIB_PATH], capture_output=True, text=True, check=True).stdout
+    assert "kfo_" not in out and "kfref" not in out
+    pkg = os.path.join(REPO, "kernelfoundry_b200")
+    for root, _, files in os.walk(pkg):
+        for f in files:
+            if f.endswith((".py", ".cu", ".cuh", ".h")):
+                src = open(os.path.join(root, f)).read()
+                assert "import oracle" not in src and "from oracle" not in src, f
+
+
+def test_no_gpu_dependency_at_load():
+    """libkf_attn.so needs no libcuda / libcudart at load time (static runtime, driver via entry point)."""
+    from kernelfoundry_b200.build import LIB_PATH
+
+    out = subprocess.run(["readelf", "-d", LIB_PATH], capture_output=True, text=True, check=True).stdout
+    needed = re.findall(r"Shared library: \[(.*?)\]", out)
+    assert not any(n.startswith("libcuda.so") or n.startswith("libcudart") for n in needed), needed
+
+
+def test_strerror_covers_codes(kf_lib):
+    texts = {kf_lib.kf_strerror(c).decode() for c in range(0, 8)}
+    assert len(texts) == 8
+    assert kf_lib.kf_strerror(12345).decode() == "unknown status"
+    assert b"sm_100a" in kf_lib.kf_version()
+
+
+FAKE = ctypes.c_void_p(0x10000)          # 16-byte aligned, never dereferenced
+MISALIGNED = ctypes.c_void_p(0x10008)
+
+
+def _fwd(lib, B=1, Hq=4, Hkv=2, Sq=8, Skv=8, D=64, q=FAKE, k=FAKE, v=FAKE, o=FAKE):
+    return lib.kf_attn_fwd(q, k, v, o, B, Hq, Hkv, Sq, Skv, D, None, 0, None)
+
+
+def test_argument_validation_without_gpu(kf_lib):
+    from kernelfoundry_b200 import _lib as L
+
+    assert _fwd(kf_lib, D=32) == L.KF_ERR_UNSUPPORTED_HEAD_DIM
+    assert _fwd(kf_lib, D=96) == L.KF_ERR_UNSUPPORTED_HEAD_DIM
+    assert _fwd(kf_lib, Hq=6, Hkv=4) == L.KF_ERR_INVALID_ARG        # H_q % H_kv != 0
+    assert _fwd(kf_lib, Hkv=0) == L.KF_ERR_INVALID_ARG
+    assert _fwd(kf_lib, B=-1) == L.KF_ERR_INVALID_ARG
+    assert _fwd(kf_lib, Skv=0) == L.KF_ERR_INVALID_ARG              # softmax over no keys
+    assert _fwd(kf_lib, q=ctypes.c_void_p(0)) == L.KF_ERR_INVALID_ARG
+    assert _fwd(kf_lib, k=MISALIGNED) == L.KF_ERR_MISALIGNED
+    assert _fwd(kf_lib, o=MISALIGNED) == L.KF_ERR_MISALIGNED
+    # Empty problems are a successful no-op and never reach the GPU.
+    assert _fwd(kf_lib, B=0) == L.KF_OK
+    assert _fwd(kf_lib, Sq=0) == L.KF_OK
+    assert kf_lib.kf_attn_fwd_partial(FAKE, FAKE, FAKE, FAKE, None, None, 1, 4, 2, 8, 8, 64, None, 0, None) \
+        == L.KF_ERR_INVALID_ARG
+    assert kf_lib.kf_attn_combine(FAKE, FAKE, FAKE, 0, FAKE, None, None, 1, 4, 8, 64, None) == L.KF_ERR_INVALID_ARG
+    assert kf_lib.kf_attn_combine(FAKE, FAKE, FAKE, 2, FAKE, None, None, 1, 4, 8, 48, None) \
+        == L.KF_ERR_UNSUPPORTED_HEAD_DIM
+    assert kf_lib.kf_attn_combine(FAKE, FAKE, FAKE, 2, FAKE, None, None, 0, 4, 8, 64, None) == L.KF_OK
+    assert kf_lib.kf_attn_workspace_bytes(1, 6, 4, 1, 100, 128) == 0
+    assert kf_lib.kf_launch_flash_attn(FAKE, FAKE, FAKE, FAKE, 1, 16, 1, 1, 48, None) \
+        == L.KF_ERR_UNSUPPORTED_HEAD_DIM
+
+
+@pytest.mark.skipif(os.path.exists("/dev/nvidia0"), reason="checks the no-driver path")
+def test_compute_call_without_driver_reports_cuda_error(kf_lib):
+    """Without a GPU a valid call fails with a status code (never a crash or a CPU fallback)."""
+    from kernelfoundry_b200 import _lib as L
+
+    rc = _fwd(kf_lib)
+    assert rc in (L.KF_ERR_CUDA, L.KF_ERR_UNSUPPORTED_DEVICE)
+    assert kf_lib.kf_last_cuda_error() != 0
+
+
+def test_python_api_refuses_cpu_tensors(kf_lib):
+    import torch
+
+    from kernelfoundry_b200 import flash_attn_fwd
+
+    q = torch.zeros(1, 2, 4, 64, dtype=torch.float16)
+    with pytest.raises(ValueError, match="CUDA"):
+        flash_attn_fwd(q, q[:, :1], q[:, :1])

@@ -1,0 +1,110 @@
+"""Parity of the short-query (decode) split-KV path on a B200, through the C ABI.
+
+The reference's own harness never checks decode (all 18 cases have
+S_q = S_kv); these cases are pinned by the fp64 oracle (reference_attn, which
+handles S_q != S_kv) and by the reference CUDA kernel in test_prefill_gpu.py.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle.attn_oracle import normal_qkv
+
+from gpu_util import assert_close, oracle64, run_fwd, to_dev
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("B", [1, 16, 64])
+def test_c3_decode_kv4096(cuda, B):
+    from kernelfoundry_b200 import plan
+
+    Q, K, V = normal_qkv(B, 32, 8, 1, 4096, 128, seed=3000 + B)
+    assert plan(B, 32, 8, 1, 4096, 128)["path"] == "decode"
+    got, Mi, Li = run_fwd(Q, K, V, cuda, return_lse=True)
+    O, rMi, rLi = oracle64(Q, K, V)
+    assert_close(got, O, f"decode B={B}")
+    assert np.abs(Mi - rMi).max() < 1e-3
+    assert np.abs(Li / rLi - 1).max() < 1e-3
+
+
+def test_c5_long_decode(cuda):
+    from kernelfoundry_b200 import plan
+
+    Q, K, V = normal_qkv(1, 32, 8, 1, 131072, 128, seed=5005)
+    pl = plan(1, 32, 8, 1, 131072, 128)
+    assert pl["path"] == "decode" and pl["n_split"] > 1
+    got = run_fwd(Q, K, V, cuda)
+    assert_close(got, oracle64(Q, K, V)[0], "long decode")
+
+
+SHAPES = [
+    (4, 32, 1, 1, 2048, 64),     # MQA, D=64 (two 16-row tiles)
+    (2, 32, 1, 1, 1000, 128),    # MQA, D=128
+    (3, 8, 8, 1, 777, 256),      # D=256
+    (2, 4, 1, 1, 300, 16),       # D=16
+    (1, 40, 8, 1, 513, 128),     # GQA ratio 5
+    (2, 32, 8, 2, 1024, 128),    # S_q = 2 (speculative-style short query)
+    (1, 32, 8, 8, 700, 128),     # R = 32
+    (1, 32, 1, 2, 4096, 64),     # R = 64 -> two row groups
+    (1, 8, 2, 1, 1, 128),        # single key
+    (2, 8, 2, 1, 63, 128),
+    (2, 8, 2, 1, 65, 128),
+    (1, 8, 2, 1, 4097, 128),
+]
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "B{}_Hq{}_Hkv{}_Sq{}_Skv{}_D{}".format(*s))
+def test_decode_shapes(cuda, shape):
+    from kernelfoundry_b200 import plan
+
+    assert plan(*shape)["path"] == "decode"
+    Q, K, V = normal_qkv(*shape, seed=7 * sum(shape))
+    got, Mi, Li = run_fwd(Q, K, V, cuda, return_lse=True)
+    O, rMi, rLi = oracle64(Q, K, V)
+    assert_close(got, O, str(shape))
+    assert np.abs(Mi - rMi).max() < 1e-3
+    assert np.abs(Li / rLi - 1).max() < 1e-3
+
+
+def test_workspace_optional_and_reusable(cuda):
+    """No workspace (single split) and a shared workspace reused across shapes give correct results."""
+    import torch
+
+    from kernelfoundry_b200 import flash_attn_fwd, plan
+    from kernelfoundry_b200.attention import new_workspace, workspace_bytes
+
+    assert plan(1, 32, 8, 1, 4096, 128, workspace_bytes=0)["n_split"] == 1
+    ws = new_workspace(max(workspace_bytes(1, 32, 8, 1, 8192, 128), workspace_bytes(4, 32, 8, 1, 3000, 128)), cuda)
+    for shape in [(1, 32, 8, 1, 8192, 128), (4, 32, 8, 1, 3000, 128), (1, 32, 8, 1, 8192, 128), (2, 8, 2, 1, 999, 128)]:
+        Q, K, V = normal_qkv(*shape, seed=sum(shape))
+        q, k, v = (to_dev(x, cuda) for x in (Q, K, V))
+        ref = oracle64(Q, K, V)[0]
+        out_ws = flash_attn_fwd(q, k, v, workspace=ws).cpu().numpy()
+        out_none = flash_attn_fwd(q, k, v, workspace=torch.empty(0, dtype=torch.uint8, device=cuda)).cpu().numpy()
+        assert_close(out_ws, ref, f"ws {shape}")
+        assert_close(out_none, ref, f"no-ws {shape}")
+    # The ticket counters at the head of the workspace are back to zero.
+    assert int(ws[:65536].view(torch.int32).abs().sum()) == 0
+
+
+def test_partials_and_combine_match_full(cuda):
+    """Per-slice partials (as on G GPUs) merged by kf_attn_combine == attention over the whole cache."""
+    import torch
+
+    from kernelfoundry_b200 import combine_partials, flash_attn_partial
+
+    Q, K, V = normal_qkv(1, 32, 8, 1, 16384, 128, seed=99)
+    q = to_dev(Q, cuda)
+    cuts = [0, 4096, 4097, 10000, 16384]
+    parts = [flash_attn_partial(q, to_dev(K[:, :, lo:hi].copy(), cuda), to_dev(V[:, :, lo:hi].copy(), cuda))
+             for lo, hi in zip(cuts[:-1], cuts[1:])]
+    O_p = torch.stack([p[0] for p in parts])
+    m_p = torch.stack([p[1] for p in parts])
+    l_p = torch.stack([p[2] for p in parts])
+    out, Mi, Li = combine_partials(O_p, m_p, l_p, return_lse=True)
+    O, rMi, rLi = oracle64(Q, K, V)
+    assert_close(out.cpu().numpy(), O, "combined")
+    assert np.abs(Mi.cpu().numpy() - rMi).max() < 1e-3
+    assert np.abs(Li.cpu().numpy() / rLi - 1).max() < 1e-3

@@ -1,0 +1,144 @@
+"""Parity of the attention forward (prefill shapes) on a B200, through the C ABI.
+
+Oracles: the fp64 NumPy restatement of kernel_models/flash_attn.py:
+reference_attn (pinned to the reference's own outputs by test_oracle.py and
+tests/golden/), the fp32 C restatement of the reference harness's cpu_attn,
+and the reference CUDA kernel itself (oracle/_ref/libkfref.so, built from the
+reference sources).  Tolerances: max-abs 2e-3 and rel-L2 1e-3 vs fp64
+(north star); max-abs 5e-2 vs fp32 cpu_attn on the 18 harness cases
+(tests/test_flash_attn.cu:22).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+import oracle
+from oracle.attn_oracle import error_stats, normal_qkv
+
+from conftest import golden_case, golden_names
+from gpu_util import assert_close, oracle64, run_fwd, to_dev
+
+pytestmark = pytest.mark.gpu
+
+
+def test_golden_vectors(cuda, sdpa_golden):
+    """Every golden case (prefill, decode, GQA, MQA, D=16/256, ragged) vs the reference's own fp64 output."""
+    for name in golden_names(sdpa_golden):
+        _, Q, K, V = golden_case(sdpa_golden, name)
+        got = run_fwd(Q, K, V, cuda)
+        assert_close(got, sdpa_golden[f"{name}/O_ref64"], name)
+
+
+@pytest.mark.parametrize("case", oracle.LEGACY_CASES, ids=lambda c: "B{}_S{}_Hq{}_Hkv{}_D{}_s{}".format(*c))
+def test_legacy_harness_case(cuda, case):
+    """The reference harness's 18 cases through the reference-compatible launcher."""
+    import torch
+
+    from kernelfoundry_b200 import launch_flash_attn
+
+    B, S, Hq, Hkv, D, seed = case
+    (q32, k32, v32), (q16, k16, v16) = oracle.legacy_case_inputs(*case)
+    q, k, v = (to_dev(x, cuda) for x in (q16, k16, v16))
+    o = torch.full((B, Hq, S, D), float("nan"), dtype=torch.float32, device=cuda)
+    rc = launch_flash_attn(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), B, S, Hq, Hkv, D, 0)
+    assert rc == 0
+    got = o.cpu().numpy()
+    ref32 = oracle.cpu_attn_f32(q32, k32, v32)          # the reference harness's check
+    assert np.abs(got - ref32).max() <= oracle.LEGACY_TOL
+    ref64 = oracle64(q16, k16, v16)[0]                  # north-star check on the same fp16 inputs
+    assert_close(got, ref64, f"legacy {case}")
+
+
+BASELINE = {
+    "C1_prefill_S512": (1, 32, 8, 512, 512, 128, 1001),
+    "C2_prefill_S4096": (1, 32, 8, 4096, 4096, 128, 1002),
+    "C4_mqa_D64": (4, 32, 1, 2048, 2048, 64, 1004),
+}
+
+
+@pytest.mark.parametrize("name", list(BASELINE))
+def test_baseline_configs_full_size(cuda, name):
+    B, Hq, Hkv, Sq, Skv, D, seed = BASELINE[name]
+    Q, K, V = normal_qkv(B, Hq, Hkv, Sq, Skv, D, seed)
+    got, Mi, Li = run_fwd(Q, K, V, cuda, return_lse=True)
+    O, rMi, rLi = oracle64(Q, K, V)
+    assert_close(got, O, name)
+    assert np.abs(Mi - rMi).max() < 1e-3
+    assert np.abs(Li / rLi - 1).max() < 1e-3
+
+
+def test_baseline_prefill_batch8_sampled(cuda):
+    """C2 at B=8 (the batch-sharded configuration): full run, oracle on b = 0 and 7."""
+    Q, K, V = normal_qkv(8, 32, 8, 4096, 4096, 128, 1012)
+    got = run_fwd(Q, K, V, cuda)
+    for b in (0, 7):
+        ref = oracle64(Q[b:b + 1], K[b:b + 1], V[b:b + 1])[0]
+        assert_close(got[b:b + 1], ref, f"b={b}")
+
+
+RAGGED = [
+    (2, 8, 2, 300, 1000, 128),
+    (1, 4, 4, 129, 17, 64),
+    (1, 2, 1, 257, 300, 256),
+    (1, 2, 2, 1000, 129, 16),
+    (3, 6, 3, 200, 64, 128),
+    (1, 2, 2, 33, 4096, 128),
+    (1, 1, 1, 256, 1, 64),
+]
+
+
+@pytest.mark.parametrize("shape", RAGGED, ids=lambda s: "B{}_Hq{}_Hkv{}_Sq{}_Skv{}_D{}".format(*s))
+def test_ragged_shapes(cuda, shape):
+    Q, K, V = normal_qkv(*shape, seed=sum(shape))
+    got, Mi, Li = run_fwd(Q, K, V, cuda, return_lse=True)
+    O, rMi, rLi = oracle64(Q, K, V)
+    assert_close(got, O, str(shape))
+    assert np.abs(Mi - rMi).max() < 1e-3
+    assert np.abs(Li / rLi - 1).max() < 1e-3
+
+
+def test_partial_form_prefill(cuda):
+    from kernelfoundry_b200 import flash_attn_partial
+
+    Q, K, V = normal_qkv(1, 8, 2, 384, 700, 128, seed=77)
+    O_u, m, l = (t.cpu().numpy() for t in flash_attn_partial(*(to_dev(x, cuda) for x in (Q, K, V))))
+    O, rMi, rLi = oracle64(Q, K, V)
+    assert_close(O_u / l[..., None], O, "partial O_u/l")
+    assert np.abs(m - rMi).max() < 1e-3
+    assert np.abs(l / rLi - 1).max() < 1e-3
+
+
+def _ref_kernel(Q, K, V, device):
+    """Run the reference CUDA kernel (compiled from its sources) on the same fp16 inputs."""
+    import torch
+
+    ref = oracle.load_ref_lib()
+    B, Hq, Sq, D = Q.shape
+    Hkv, Skv = K.shape[1], K.shape[2]
+    q, k, v = (to_dev(x, device) for x in (Q, K, V))
+    o = torch.empty((B, Hq, Sq, D), dtype=torch.float32, device=device)
+    mi = torch.empty((B, Hq, Sq), dtype=torch.float32, device=device)
+    li = torch.empty_like(mi)
+    P = ctypes.c_void_p
+    rc = ref.kfref_launch_general(P(q.data_ptr()), P(k.data_ptr()), P(v.data_ptr()), P(o.data_ptr()),
+                                  P(mi.data_ptr()), P(li.data_ptr()), B, Sq, Skv, Hq, Hkv, D,
+                                  P(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0
+    torch.cuda.synchronize()
+    return o.cpu().numpy(), mi.cpu().numpy(), li.cpu().numpy()
+
+
+@pytest.mark.parametrize("shape", [(1, 32, 8, 512, 512, 128), (2, 8, 2, 129, 129, 64), (1, 4, 1, 1, 4096, 128),
+                                   (3, 8, 8, 1, 777, 256), (1, 2, 1, 16, 16, 16)])
+def test_matches_reference_cuda_kernel(cuda, shape):
+    """Same fp16 inputs through the reference's own kernel: outputs and Mi/Li agree."""
+    Q, K, V = normal_qkv(*shape, seed=3 * sum(shape))
+    ref_o, ref_mi, ref_li = _ref_kernel(Q, K, V, cuda)
+    got, Mi, Li = run_fwd(Q, K, V, cuda, return_lse=True)
+    ma, rl = error_stats(got, ref_o)
+    assert ma <= 2e-3 and rl <= 1e-3, (ma, rl)
+    assert np.abs(Mi - ref_mi).max() < 1e-3
+    assert np.abs(Li / ref_li - 1).max() < 1e-3
