@@ -13,7 +13,8 @@ rank's batch; inputs are resident in HBM and rotate over 4 buffer sets
 (448 MiB > 2x the 126 MB L2).  `e2e` is the same metric through the public
 API (flash_attn_fwd) with the step's Q/K/V copied from pinned host memory and
 O copied back inside the timed region.  `extra` holds the decode configs
-(HBM GB/s with bytes = 2*B*H_kv*S_kv*D*2 + 2*B*H_q*D + 4*B*H_q*D), MQA D=64,
+(HBM GB/s with bytes = 2*B*H_kv*S_kv*D*2 + 2*B*H_q*D + 4*B*H_q*D; device time
+from CUDA-graph replay, the host-call time beside it), MQA D=64,
 prefill S=512 and, for N > 1, the KV-split long decode across the N GPUs.
 
 --impl reference times the reference's CPU path for the same workload: the
@@ -168,6 +169,31 @@ def time_loop(fn, iters, warmup, stream):
     return e0.elapsed_time(e1) / iters
 
 
+def time_graph(fn, n_calls, reps, stream):
+    """Mean ms per call with the n_calls calls captured once in a CUDA graph and
+    replayed `reps` times (device time without Python/launch overhead)."""
+    import torch
+
+    for i in range(n_calls):
+        fn(i)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(n_calls):
+            fn(i)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        g.replay()
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / (reps * n_calls)
+    del g
+    return ms
+
+
 def max_over_ranks(vals, world, device):
     import torch
     import torch.distributed as dist
@@ -294,8 +320,11 @@ def run_extras(args, rank, world, dev, peaks):
             j = i % rot
             flash_attn_fwd(qs[j], ks[j], vs[j], out=os_[j])
 
-        ms = time_loop(f, iters, 3, stream)
+        host_ms = time_loop(f, iters, 3, stream)
+        n_calls = rot * max(1, 8 // rot)
+        ms = time_graph(f, n_calls, max(2, iters // n_calls), stream)
         pl = plan(B, Hq, Hkv, Sq, Skv, Dh)
+        pl["host_call_us"] = round(host_ms * 1e3, 2)
         del qs, ks, vs, os_
         return ms, rot, pl
 
@@ -304,11 +333,12 @@ def run_extras(args, rank, world, dev, peaks):
         gbs = decode_bytes(B, H_Q, H_KV, 4096, D) / (ms * 1e-3) / 1e9
         out[f"decode_kv4096_B{B}"] = {"us": round(ms * 1e3, 2), "GB/s": round(gbs, 1),
                                       "frac_hbm": round(gbs / peaks["hbm_gbs"], 3), "n_split": pl["n_split"],
-                                      "rotated_sets": rot}
+                                      "rotated_sets": rot, "host_call_us": pl["host_call_us"]}
     ms, rot, pl = bench_cfg(1, H_Q, H_KV, 1, 131072, D)
     gbs = decode_bytes(1, H_Q, H_KV, 131072, D) / (ms * 1e-3) / 1e9
     out["long_decode_kv131072_1gpu"] = {"us": round(ms * 1e3, 2), "GB/s": round(gbs, 1),
-                                        "frac_hbm": round(gbs / peaks["hbm_gbs"], 3), "n_split": pl["n_split"]}
+                                        "frac_hbm": round(gbs / peaks["hbm_gbs"], 3), "n_split": pl["n_split"],
+                                        "host_call_us": pl["host_call_us"]}
     ms, rot, pl = bench_cfg(4, 32, 1, 2048, 2048, 64)
     tf = prefill_flops(4, 32, 2048, 2048, 64) / (ms * 1e-3) / 1e12
     out["mqa_d64_B4_S2048"] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 1),

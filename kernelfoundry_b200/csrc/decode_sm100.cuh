@@ -46,11 +46,12 @@ struct DecodeCfg {
     static constexpr int Q_BYTES = (QROWS * QPITCH * 2 + 15) / 16 * 16;
     static constexpr int MAX_SPLIT = 256;
     static constexpr int RED_BYTES = NW * QROWS * (D + 2) * 4;
-    static constexpr int CMB_BYTES = (MAX_SPLIT + 2) * QROWS * 4;
+    // split merge: weights [MAX_SPLIT][QROWS] + M, L, and two bulk-copy buffers of >= 1 split each
+    static constexpr int CMB_BYTES = (MAX_SPLIT * QROWS + 2 * QROWS) * 4 + 2 * QROWS * D * 4;
     static constexpr int STAGES_BYTES = NSTAGE * STAGE_BYTES;
     static constexpr int BIG0 = STAGES_BYTES > RED_BYTES ? STAGES_BYTES : RED_BYTES;
     static constexpr int BIG = BIG0 > CMB_BYTES ? BIG0 : CMB_BYTES;
-    static constexpr int SMEM_BYTES = 1024 + BIG + Q_BYTES + 256;
+    static constexpr int SMEM_BYTES = 1024 + BIG + Q_BYTES + 256;   // + barriers/flags
     static constexpr int THREADS = 32 * (NW + 1);
     static_assert(NW * 16 == TK, "each consumer warp owns 16 rows of a stage");
     static_assert(SMEM_BYTES <= 232448, "shared memory over budget");
@@ -67,6 +68,7 @@ struct DecodeParams {
     int H_q, H_kv, S_q, S_kv, G, R, n_rg, n_split, chunk;
     float scale_log2, scale;
     int unnormalized;
+    int kv_box;            // rows per K/V TMA box: min(TK, S_kv)
     unsigned long long timeout_ns;
 };
 
@@ -84,7 +86,8 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
     uint16_t* sQ = reinterpret_cast<uint16_t*>(smem + C::BIG);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BIG + C::Q_BYTES);
     uint64_t* empty = full + NSTAGE;
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + NSTAGE);
+    uint64_t* merge_bar = empty + NSTAGE;      // [2] split-merge bulk copies
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(merge_bar + 2);
     volatile int* is_last = abort_flag + 1;
 
     const int tid = threadIdx.x;
@@ -107,18 +110,30 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], NW);
         }
+        mbar_init(&merge_bar[0], 1);
+        mbar_init(&merge_bar[1], 1);
         *abort_flag = 0;
         *is_last = 0;
         fence_mbar_init();
     }
-    // Q rows of this (b, h_kv, row group) -> padded shared tile (rows >= nrows are zero).
-    for (int idx = tid; idx < QROWS * (D / 8); idx += C::THREADS) {
-        const int row = idx / (D / 8), ch = idx % (D / 8);
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (row < nrows) v = *reinterpret_cast<const uint4*>(p.Q + (row_base + row) * D + ch * 8);
-        *reinterpret_cast<uint4*>(sQ + row * QPITCH + ch * 8) = v;
+    if (p.kv_box < TK) {
+        // Short KV: TMA fills only kv_box rows of each tile; the rest stay zero.
+        for (int i = tid; i < C::STAGES_BYTES / 16; i += C::THREADS)
+            reinterpret_cast<uint4*>(sBig)[i] = make_uint4(0, 0, 0, 0);
+        fence_proxy_async_smem();
     }
     __syncthreads();
+    if (warp < NW) {
+        // Consumers stage Q (padded, rows >= nrows zero) while the producer's first
+        // K/V copies are already in flight.
+        for (int idx = tid; idx < QROWS * (D / 8); idx += NW * 32) {
+            const int row = idx / (D / 8), ch = idx % (D / 8);
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (row < nrows) v = *reinterpret_cast<const uint4*>(p.Q + (row_base + row) * D + ch * 8);
+            *reinterpret_cast<uint4*>(sQ + row * QPITCH + ch * 8) = v;
+        }
+        named_bar_sync(1, NW * 32);
+    }
 
     float o[MT][D / 8][4];
     float mrow[MT][2], lsum[MT][2];
@@ -144,7 +159,7 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
                     atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_SOFTMAX);
                     break;
                 }
-                mbar_arrive_expect_tx(&full[slot], C::STAGE_BYTES);
+                mbar_arrive_expect_tx(&full[slot], 2 * NSPAN * p.kv_box * SWB);
                 uint8_t* dK = sBig + slot * C::STAGE_BYTES;
                 uint8_t* dV = dK + C::TILE_BYTES;
                 const int row = kv_lo + i * TK;
@@ -328,8 +343,12 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         return;
     }
 
-    // ---- split partial: (m, l, O_u) relative to this split's max
+    // ---- split partial: (m, l, O_u) relative to this split's max.
+    // Layout: a (b, h_kv, row group) unit owns rows [row_base, row_base + nrows);
+    // its partials are [split][row][D] at row_base * ns * D, so a run of splits
+    // is one contiguous block the merging CTA can bulk-copy.
     const int ns = p.n_split;
+    const size_t unit_off = row_base * static_cast<size_t>(ns);
     for (int idx = tid; idx < nrows * (D / 4); idx += C::THREADS) {
         const int row = idx / (D / 4), d = (idx % (D / 4)) * 4;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -339,12 +358,14 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
             const float4 v = *reinterpret_cast<const float4*>(red_o + (w * QROWS + row) * D + d);
             acc.x += wt * v.x; acc.y += wt * v.y; acc.z += wt * v.z; acc.w += wt * v.w;
         }
-        *reinterpret_cast<float4*>(p.part_O + ((row_base + row) * ns + split) * D + d) = acc;
+        *reinterpret_cast<float4*>(p.part_O + (unit_off + static_cast<size_t>(split) * nrows + row) * D + d) = acc;
     }
     if (tid < nrows) {
-        *reinterpret_cast<float2*>(p.part_ml + ((row_base + tid) * ns + split) * 2) = make_float2(Mrow[tid], Lrow[tid]);
+        *reinterpret_cast<float2*>(p.part_ml + (unit_off + static_cast<size_t>(split) * nrows + tid) * 2) =
+            make_float2(Mrow[tid], Lrow[tid]);
     }
     __threadfence();
+    fence_proxy_async_global();
     __syncthreads();
     const size_t cidx = (static_cast<size_t>(b) * p.H_kv + hk) * p.n_rg + rg;
     if (tid == 0) {
@@ -354,42 +375,103 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
     __syncthreads();
     if (!*is_last) return;
     __threadfence();
+    fence_proxy_async_global();
 
-    // ---- last CTA of this (b, h_kv, row group): merge all splits
-    float* swt = reinterpret_cast<float*>(sBig);               // [ns][QROWS]
-    float* sM = swt + ns * QROWS;
+    // ---- last CTA of this unit: merge all splits.
+    // (1) per row: M = max_s m_s, weights w_s = e^{m_s - M}, L = sum_s w_s l_s
+    //     (one warp per row, lanes over splits);
+    // (2) O = sum_s w_s O_s / L, with runs of splits brought into shared memory
+    //     by double-buffered TMA bulk copies and reduced from there.
+    constexpr int WT_BYTES = (C::MAX_SPLIT * QROWS + 2 * QROWS) * 4;
+    float* swt = reinterpret_cast<float*>(sBig + C::BIG - WT_BYTES);   // [ns][nrows]
+    float* sM = swt + C::MAX_SPLIT * QROWS;
     float* sL = sM + QROWS;
-    if (tid < nrows) {
-        const float* ml = p.part_ml + (row_base + tid) * ns * 2;
+    const float* ml = p.part_ml + unit_off * 2;
+    for (int r = warp; r < nrows; r += NW + 1) {
         float M = -CUDART_INF_F;
-        for (int s2 = 0; s2 < ns; ++s2) M = fmaxf(M, __ldcg(ml + 2 * s2));
+        for (int s2 = lane; s2 < ns; s2 += 32) M = fmaxf(M, __ldcg(ml + (s2 * nrows + r) * 2));
+#pragma unroll
+        for (int o2 = 16; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
         const float Mu = (M == -CUDART_INF_F) ? 0.f : M;
         float L = 0.f;
-        for (int s2 = 0; s2 < ns; ++s2) {
-            const float wt = ex2_approx((__ldcg(ml + 2 * s2) - Mu) * c);
-            swt[s2 * QROWS + tid] = wt;
-            L += wt * __ldcg(ml + 2 * s2 + 1);
+        for (int s2 = lane; s2 < ns; s2 += 32) {
+            const float2 v = __ldcg(reinterpret_cast<const float2*>(ml + (s2 * nrows + r) * 2));
+            const float wt = ex2_approx((v.x - Mu) * c);
+            swt[s2 * nrows + r] = wt;
+            L += wt * v.y;
         }
-        sM[tid] = M;
-        sL[tid] = L;
+#pragma unroll
+        for (int o2 = 16; o2 > 0; o2 >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o2);
+        if (lane == 0) {
+            sM[r] = M;
+            sL[r] = L;
+        }
     }
     __syncthreads();
-    for (int idx = tid; idx < nrows * (D / 4); idx += C::THREADS) {
-        const int row = idx / (D / 4), d = (idx % (D / 4)) * 4;
-        const float4* src = reinterpret_cast<const float4*>(p.part_O + (row_base + row) * ns * D + d);
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int s2 = 0; s2 < ns; ++s2) {
-            const float wt = swt[s2 * QROWS + row];
-            const float4 v = __ldcg(src + s2 * (D / 4));
-            acc.x += wt * v.x; acc.y += wt * v.y; acc.z += wt * v.z; acc.w += wt * v.w;
-        }
-        const float sc = p.unnormalized ? 1.f : 1.f / sL[row];
-        acc.x *= sc; acc.y *= sc; acc.z *= sc; acc.w *= sc;
-        *reinterpret_cast<float4*>(p.O + (row_base + row) * D + d) = acc;
+
+    constexpr int KMAX = (QROWS * (D / 4) + C::THREADS - 1) / C::THREADS;
+    const int items = nrows * (D / 4);
+    const uint32_t split_bytes = static_cast<uint32_t>(nrows) * D * 4;
+    const int buf_bytes = ((C::BIG - WT_BYTES) / 2) / 16 * 16;
+    int per_chunk = buf_bytes / static_cast<int>(split_bytes);
+    per_chunk = per_chunk < 1 ? 1 : (per_chunk > ns ? ns : per_chunk);
+    const int n_chunks = (ns + per_chunk - 1) / per_chunk;
+    const float* src = p.part_O + unit_off * D;
+    auto issue = [&](int ch) {
+        const int s0 = ch * per_chunk;
+        const int cnt = min(per_chunk, ns - s0);
+        uint64_t* bar = &merge_bar[ch & 1];
+        mbar_arrive_expect_tx(bar, cnt * split_bytes);
+        bulk_g2s(sBig + (ch & 1) * buf_bytes, src + static_cast<size_t>(s0) * nrows * D, cnt * split_bytes, bar);
+    };
+    if (tid == 0) {
+        issue(0);
+        if (n_chunks > 1) issue(1);
     }
-    if (tid < nrows) {
-        if (p.Mi) p.Mi[row_base + tid] = sM[tid] * p.scale;
-        if (p.Li) p.Li[row_base + tid] = sL[tid];
+    float4 acc[KMAX];
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    bool ok = true;
+    for (int ch = 0; ch < n_chunks; ++ch) {
+        int dummy = 0;
+        ok = mbar_wait_bounded(&merge_bar[ch & 1], (ch >> 1) & 1, &dummy, p.timeout_ns);
+        if (!ok) {   // cannot happen unless the copy engine stalls; leave the unit unwritten
+            atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_TMA);
+            break;
+        }
+        const float* sb = reinterpret_cast<const float*>(sBig + (ch & 1) * buf_bytes);
+        const int s0 = ch * per_chunk;
+        const int cnt = min(per_chunk, ns - s0);
+#pragma unroll
+        for (int k = 0; k < KMAX; ++k) {
+            const int it = tid + k * C::THREADS;
+            if (it < items) {
+                const int r = it / (D / 4), d = (it % (D / 4)) * 4;
+                for (int s2 = 0; s2 < cnt; ++s2) {
+                    const float wt = swt[(s0 + s2) * nrows + r];
+                    const float4 v = *reinterpret_cast<const float4*>(sb + (s2 * nrows + r) * D + d);
+                    acc[k].x += wt * v.x; acc[k].y += wt * v.y; acc[k].z += wt * v.z; acc[k].w += wt * v.w;
+                }
+            }
+        }
+        __syncthreads();   // buffer (ch & 1) fully read
+        if (tid == 0 && ch + 2 < n_chunks) issue(ch + 2);
+    }
+    if (ok) {
+#pragma unroll
+        for (int k = 0; k < KMAX; ++k) {
+            const int it = tid + k * C::THREADS;
+            if (it < items) {
+                const int r = it / (D / 4), d = (it % (D / 4)) * 4;
+                const float sc = p.unnormalized ? 1.f : 1.f / sL[r];
+                *reinterpret_cast<float4*>(p.O + (row_base + r) * D + d) =
+                    make_float4(acc[k].x * sc, acc[k].y * sc, acc[k].z * sc, acc[k].w * sc);
+            }
+        }
+        if (tid < nrows) {
+            if (p.Mi) p.Mi[row_base + tid] = sM[tid] * p.scale;
+            if (p.Li) p.Li[row_base + tid] = sL[tid];
+        }
     }
     if (tid == 0) p.counters[cidx] = 0u;
 }

@@ -11,6 +11,7 @@
 #include <atomic>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -83,8 +84,11 @@ int device_info(DeviceInfo** out) {
 
 // Sets the dynamic shared-memory opt-in of a kernel once per device and
 // returns how many of its CTAs fit on one SM.
-template <typename Kern>
-int kernel_setup(Kern kern, int smem_bytes, int threads, int* blocks_per_sm) {
+// Keyed by the kernel itself (a template argument): every instantiation has
+// its own cache slot even though they share one function type.
+template <auto Kern>
+int kernel_setup(int smem_bytes, int threads, int* blocks_per_sm) {
+    constexpr auto kern = Kern;
     struct Slot { std::atomic<int> bps{0}; };
     static Slot slots[kMaxDevices];
     int dev = 0;
@@ -177,7 +181,7 @@ size_t split_ws_bytes(long long rows, int n_split, int D) {
 template <int D, int MT>
 int decode_blocks_per_sm(int* bps) {
     using C = kf::DecodeCfg<D, MT>;
-    return kernel_setup(kf::decode_fwd_kernel<D, MT>, C::SMEM_BYTES, C::THREADS, bps);
+    return kernel_setup<kf::decode_fwd_kernel<D, MT>>(C::SMEM_BYTES, C::THREADS, bps);
 }
 
 int decode_bps(int D, int mt, int* bps) {
@@ -208,7 +212,16 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
     const int TK = 64;
     const int total_stages = (S_kv + TK - 1) / TK;
     const double cap = static_cast<double>(sm_count) * blocks_per_sm;
-    const double ovh = 2.0;   // per-CTA fixed cost in stage-equivalents
+    // Cost model (microseconds): HBM-bound streaming of all K/V bytes, a fixed
+    // start-up per CTA wave, a per-CTA rate limit (bytes a CTA keeps in flight
+    // / latency), plus the split merge (one CTA per unit bulk-copies
+    // n_split partials of nrows x D floats).
+    // Constants fitted to a split-count sweep on B200 (KV=4096 at B=1/16/64, KV=131072 at B=1).
+    const double kBwTotal = 6.0e3, kBwCta = 50.0, kBwMerge = 100.0;   // GB/s == bytes/ns -> x1e-3 per us
+    const double kT0 = 2.0, kMerge0 = 1.5;
+    const double stage_bytes = 2.0 * TK * D * 2;
+    const double total_bytes = static_cast<double>(units) * total_stages * stage_bytes;
+    const int nrows = R < 16 * pl->mt ? R : 16 * pl->mt;
     int best_s = 1;
     double best_cost = 1e300;
     const int max_s = total_stages < kf::DecodeCfg<128, 1>::MAX_SPLIT ? total_stages : kf::DecodeCfg<128, 1>::MAX_SPLIT;
@@ -218,11 +231,24 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
         const int s_eff = (total_stages + nst - 1) / nst;
         if (s_eff != s) continue;
         if (s > 1 && (units > kCounterSlots || split_ws_bytes(rows, s, D) > ws_bytes)) break;
-        const double cost = units * s * (nst + ovh) / cap + (nst + ovh) + (s > 1 ? 1.0 : 0.0);
-        if (cost < best_cost) {
+        const double ctas = static_cast<double>(units) * s;
+        const double bw = ctas * kBwCta < kBwTotal ? ctas * kBwCta : kBwTotal;
+        const double t_stream = total_bytes / (bw * 1e3) + kT0 * std::ceil(ctas / cap);
+        const double t_cta = kT0 + nst * stage_bytes / (kBwCta * 1e3);
+        const double t_merge = s > 1 ? kMerge0 + s * nrows * D * 4.0 / (kBwMerge * 1e3) : 0.0;
+        const double cost = (t_stream > t_cta ? t_stream : t_cta) + t_merge;
+        if (cost < best_cost * 0.999) {
             best_cost = cost;
             best_s = s;
         }
+    }
+    // Tuning override (benchmark sweeps): KF_DECODE_NSPLIT=<n> forces the split
+    // count when the workspace allows it.
+    if (const char* ov = std::getenv("KF_DECODE_NSPLIT")) {
+        int want = std::atoi(ov);
+        if (want >= 1 && want <= max_s && (want == 1 || (units <= kCounterSlots &&
+                                                        split_ws_bytes(rows, want, D) <= ws_bytes)))
+            best_s = (total_stages + ((total_stages + want - 1) / want) - 1) / ((total_stages + want - 1) / want);
     }
     const int nst = (total_stages + best_s - 1) / best_s;
     pl->n_split = best_s;
@@ -253,12 +279,16 @@ int launch_prefill(const void* Q, const void* K, const void* V, float* O, float*
                    int H_q, int H_kv, int S_q, int S_kv, cudaStream_t s) {
     using C = kf::PrefillCfg<D>;
     int bps = 0;
-    int rc = kernel_setup(kf::prefill_fwd_kernel<D>, C::SMEM_BYTES, C::THREADS, &bps);
+    int rc = kernel_setup<kf::prefill_fwd_kernel<D>>(C::SMEM_BYTES, C::THREADS, &bps);
     if (rc != KF_OK) return rc;
+    // A TMA box may not exceed the tensor: short sequences load S rows and the
+    // kernel keeps the remaining tile rows zero.
+    const int q_box = S_q < C::BM ? S_q : C::BM;
+    const int kv_box = S_kv < C::BC ? S_kv : C::BC;
     CUtensorMap mq, mk, mv;
-    if ((rc = make_map(&mq, Q, D, S_q, static_cast<long long>(B) * H_q, C::BM, C::SWB)) != KF_OK) return rc;
-    if ((rc = make_map(&mk, K, D, S_kv, static_cast<long long>(B) * H_kv, C::BC, C::SWB)) != KF_OK) return rc;
-    if ((rc = make_map(&mv, V, D, S_kv, static_cast<long long>(B) * H_kv, C::BC, C::SWB)) != KF_OK) return rc;
+    if ((rc = make_map(&mq, Q, D, S_q, static_cast<long long>(B) * H_q, q_box, C::SWB)) != KF_OK) return rc;
+    if ((rc = make_map(&mk, K, D, S_kv, static_cast<long long>(B) * H_kv, kv_box, C::SWB)) != KF_OK) return rc;
+    if ((rc = make_map(&mv, V, D, S_kv, static_cast<long long>(B) * H_kv, kv_box, C::SWB)) != KF_OK) return rc;
     kf::PrefillParams p;
     p.O = O;
     p.Mi = Mi;
@@ -272,6 +302,8 @@ int launch_prefill(const void* Q, const void* K, const void* V, float* O, float*
     p.scale_log2 = p.scale * 1.4426950408889634f;
     p.unnormalized = unnorm;
     p.timeout_ns = g_timeout_ns.load();
+    p.q_box = q_box;
+    p.kv_box = kv_box;
     const int rows_per_cta = C::NQ * C::BM;
     dim3 grid((S_q + rows_per_cta - 1) / rows_per_cta, H_q, B);
     kf::prefill_fwd_kernel<D><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, p);
@@ -284,11 +316,12 @@ int launch_decode_t(const Plan& pl, const void* Q, const void* K, const void* V,
                     int unnorm, int B, int H_q, int H_kv, int S_q, int S_kv, void* ws, cudaStream_t s) {
     using C = kf::DecodeCfg<D, MT>;
     int bps = 0;
-    int rc = kernel_setup(kf::decode_fwd_kernel<D, MT>, C::SMEM_BYTES, C::THREADS, &bps);
+    int rc = kernel_setup<kf::decode_fwd_kernel<D, MT>>(C::SMEM_BYTES, C::THREADS, &bps);
     if (rc != KF_OK) return rc;
+    const int kv_box = S_kv < C::TK ? S_kv : C::TK;
     CUtensorMap mk, mv;
-    if ((rc = make_map(&mk, K, D, S_kv, static_cast<long long>(B) * H_kv, C::TK, C::SWB)) != KF_OK) return rc;
-    if ((rc = make_map(&mv, V, D, S_kv, static_cast<long long>(B) * H_kv, C::TK, C::SWB)) != KF_OK) return rc;
+    if ((rc = make_map(&mk, K, D, S_kv, static_cast<long long>(B) * H_kv, kv_box, C::SWB)) != KF_OK) return rc;
+    if ((rc = make_map(&mv, V, D, S_kv, static_cast<long long>(B) * H_kv, kv_box, C::SWB)) != KF_OK) return rc;
     kf::DecodeParams p;
     p.Q = static_cast<const uint16_t*>(Q);
     p.O = O;
@@ -311,6 +344,7 @@ int launch_decode_t(const Plan& pl, const void* Q, const void* K, const void* V,
     p.scale_log2 = p.scale * 1.4426950408889634f;
     p.unnormalized = unnorm;
     p.timeout_ns = g_timeout_ns.load();
+    p.kv_box = kv_box;
     dim3 grid(pl.n_split, H_kv * pl.n_rg, B);
     kf::decode_fwd_kernel<D, MT><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
     cudaError_t e = cudaGetLastError();

@@ -14,12 +14,15 @@
 //               past S_q / S_kv).
 //   warp 1      TMEM owner + single-thread MMA issuer:
 //                 S_t  = Q_t K_j^T        (tcgen05.mma, M=128, N=BC, fp32 in TMEM)
-//                 O_t += P_t V_j          (tcgen05.mma, M=128, N=D,  fp32 in TMEM)
+//                 O_t += P_t V_j          (tcgen05.mma, A = P_t from TMEM, M=128, N=D)
 //               in the order PV_A(j-1), QK_A(j), PV_B(j-1), QK_B(j), so the tensor
 //               core works on one tile while the other tile's softmax runs.
 //   warps 4..   one softmax warpgroup per Q tile, one thread per query row:
 //               tcgen05.ld of the S row, row max in registers, exp2 with the
-//               scale folded in, P (fp16) written to swizzled shared memory,
+//               scale folded in, P (fp16 pairs) written back over the first
+//               BC/2 TMEM columns of S_t with tcgen05.st (the PV MMA's A operand;
+//               the next QK MMA into S_t is issued after that PV, and tcgen05 MMAs
+//               from one thread execute in order),
 //               lazy rescale of the O row in TMEM only when the running max
 //               grows by more than 2^8; epilogue O /= l straight from TMEM.
 // All waits are bounded (kf_ptx.cuh); a timeout raises a device error word
@@ -42,10 +45,9 @@ struct PrefillCfg {
     static constexpr int NSPAN = D / SWE;              // spans (TMA boxes) per row
     static constexpr int Q_BYTES = BM * D * 2;
     static constexpr int KV_BYTES = BC * D * 2;
-    static constexpr int P_BYTES = BM * BC * 2;
     static constexpr int SMEM_LIMIT = 232448;          // 227 KB opt-in per CTA
     static constexpr int BAR_BYTES = 1024;
-    static constexpr int FIXED = NQ * (Q_BYTES + P_BYTES);
+    static constexpr int FIXED = NQ * Q_BYTES;
     static constexpr int NSLOT_RAW = (SMEM_LIMIT - 1024 - BAR_BYTES - FIXED) / KV_BYTES;
     static constexpr int NSLOT = NSLOT_RAW > 8 ? 8 : NSLOT_RAW;
     static constexpr int SMEM_BYTES = 1024 + FIXED + NSLOT * KV_BYTES + BAR_BYTES;
@@ -53,6 +55,13 @@ struct PrefillCfg {
     static constexpr int TMEM_COLS = TMEM_USED <= 32 ? 32 : TMEM_USED <= 64 ? 64 : TMEM_USED <= 128 ? 128
                                    : TMEM_USED <= 256 ? 256 : 512;
     static constexpr int THREADS = 128 * (1 + NQ);
+    // Registers after rebalancing (NQ == 2: 384 threads launch with 168 each):
+    // control warpgroup 128 x 112 + softmax warpgroups 256 x 192 = 63488 <= 64512.
+    static constexpr bool REBALANCE = NQ == 2;
+    static constexpr int REG_CTRL = 112;
+    static constexpr int REG_SOFTMAX = 192;
+    static_assert(!REBALANCE || 128 * REG_CTRL + 256 * REG_SOFTMAX <= THREADS * (65536 / THREADS / 8 * 8),
+                  "register split exceeds the launch allocation");
     static_assert(NSLOT >= 2, "K/V ring needs at least two slots");
     static_assert(SMEM_BYTES <= SMEM_LIMIT, "shared memory over budget");
     static_assert(TMEM_USED <= 512, "TMEM over budget");
@@ -66,6 +75,8 @@ struct PrefillParams {
     float scale_log2;   // (1/sqrt(D)) * log2(e)
     float scale;        // 1/sqrt(D)
     int unnormalized;   // 1: write O_u = sum exp(s - Mi) v (partial form), Mi/Li required
+    int q_box;          // rows per Q TMA box: min(BM, S_q)
+    int kv_box;         // rows per K/V TMA box: min(BC, S_kv)
     unsigned long long timeout_ns;
 };
 
@@ -96,8 +107,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQ = smem;
-    uint8_t* sP = sQ + NQ * C::Q_BYTES;
-    uint8_t* sKV = sP + NQ * C::P_BYTES;
+    uint8_t* sKV = sQ + NQ * C::Q_BYTES;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + NSLOT * C::KV_BYTES);
     uint64_t* q_full = bars;
     uint64_t* s_full = q_full + NQ;
@@ -134,6 +144,14 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         *abort_flag = 0;
         fence_mbar_init();
     }
+    if (p.q_box < BM || p.kv_box < BC) {
+        // Short sequence: TMA writes only the first box rows of each tile; the
+        // remaining rows must read as zero (zero V rows keep 0 * V finite).
+        for (int i = threadIdx.x; i < (NQ * C::Q_BYTES + NSLOT * C::KV_BYTES) / 16;
+             i += blockDim.x)
+            reinterpret_cast<uint4*>(sQ)[i] = make_uint4(0, 0, 0, 0);
+        fence_proxy_async_smem();
+    }
     if (warp == 1) {
         tmem_alloc(tmem_slot, C::TMEM_COLS);
         tmem_relinquish();
@@ -145,14 +163,17 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
+        if constexpr (C::REBALANCE) setmaxnreg_dec<C::REG_CTRL>();
         if (lane == 0) {
             tma_prefetch_desc(&tmQ);
             tma_prefetch_desc(&tmK);
             tma_prefetch_desc(&tmV);
             const int bh_q = b * p.H_q + h;
             const int bh_kv = b * p.H_kv + h_kv;
+            const uint32_t q_bytes = NSPAN * p.q_box * SWB;
+            const uint32_t kv_bytes = NSPAN * p.kv_box * SWB;
             for (int t = 0; t < nq_active; ++t) {
-                mbar_arrive_expect_tx(&q_full[t], C::Q_BYTES);
+                mbar_arrive_expect_tx(&q_full[t], q_bytes);
                 for (int s = 0; s < NSPAN; ++s)
                     tma_load_3d(sQ + t * C::Q_BYTES + s * BM * SWB, &tmQ, &q_full[t], s * SWE, q_row0 + t * BM, bh_q);
             }
@@ -165,7 +186,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_MMA);
                     break;
                 }
-                mbar_arrive_expect_tx(&kv_full[slot], C::KV_BYTES);
+                mbar_arrive_expect_tx(&kv_full[slot], kv_bytes);
                 const CUtensorMap* map = (i & 1) ? &tmV : &tmK;
                 uint8_t* dst = sKV + slot * C::KV_BYTES;
                 for (int s = 0; s < NSPAN; ++s)
@@ -182,12 +203,12 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
+        if constexpr (C::REBALANCE) setmaxnreg_dec<C::REG_CTRL>();
         if (lane == 0) {
             constexpr uint32_t idesc_qk = umma_idesc_f16_f32(BM, BC, false, false);
             constexpr uint32_t idesc_pv = umma_idesc_f16_f32(BM, D, false, true);
             constexpr uint32_t lay_qk = umma_layout_code(SWB);
-            constexpr uint32_t lay_p = umma_layout_code(128);
-            const uint32_t sQa = smem_u32(sQ), sPa = smem_u32(sP), sKVa = smem_u32(sKV);
+            const uint32_t sQa = smem_u32(sQ), sKVa = smem_u32(sKV);
             bool ok = true;
             for (int t = 0; t < nq_active && ok; ++t) ok = mbar_wait_bounded(&q_full[t], 0, abort_flag, p.timeout_ns);
             if (!ok) atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_TMA);
@@ -209,15 +230,13 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                             atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_SOFTMAX); ok = false; break;
                         }
                         tc_fence_after();
-                        const uint32_t pbase = sPa + t * C::P_BYTES;
                         const uint32_t vbase = sKVa + slotV * C::KV_BYTES;
 #pragma unroll
                         for (int kk = 0; kk < BC / 16; ++kk) {
-                            // P: K-major, 64-element spans of BM rows; V: MN-major spans of SWE columns.
-                            const uint32_t pa = pbase + (kk * 16 / 64) * (BM * 128) + ((kk * 16) % 64) * 2;
-                            const uint64_t adesc = umma_desc(pa, 16, 8 * 128, lay_p);
+                            // A = P_t in TMEM (fp16 pairs over the first BC/2 columns of S_t);
+                            // B = V: MN-major spans of SWE columns, 8-row groups of SWB bytes.
                             const uint64_t bdesc = umma_desc(vbase + kk * 16 * SWB, BC * SWB, 8 * SWB, lay_qk);
-                            umma_ss(tO, adesc, bdesc, idesc_pv, (j > 1 || kk > 0) ? 1u : 0u);
+                            umma_ts(tO, tS + kk * 8, bdesc, idesc_pv, (j > 1 || kk > 0) ? 1u : 0u);
                         }
                         if (j == n_kv) umma_commit(&o_full[t]);
                     }
@@ -243,8 +262,11 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             umma_commit(mma_done);
             mbar_wait_drain(mma_done, 0, p.timeout_ns);
         }
-    } else if (warp >= 4) {
+    } else if (warp < 4) {
+        if constexpr (C::REBALANCE) setmaxnreg_dec<C::REG_CTRL>();   // idle warps of the control group
+    } else {
         // ------------------------------------------------------------ softmax warpgroups
+        if constexpr (C::REBALANCE) setmaxnreg_inc<C::REG_SOFTMAX>();
         const int t = (warp - 4) >> 2;
         const int wq = warp & 3;                 // TMEM sub-partition of this warp
         const int row = wq * 32 + lane;          // query row within the tile
@@ -252,7 +274,6 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             const uint32_t tl = tmem + (static_cast<uint32_t>(wq * 32) << 16);
             const uint32_t tS = tl + t * BC;
             const uint32_t tO = tl + NQ * BC + t * D;
-            uint8_t* sPt = sP + t * C::P_BYTES;
             const float c = p.scale_log2;
             float m_ref = -CUDART_INF_F, m_true = -CUDART_INF_F, l = 0.f;
             bool ok = true;
@@ -272,16 +293,19 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     for (int cc = 0; cc < BC; ++cc)
                         if (cc >= kv_valid) sr[cc] = __float_as_uint(-CUDART_INF_F);
                 }
-                float mx0 = __uint_as_float(sr[0]), mx1 = __uint_as_float(sr[1]);
-                float mx2 = __uint_as_float(sr[2]), mx3 = __uint_as_float(sr[3]);
+#define KF_S(i) __uint_as_float(sr[i])
+                // Row max: three-input max, four independent chains.
+                float mx0 = KF_S(0), mx1 = KF_S(1), mx2 = KF_S(2), mx3 = KF_S(3);
 #pragma unroll
-                for (int cc = 4; cc < BC; cc += 4) {
-                    mx0 = fmaxf(mx0, __uint_as_float(sr[cc]));
-                    mx1 = fmaxf(mx1, __uint_as_float(sr[cc + 1]));
-                    mx2 = fmaxf(mx2, __uint_as_float(sr[cc + 2]));
-                    mx3 = fmaxf(mx3, __uint_as_float(sr[cc + 3]));
+                for (int cc = 4; cc + 8 <= BC; cc += 8) {
+                    mx0 = fmax3f(mx0, KF_S(cc), KF_S(cc + 1));
+                    mx1 = fmax3f(mx1, KF_S(cc + 2), KF_S(cc + 3));
+                    mx2 = fmax3f(mx2, KF_S(cc + 4), KF_S(cc + 5));
+                    mx3 = fmax3f(mx3, KF_S(cc + 6), KF_S(cc + 7));
                 }
-                const float m_new = fmaxf(m_true, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)));
+                mx0 = fmax3f(mx0, KF_S(BC - 4), KF_S(BC - 3));
+                mx1 = fmax3f(mx1, KF_S(BC - 2), KF_S(BC - 1));
+                const float m_new = fmax3f(m_true, fmaxf(mx0, mx1), fmaxf(mx2, mx3));
                 m_true = m_new;
                 // Lazy rescale: keep the reference max unless the row max grew by
                 // more than 2^8 (P <= 256 stays exact enough in fp16, l and O in fp32).
@@ -298,24 +322,29 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                         l *= f;
                     }
                 }
-                const float neg = -m_ref * c;
-                float s0 = 0.f, s1 = 0.f;
+                // P = 2^(s*c - m_ref*c): paired FMA, MUFU ex2, paired row-sum adds;
+                // packed to fp16 pairs and written over the first BC/2 TMEM
+                // columns of S_t (this thread's row), the A operand of the PV MMA.
+                const float2 c2 = make_float2(c, c);
+                const float2 neg2 = make_float2(-m_ref * c, -m_ref * c);
+                float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+                uint32_t pk[BC / 2];
 #pragma unroll
-                for (int ch = 0; ch < BC / 8; ++ch) {
-                    float e[8];
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) e[k] = ex2_approx(fmaf(__uint_as_float(sr[ch * 8 + k]), c, neg));
-                    s0 += (e[0] + e[1]) + (e[2] + e[3]);
-                    s1 += (e[4] + e[5]) + (e[6] + e[7]);
-                    uint4 v;
-                    v.x = pack_half2(e[0], e[1]);
-                    v.y = pack_half2(e[2], e[3]);
-                    v.z = pack_half2(e[4], e[5]);
-                    v.w = pack_half2(e[6], e[7]);
-                    const int span = ch >> 3, chunk = ch & 7;
-                    *reinterpret_cast<uint4*>(sPt + span * (BM * 128) + row * 128 + ((chunk ^ (row & 7)) << 4)) = v;
+                for (int i = 0; i < BC; i += 4) {
+                    const float2 x0 = ffma2(make_float2(KF_S(i), KF_S(i + 1)), c2, neg2);
+                    const float2 x1 = ffma2(make_float2(KF_S(i + 2), KF_S(i + 3)), c2, neg2);
+                    const float2 e0 = make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
+                    const float2 e1 = make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
+                    acc0 = fadd2(acc0, e0);
+                    acc1 = fadd2(acc1, e1);
+                    pk[i / 2] = pack_half2(e0.x, e0.y);
+                    pk[i / 2 + 1] = pack_half2(e1.x, e1.y);
                 }
-                l += s0 + s1;
+#undef KF_S
+#pragma unroll
+                for (int cc = 0; cc < BC / 64; ++cc)
+                    tmem_st32(tS + cc * 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[cc * 32]));
+                l += (acc0.x + acc0.y) + (acc1.x + acc1.y);
                 if (rescale) {
                     // O_t is stable here: PV_t(j-1) completed before S_t(j) was committed.
 #pragma unroll
@@ -327,9 +356,8 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                         for (int k = 0; k < OCH; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * f);
                         tmem_st_chunk<OCH>(tO + dc * OCH, o);
                     }
-                    tmem_wait_st();
                 }
-                fence_proxy_async_smem();
+                tmem_wait_st();          // P (and any rescaled O) written before the MMA reads them
                 tc_fence_before();
                 mbar_arrive(&p_full[t]);
             }
