@@ -16,7 +16,7 @@ PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 REPO_DIR = os.path.dirname(PKG_DIR)
 CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_DIR = os.path.join(PKG_DIR, "lib")
-LIB_PATH = os.path.join(LIB_DIR, "libkf_attn.so")
+LIB_PATH = os.environ.get("KF_LIB_PATH") or os.path.join(LIB_DIR, "libkf_attn.so")
 SOURCES = ["kf_api.cu"]
 HEADERS = ["kf_ptx.cuh", "prefill_sm100.cuh", "decode_sm100.cuh"]
 
