@@ -113,6 +113,29 @@ int kf_attn_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t work
 int kf_launch_flash_attn(const uint16_t* Q, const uint16_t* K, const uint16_t* V, float* O,
                          int B, int S, int H_q, int H_kv, int D, void* stream);
 
+/* Short-query (decode) attention that allocates nothing and takes no workspace.
+ * No counterpart in the reference (its launcher cudaMallocs Mi/Li on every
+ * call, tests/test_flash_attn.cu:60-70); this entry exists for callers that
+ * cannot allocate device memory at call time: serving loops that gave all free
+ * device memory to a KV-cache pool at start-up and have no allocator left to
+ * call, and latency-bound decode loops that must not call cudaMalloc because
+ * it can synchronize the device and stall work queued on other streams.
+ *   - Same arguments and results as kf_attn_fwd, for shapes that take the
+ *     split-KV decode kernel (H_q/H_kv * S_q <= 64 for D <= 128, <= 32 for
+ *     D = 256); other shapes return KF_ERR_INVALID_ARG.
+ *   - The split partials and ticket counters live in a fixed 2 MiB array inside
+ *     the library, held by every GPU that loads it until the process exits.  A
+ *     call whose plan needs more than 2 MiB returns KF_ERR_WORKSPACE (use
+ *     kf_attn_fwd with a workspace); nothing is allocated either way.
+ *   - The first call on a device looks up that array's device address (once per
+ *     device, with the device current); make that first call before any stream
+ *     capture.
+ *   - Every call shares the one array: calls whose kernels overlap on the GPU
+ *     (different streams, or different host threads on one device) race and
+ *     corrupt each other's results.  Serialize them (one stream). */
+int kf_attn_fwd_noalloc(const void* Q, const void* K, const void* V, float* O,
+                        int B, int H_q, int H_kv, int S_q, int S_kv, int D, void* stream);
+
 /* ---- device error word / bounded waits ----------------------------------
  * Kernels never spin forever: each wait gives up after a wall-clock limit
  * (default 1 s), records the failure in a per-device error word and unwinds.

@@ -24,7 +24,7 @@ EXPORTED = [
     "kf_strerror", "kf_last_cuda_error", "kf_version",
     "kf_attn_fwd", "kf_attn_fwd_lse", "kf_attn_fwd_partial", "kf_attn_combine",
     "kf_attn_workspace_bytes", "kf_attn_workspace_init", "kf_attn_plan",
-    "kf_launch_flash_attn", "kf_device_error", "kf_set_wait_timeout_ns",
+    "kf_launch_flash_attn", "kf_attn_fwd_noalloc", "kf_device_error", "kf_set_wait_timeout_ns",
     "kf_selftest_wait_timeout",
 ]
 
@@ -74,6 +74,8 @@ def lib():
     L.kf_attn_plan.restype = I
     L.kf_launch_flash_attn.argtypes = [P, P, P, P, I, I, I, I, I, P]
     L.kf_launch_flash_attn.restype = I
+    L.kf_attn_fwd_noalloc.argtypes = [P, P, P, P, I, I, I, I, I, I, P]
+    L.kf_attn_fwd_noalloc.restype = I
     L.kf_device_error.argtypes = [I, ctypes.POINTER(ctypes.c_uint)]
     L.kf_device_error.restype = I
     L.kf_set_wait_timeout_ns.argtypes = [ctypes.c_ulonglong]

@@ -385,6 +385,41 @@ int attn_core(const void* Q, const void* K, const void* V, float* O, float* Mi, 
     return launch_decode(pl, D, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, pl.n_split > 1 ? ws : nullptr, s);
 }
 
+// ------------------------------------------------------------------ fixed scratch (kf_attn_fwd_noalloc)
+// The split-KV decode needs scratch for its per-split partials and ticket
+// counters.  kf_attn_fwd_noalloc takes that scratch from this fixed array
+// instead of a caller workspace: every GPU that loads the library holds these
+// 2 MiB until the process exits.  In host code the array's name is only a
+// host-side stand-in; its device address comes from cudaGetSymbolAddress,
+// fetched once per device with that device current.
+constexpr size_t kNoAllocScratchBytes = size_t(2) << 20;
+std::atomic<void*> g_noalloc_scratch[kMaxDevices];
+
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_kf_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+int noalloc_scratch(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (dev < 0 || dev >= kMaxDevices) return KF_ERR_UNSUPPORTED_DEVICE;
+    void* ptr = g_noalloc_scratch[dev].load(std::memory_order_acquire);
+    if (!ptr) {
+        std::lock_guard<std::mutex> lk(g_dev_mu);
+        ptr = g_noalloc_scratch[dev].load(std::memory_order_acquire);
+        if (!ptr) {
+            if ((e = cudaGetSymbolAddress(&ptr, g_kf_noalloc_scratch)) != cudaSuccess) return cuda_fail(e);
+            if (!ptr) return cuda_fail(cudaErrorInvalidSymbol);
+            g_noalloc_scratch[dev].store(ptr, std::memory_order_release);
+        }
+    }
+    *out = ptr;
+    return KF_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -398,7 +433,8 @@ const char* kf_strerror(int code) {
         case KF_ERR_CUDA: return "CUDA runtime error (see kf_last_cuda_error)";
         case KF_ERR_DEVICE_TIMEOUT: return "a bounded in-kernel wait expired";
         case KF_ERR_UNSUPPORTED_DEVICE: return "current device is not an sm_100 (B200) GPU";
-        case KF_ERR_WORKSPACE: return "workspace too small";
+        case KF_ERR_WORKSPACE:
+            return "workspace too small (for kf_attn_fwd_noalloc: the call needs more than its fixed 2 MiB scratch)";
         default: return "unknown status";
     }
 }
@@ -501,6 +537,29 @@ int kf_device_error(int clear, unsigned* raw) {
 }
 
 void kf_set_wait_timeout_ns(unsigned long long ns) { g_timeout_ns.store(ns ? ns : kDefaultTimeoutNs); }
+
+int kf_attn_fwd_noalloc(const void* Q, const void* K, const void* V, float* O, int B, int H_q, int H_kv, int S_q,
+                        int S_kv, int D, void* stream) {
+    int rc = validate(Q, K, V, O, B, H_q, H_kv, S_q, S_kv, D);
+    if (rc != KF_OK) return rc;
+    if (B == 0 || S_q == 0) return KF_OK;
+    if (!use_decode(H_q / H_kv, S_q, D)) return KF_ERR_INVALID_ARG;   // short-query (decode) shapes only
+    // Same plan kf_attn_fwd makes when its workspace is large enough.
+    Plan pl;
+    if ((rc = plan_for_call(B, H_q, H_kv, S_q, S_kv, D, static_cast<size_t>(-1), &pl)) != KF_OK) return rc;
+    if (pl.ws_bytes > kNoAllocScratchBytes) return KF_ERR_WORKSPACE;
+    void* scratch = nullptr;
+    if (pl.n_split > 1) {
+        if ((rc = noalloc_scratch(&scratch)) != KF_OK) return rc;
+        // The array keeps the last call's contents: the ticket counters this call
+        // uses must start at zero, so clear them (the partials are overwritten).
+        const size_t units = static_cast<size_t>(B) * H_kv * pl.n_rg;
+        cudaError_t e = cudaMemsetAsync(scratch, 0, units * sizeof(unsigned), static_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) return cuda_fail(e);
+    }
+    return launch_decode(pl, D, Q, K, V, O, nullptr, nullptr, 0, B, H_q, H_kv, S_q, S_kv, scratch,
+                         static_cast<cudaStream_t>(stream));
+}
 
 int kf_selftest_wait_timeout(unsigned long long timeout_ns, void* stream) {
     DeviceInfo* di = nullptr;
