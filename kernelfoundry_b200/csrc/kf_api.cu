@@ -163,6 +163,9 @@ struct Plan {
     int chunk = 0;       // decode: KV rows per split
     size_t ws_bytes = 0; // workspace the plan uses
     long long ctas = 0;
+    // prefill work list: units = B * H_q * q-blocks; the last (units - plain)
+    // units (a partial last wave) are split over split_k CTAs of `per` KV tiles
+    int pf_qblk = 1, pf_units = 0, pf_plain = 0, pf_k = 1, pf_per = 0;
 };
 
 int decode_max_mt(int D) { return D <= 128 ? 2 : 1; }
@@ -199,7 +202,33 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
     if (!use_decode(G, S_q, D)) {
         pl->path = 0;
         const int rows_per_cta = (D <= 128 ? 2 : 1) * 128;
-        pl->ctas = static_cast<long long>((S_q + rows_per_cta - 1) / rows_per_cta) * H_q * B;
+        const int bc = D <= 128 ? 128 : 64;
+        pl->pf_qblk = (S_q + rows_per_cta - 1) / rows_per_cta;
+        const long long units = static_cast<long long>(pl->pf_qblk) * H_q * B;
+        if (units > (1ll << 31) - 1) return KF_ERR_INVALID_ARG;
+        pl->pf_units = static_cast<int>(units);
+        pl->pf_plain = pl->pf_units;
+        // One CTA per SM: a last wave at most half full is split along KV so it
+        // finishes in 1/k of a unit's time (partials merged by the last chunk).
+        const int cap = sm_count;
+        const int rem = static_cast<int>(units % cap);
+        const int n_kv = (S_kv + bc - 1) / bc;
+        int k = rem > 0 ? cap / rem : 1;
+        k = k > 4 ? 4 : k;
+        k = k > n_kv / 2 ? n_kv / 2 : k;
+        if (k >= 2) {
+            const int per = (n_kv + k - 1) / k;
+            const int k_eff = (n_kv + per - 1) / per;
+            const size_t part = static_cast<size_t>(rem) * k_eff * rows_per_cta * (D + 2) * sizeof(float);
+            const size_t need = kCounterBytes + ((part + 255) / 256) * 256;
+            if (k_eff >= 2 && need <= ws_bytes) {
+                pl->pf_plain = pl->pf_units - rem;
+                pl->pf_k = k_eff;
+                pl->pf_per = per;
+                pl->ws_bytes = need;
+            }
+        }
+        pl->ctas = pl->pf_plain + static_cast<long long>(pl->pf_units - pl->pf_plain) * pl->pf_k;
         return KF_OK;
     }
     pl->path = 1;
@@ -275,8 +304,8 @@ int plan_for_call(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_
 
 // ------------------------------------------------------------------ launches
 template <int D>
-int launch_prefill(const void* Q, const void* K, const void* V, float* O, float* Mi, float* Li, int unnorm, int B,
-                   int H_q, int H_kv, int S_q, int S_kv, cudaStream_t s) {
+int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, float* O, float* Mi, float* Li,
+                   int unnorm, int B, int H_q, int H_kv, int S_q, int S_kv, void* ws, cudaStream_t s) {
     using C = kf::PrefillCfg<D>;
     int bps = 0;
     int rc = kernel_setup<kf::prefill_fwd_kernel<D>>(C::SMEM_BYTES, C::THREADS, &bps);
@@ -304,9 +333,17 @@ int launch_prefill(const void* Q, const void* K, const void* V, float* O, float*
     p.timeout_ns = g_timeout_ns.load();
     p.q_box = q_box;
     p.kv_box = kv_box;
-    const int rows_per_cta = C::NQ * C::BM;
-    dim3 grid((S_q + rows_per_cta - 1) / rows_per_cta, H_q, B);
-    kf::prefill_fwd_kernel<D><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, p);
+    p.n_qblk = pl.pf_qblk;
+    p.n_units = pl.pf_units;
+    p.n_plain = pl.pf_plain;
+    p.split_k = pl.pf_k;
+    p.per = pl.pf_per;
+    const bool split = pl.pf_plain < pl.pf_units;
+    p.counters = split ? static_cast<unsigned*>(ws) : nullptr;
+    p.part = split ? reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kCounterBytes) : nullptr;
+    const long long ctas = pl.ctas;
+    if (ctas <= 0 || ctas > 0x7fffffffll) return KF_ERR_INVALID_ARG;
+    kf::prefill_fwd_kernel<D><<<static_cast<unsigned>(ctas), C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, p);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KF_OK : cuda_fail(e);
 }
@@ -376,10 +413,10 @@ int attn_core(const void* Q, const void* K, const void* V, float* O, float* Mi, 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (pl.path == 0) {
         switch (D) {
-            case 16: return launch_prefill<16>(Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, s);
-            case 64: return launch_prefill<64>(Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, s);
-            case 128: return launch_prefill<128>(Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, s);
-            default: return launch_prefill<256>(Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, s);
+            case 16: return launch_prefill<16>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s);
+            case 64: return launch_prefill<64>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s);
+            case 128: return launch_prefill<128>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s);
+            default: return launch_prefill<256>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s);
         }
     }
     return launch_decode(pl, D, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, pl.n_split > 1 ? ws : nullptr, s);

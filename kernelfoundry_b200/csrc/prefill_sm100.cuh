@@ -9,9 +9,10 @@
 //
 // One CTA owns NQ query tiles of 128 rows of one (b, h_q) and streams all of
 // that head's K/V through a ring of shared-memory slots:
-//   warp 0      TMA producer: Q tiles once, then K_0, V_0, K_1, V_1, ... into
-//               the ring (3-D tensor maps, 128-B (or 32-B) swizzle, zero fill
-//               past S_q / S_kv).
+//   warp 0      TMA producer: Q tiles once, then K_0, K_1, V_0, K_2, V_1, ...
+//               (the order the MMAs consume them, so each slot is refilled about
+//               two KV steps ahead of its use) into the ring (3-D tensor maps,
+//               128-B (or 32-B) swizzle, zero fill past S_q / S_kv).
 //   warp 1      TMEM owner + single-thread MMA issuer:
 //                 S_t  = Q_t K_j^T        (tcgen05.mma, M=128, N=BC, fp32 in TMEM)
 //                 O_t += P_t V_j          (tcgen05.mma, A = P_t from TMEM, M=128, N=D)
@@ -77,6 +78,15 @@ struct PrefillParams {
     int unnormalized;   // 1: write O_u = sum exp(s - Mi) v (partial form), Mi/Li required
     int q_box;          // rows per Q TMA box: min(BM, S_q)
     int kv_box;         // rows per K/V TMA box: min(BC, S_kv)
+    // Work list (1-D grid).  Unit u = (b, h_q, 256-row block) with the block index
+    // fastest.  Units [0, n_plain) take one CTA over all keys; each of the units
+    // [n_plain, n_units) -- the partial last wave -- is split over split_k CTAs,
+    // each taking `per` KV tiles, which write softmax partials to `part` and the
+    // last to finish (ticket in `counters`) merges them into O.
+    int n_qblk;         // 256-row blocks per (b, h_q)
+    int n_units, n_plain, split_k, per;
+    float* part;        // [n_units - n_plain][split_k][NQ*BM][D + 2]
+    unsigned* counters; // one ticket per split unit, zero between calls
     unsigned long long timeout_ns;
 };
 
@@ -118,16 +128,30 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     uint64_t* mma_done = kv_empty + NSLOT;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile int* ticket_last = abort_flag + 1;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int h = blockIdx.y;
-    const int b = blockIdx.z;
+    // Work item of this CTA: a whole unit, or one KV chunk of a split unit.
+    const int cta = blockIdx.x;
+    int unit, chunk = 0;
+    if (cta < p.n_plain) {
+        unit = cta;
+    } else {
+        unit = p.n_plain + (cta - p.n_plain) / p.split_k;
+        chunk = (cta - p.n_plain) % p.split_k;
+    }
+    const bool split = unit >= p.n_plain;
+    const int qblk = unit % p.n_qblk;
+    const int h = (unit / p.n_qblk) % p.H_q;
+    const int b = unit / (p.n_qblk * p.H_q);
     const int h_kv = h / p.G;
-    const int q_row0 = blockIdx.x * NQ * BM;
+    const int q_row0 = qblk * NQ * BM;
     const int rows_left = p.S_q - q_row0;
     const int nq_active = rows_left >= NQ * BM ? NQ : (rows_left + BM - 1) / BM;
-    const int n_kv = (p.S_kv + BC - 1) / BC;
+    const int n_kv_all = (p.S_kv + BC - 1) / BC;
+    const int kt0 = split ? chunk * p.per : 0;                                  // first KV tile
+    const int n_kv = split ? min(p.per, n_kv_all - kt0) : n_kv_all;            // KV tiles of this CTA
 
     if (threadIdx.x == 0) {
         for (int t = 0; t < NQ; ++t) {
@@ -142,6 +166,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         }
         mbar_init(mma_done, 1);
         *abort_flag = 0;
+        *ticket_last = 0;
         fence_mbar_init();
     }
     if (p.q_box < BM || p.kv_box < BC) {
@@ -187,10 +212,13 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     break;
                 }
                 mbar_arrive_expect_tx(&kv_full[slot], kv_bytes);
-                const CUtensorMap* map = (i & 1) ? &tmV : &tmK;
+                // Ring order = MMA consumption order: K_0, K_1, V_0, K_2, V_1, ..., V_{n-1}.
+                const bool is_v = i != 0 && (i == n_loads - 1 || (i & 1) == 0);
+                const int tile = i == 0 ? 0 : (i == n_loads - 1 ? n_kv - 1 : (is_v ? (i - 2) >> 1 : (i + 1) >> 1));
+                const CUtensorMap* map = is_v ? &tmV : &tmK;
                 uint8_t* dst = sKV + slot * C::KV_BYTES;
                 for (int s = 0; s < NSPAN; ++s)
-                    tma_load_3d(dst + s * BC * SWB, map, &kv_full[slot], s * SWE, (i >> 1) * BC, bh_kv);
+                    tma_load_3d(dst + s * BC * SWB, map, &kv_full[slot], s * SWE, (kt0 + tile) * BC, bh_kv);
                 issued = i + 1;
             }
             if (*abort_flag) {
@@ -213,8 +241,10 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             for (int t = 0; t < nq_active && ok; ++t) ok = mbar_wait_bounded(&q_full[t], 0, abort_flag, p.timeout_ns);
             if (!ok) atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_TMA);
             for (int j = 0; j <= n_kv && ok; ++j) {
-                const int iK = 2 * j, iV = 2 * (j - 1) + 1;
-                const int slotK = iK % NSLOT, slotV = (iV + NSLOT) % NSLOT;
+                // Ring positions (see the producer): K_j and V_{j-1}.
+                const int iK = j == 0 ? 0 : 2 * j - 1;
+                const int iV = j == 0 ? 0 : (j - 1 == n_kv - 1 ? 2 * n_kv - 1 : 2 * j);
+                const int slotK = iK % NSLOT, slotV = iV % NSLOT;
                 if (j < n_kv && !mbar_wait_bounded(&kv_full[slotK], (iK / NSLOT) & 1, abort_flag, p.timeout_ns)) {
                     atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_TMA); ok = false; break;
                 }
@@ -239,6 +269,8 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                             umma_ts(tO, tS + kk * 8, bdesc, idesc_pv, (j > 1 || kk > 0) ? 1u : 0u);
                         }
                         if (j == n_kv) umma_commit(&o_full[t]);
+                        // V_{j-1} is free once the last tile's PV has read it (before QK_B(j)).
+                        if (t == nq_active - 1) umma_commit(&kv_empty[slotV]);
                     }
                     if (j < n_kv) {
                         const uint32_t qbase = sQa + t * C::Q_BYTES;
@@ -255,7 +287,6 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     }
                 }
                 if (!ok) break;
-                if (j > 0) umma_commit(&kv_empty[slotV]);
                 if (j < n_kv) umma_commit(&kv_empty[slotK]);
             }
             // Every MMA issued above must complete before TMEM is released.
@@ -287,7 +318,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 for (int cc = 0; cc < BC / 32; ++cc)
                     tmem_ld32(tS + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[cc * 32]));
                 tmem_wait_ld();
-                const int kv_valid = p.S_kv - j * BC;
+                const int kv_valid = p.S_kv - (kt0 + j) * BC;
                 if (kv_valid < BC) {
 #pragma unroll
                     for (int cc = 0; cc < BC; ++cc)
@@ -366,14 +397,88 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 ok = __all_sync(0xffffffffu, ok);
                 if (!ok) atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_MMA);
             }
-            if (ok) {
+            const int qrow = q_row0 + t * BM + row;
+            const bool store = qrow < p.S_q;
+            float* orow = p.O + ((static_cast<size_t>(b) * p.H_q + h) * p.S_q + (store ? qrow : 0)) * D;
+            const size_t mi = (static_cast<size_t>(b) * p.H_q + h) * p.S_q + (store ? qrow : 0);
+            if (split) {
+                // KV chunk of a split unit: write this row's partial (O_u, m, l)
+                // relative to its own max; the last chunk to finish merges them.
+                // Layout: O_u [split unit][chunk][ROWS][D], then (m, l) [..][ROWS][2].
+                const int su = unit - p.n_plain;
+                constexpr int ROWS = NQ * BM;
+                const size_t n_slots = static_cast<size_t>(p.n_units - p.n_plain) * p.split_k * ROWS;
+                const size_t slot0 = static_cast<size_t>(su) * p.split_k * ROWS + t * BM + row;   // chunk 0
+                const size_t my_slot = slot0 + static_cast<size_t>(chunk) * ROWS;
+                float* part_ml = p.part + n_slots * D;
+                if (ok) {
+                    tc_fence_after();
+                    const float f = ex2_approx((m_ref - m_true) * c);
+                    float* prow = p.part + my_slot * D;
+#pragma unroll
+                    for (int dc = 0; dc < D / OCH; ++dc) {
+                        uint32_t o[OCH];
+                        tmem_ld_chunk<OCH>(tO + dc * OCH, o);
+                        tmem_wait_ld();
+                        if (store) {
+#pragma unroll
+                            for (int k = 0; k < OCH; k += 4)
+                                *reinterpret_cast<float4*>(prow + dc * OCH + k) =
+                                    make_float4(__uint_as_float(o[k]) * f, __uint_as_float(o[k + 1]) * f,
+                                                __uint_as_float(o[k + 2]) * f, __uint_as_float(o[k + 3]) * f);
+                        }
+                    }
+                    if (store) *reinterpret_cast<float2*>(part_ml + my_slot * 2) = make_float2(m_true, l * f);
+                }
+                __threadfence();
+                named_bar_sync(1, 128 * nq_active);     // every active softmax thread, ok or not
+                if (threadIdx.x == 128 && !*abort_flag) {
+                    const unsigned tk = atomicAdd(&p.counters[su], 1u);
+                    *ticket_last = (tk == static_cast<unsigned>(p.split_k - 1)) ? 1 : 0;
+                }
+                named_bar_sync(1, 128 * nq_active);
+                if (*ticket_last) {
+                    __threadfence();
+                    if (store) {
+                        // split_k <= 4 (host plan): all loads of a row are independent.
+                        float2 ml[4];
+#pragma unroll
+                        for (int c2 = 0; c2 < 4; ++c2)
+                            ml[c2] = c2 < p.split_k ? __ldcg(reinterpret_cast<const float2*>(part_ml) + slot0 + c2 * ROWS)
+                                                    : make_float2(-CUDART_INF_F, 0.f);
+                        const float M = fmaxf(fmaxf(ml[0].x, ml[1].x), fmaxf(ml[2].x, ml[3].x));
+                        float w[4], L = 0.f;
+#pragma unroll
+                        for (int c2 = 0; c2 < 4; ++c2) {
+                            w[c2] = c2 < p.split_k ? ex2_approx((ml[c2].x - M) * c) : 0.f;
+                            L += w[c2] * ml[c2].y;
+                        }
+                        const float osc = p.unnormalized ? 1.0f : 1.0f / L;
+#pragma unroll
+                        for (int c2 = 0; c2 < 4; ++c2) w[c2] *= osc;
+#pragma unroll 4
+                        for (int d = 0; d < D; d += 4) {
+                            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                            for (int c2 = 0; c2 < 4; ++c2) {
+                                if (c2 < p.split_k) {
+                                    const float4 v = __ldcg(reinterpret_cast<const float4*>(
+                                        p.part + (slot0 + static_cast<size_t>(c2) * ROWS) * D + d));
+                                    acc.x += w[c2] * v.x; acc.y += w[c2] * v.y; acc.z += w[c2] * v.z; acc.w += w[c2] * v.w;
+                                }
+                            }
+                            *reinterpret_cast<float4*>(orow + d) = acc;
+                        }
+                        if (p.Mi) p.Mi[mi] = M * p.scale;
+                        if (p.Li) p.Li[mi] = L;
+                    }
+                    if (threadIdx.x == 128) p.counters[su] = 0u;
+                }
+            } else if (ok) {
                 tc_fence_after();
                 const float f = ex2_approx((m_ref - m_true) * c);   // rebase to the true max
                 const float l_true = l * f;
                 const float osc = p.unnormalized ? f : 1.0f / l;
-                const int qrow = q_row0 + t * BM + row;
-                const bool store = qrow < p.S_q;
-                float* orow = p.O + ((static_cast<size_t>(b) * p.H_q + h) * p.S_q + (store ? qrow : 0)) * D;
 #pragma unroll
                 for (int dc = 0; dc < D / OCH; ++dc) {
                     uint32_t o[OCH];
@@ -389,7 +494,6 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     }
                 }
                 if (store) {
-                    const size_t mi = (static_cast<size_t>(b) * p.H_q + h) * p.S_q + qrow;
                     if (p.Mi) p.Mi[mi] = m_true * p.scale;
                     if (p.Li) p.Li[mi] = l_true;
                 }

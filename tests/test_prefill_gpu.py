@@ -100,6 +100,33 @@ def test_ragged_shapes(cuda, shape):
     assert np.abs(Li / rLi - 1).max() < 1e-3
 
 
+@pytest.mark.parametrize("shape", [(1, 32, 8, 4096, 4096, 128), (3, 8, 2, 700, 1500, 64), (1, 4, 1, 129, 4097, 256)],
+                         ids=lambda s: "B{}_Hq{}_Hkv{}_Sq{}_Skv{}_D{}".format(*s))
+def test_tail_split_matches_unsplit(cuda, shape):
+    """A partial last wave split along KV (needs a workspace) gives the unsplit result."""
+    import torch
+
+    from kernelfoundry_b200 import flash_attn_fwd, plan
+    from kernelfoundry_b200.attention import new_workspace, workspace_bytes
+
+    need = workspace_bytes(*shape)
+    assert need > 0, "expected a split plan for this shape"
+    assert plan(*shape)["ctas"] > plan(*shape, workspace_bytes=0)["ctas"]
+    Q, K, V = normal_qkv(*shape, seed=5 * sum(shape))
+    q, k, v = (to_dev(x, cuda) for x in (Q, K, V))
+    ws = new_workspace(need, cuda)
+    split_o, split_mi, split_li = (x.cpu().numpy() for x in flash_attn_fwd(q, k, v, workspace=ws, return_lse=True))
+    none = torch.empty(0, dtype=torch.uint8, device=cuda)
+    plain_o = flash_attn_fwd(q, k, v, workspace=none).cpu().numpy()
+    ma, rl = error_stats(split_o, plain_o)
+    assert ma <= 2e-3 and rl <= 1e-3, (ma, rl)
+    O, rMi, rLi = oracle64(Q, K, V)
+    assert_close(split_o, O, "split")
+    assert np.abs(split_mi - rMi).max() < 1e-3
+    assert np.abs(split_li / rLi - 1).max() < 1e-3
+    assert int(ws[:65536].view(torch.int32).abs().sum()) == 0     # tickets reset
+
+
 def test_partial_form_prefill(cuda):
     from kernelfoundry_b200 import flash_attn_partial
 
