@@ -506,6 +506,47 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------- single-case mode (profiling)
+CASES = {
+    # name: (B, H_q, H_kv, S_q, S_kv, D)
+    "prefill_C2": (1, H_Q, H_KV, S, S, D),
+    "prefill_C2_B8": (8, H_Q, H_KV, S, S, D),
+    "prefill_C1": (1, H_Q, H_KV, 512, 512, D),
+    "mqa_C4": (4, 32, 1, 2048, 2048, 64),
+    "decode_B1": (1, H_Q, H_KV, 1, 4096, D),
+    "decode_B16": (16, H_Q, H_KV, 1, 4096, D),
+    "decode_B64": (64, H_Q, H_KV, 1, 4096, D),
+    "long_decode_C5": (1, H_Q, H_KV, 1, 131072, D),
+}
+
+
+def run_case(args):
+    """One configuration, `--warmup` then `--steps` back-to-back launches on one input set.
+
+    Small and deterministic so that a profiler can capture one launch (-s warmup -c 1);
+    prints one JSON line with the mean device time of the timed launches."""
+    import torch
+
+    from kernelfoundry_b200 import flash_attn_fwd, plan
+
+    B, Hq, Hkv, Sq, Skv, Dh = CASES[args.case]
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(77)
+    q = rand_f16((B, Hq, Sq, Dh), gen, dev)
+    k = rand_f16((B, Hkv, Skv, Dh), gen, dev)
+    v = rand_f16((B, Hkv, Skv, Dh), gen, dev)
+    o = torch.empty((B, Hq, Sq, Dh), dtype=torch.float32, device=dev)
+    ms = time_loop(lambda i: flash_attn_fwd(q, k, v, out=o), args.steps, args.warmup, torch.cuda.current_stream(dev))
+    line = {"case": args.case, "shape": [B, Hq, Hkv, Sq, Skv, Dh], "ms": round(ms, 5), "plan": plan(B, Hq, Hkv, Sq, Skv, Dh)}
+    if Sq > 1:
+        line["TFLOP/s"] = round(prefill_flops(B, Hq, Sq, Skv, Dh) / (ms * 1e-3) / 1e12, 1)
+    else:
+        line["GB/s"] = round(decode_bytes(B, Hq, Hkv, Skv, Dh) / (ms * 1e-3) / 1e9, 1)
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -514,10 +555,13 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true", help="headline only (skip decode/MQA/long-decode lines)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--case", choices=sorted(CASES), help="time one configuration only (for profiler captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
-    if args.impl == "reference":
+    if args.case:
+        run_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

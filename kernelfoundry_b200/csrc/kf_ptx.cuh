@@ -64,8 +64,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Non-blocking test of phase `parity` (acquire on success).  Tests whose results
+// are combined after all of them were issued overlap their round trips.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait on phase `parity`.  Returns false (and raises *abort) when the
 // wall-clock limit passes or another role of the CTA has already aborted.
+// A wait whose result the thread branches on costs it one barrier round trip
+// even when the phase has already completed; issue loops keep waits few.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   volatile int* abort_flag, uint64_t timeout_ns) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -272,6 +288,18 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t smem_addr, uint32_t lbo_b
     d |= 1ull << 46;  // descriptor version for tcgen05
     d |= static_cast<uint64_t>(layout & 7u) << 61;
     return d;
+}
+
+// The same descriptor split in two 32-bit words.  The high word (SBO, version,
+// layout) is fixed per operand kind; the low word is (start >> 4) | (LBO >> 4) << 16.
+// Shared-memory offsets stay below 2^18, so the 14-bit start field never carries
+// and stepping an operand by `bytes` is a plain add of bytes >> 4 to the low word.
+__host__ __device__ constexpr uint32_t umma_desc_hi(uint32_t sbo_bytes, uint32_t layout) {
+    return ((sbo_bytes >> 4) & 0x3FFFu) | (1u << 14) | ((layout & 7u) << 29);
+}
+__host__ __device__ constexpr uint32_t umma_desc_lbo(uint32_t lbo_bytes) { return ((lbo_bytes >> 4) & 0x3FFFu) << 16; }
+__device__ __forceinline__ uint64_t umma_desc_join(uint32_t lo, uint32_t hi) {
+    return (static_cast<uint64_t>(hi) << 32) | lo;
 }
 
 // Instruction descriptor, kind::f16 with fp16 A/B and fp32 accumulate.

@@ -113,6 +113,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     constexpr int BM = C::BM, BC = C::BC, NQ = C::NQ, SWB = C::SWB, SWE = C::SWE, NSPAN = C::NSPAN;
     constexpr int NSLOT = C::NSLOT;
     constexpr int OCH = D < 32 ? D : 32;   // TMEM columns per O chunk
+    constexpr int RCH = D < 16 ? D : 16;   // TMEM columns per O chunk while S is held in registers
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -122,7 +123,8 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     uint64_t* q_full = bars;
     uint64_t* s_full = q_full + NQ;
     uint64_t* p_full = s_full + NQ;
-    uint64_t* o_full = p_full + NQ;
+    uint64_t* p_half = p_full + NQ;
+    uint64_t* o_full = p_half + NQ;
     uint64_t* kv_full = o_full + NQ;
     uint64_t* kv_empty = kv_full + NSLOT;
     uint64_t* mma_done = kv_empty + NSLOT;
@@ -158,6 +160,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             mbar_init(&q_full[t], 1);
             mbar_init(&s_full[t], 1);
             mbar_init(&p_full[t], 128);
+            mbar_init(&p_half[t], 128);
             mbar_init(&o_full[t], 1);
         }
         for (int s = 0; s < NSLOT; ++s) {
@@ -235,59 +238,91 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         if (lane == 0) {
             constexpr uint32_t idesc_qk = umma_idesc_f16_f32(BM, BC, false, false);
             constexpr uint32_t idesc_pv = umma_idesc_f16_f32(BM, D, false, true);
-            constexpr uint32_t lay_qk = umma_layout_code(SWB);
-            const uint32_t sQa = smem_u32(sQ), sKVa = smem_u32(sKV);
+            // Descriptors as (low, high) words: the high word is a constant and every
+            // operand step is one add on the low word (the issue loop stays short).
+            constexpr uint32_t DESC_HI = umma_desc_hi(8 * SWB, umma_layout_code(SWB));
+            const uint32_t q_lo = (smem_u32(sQ) >> 4) + umma_desc_lbo(16);
+            const uint32_t kv_lo = smem_u32(sKV) >> 4;
             bool ok = true;
             for (int t = 0; t < nq_active && ok; ++t) ok = mbar_wait_bounded(&q_full[t], 0, abort_flag, p.timeout_ns);
             if (!ok) atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_TMA);
+            // The tensor core queues only a few MMAs, so every barrier round trip this
+            // thread waits on (~120 cycles even for a completed phase) idles it.  The
+            // loop keeps them few: ring slot/phase are counters, K and V are tested
+            // together, and a completed p_full makes the p_half wait unnecessary.
+            int slotK = 0, parK = 0;        // ring position of K_j
+            int slotV = 0, parV = 0;        // ring position of V_{j-1}
             for (int j = 0; j <= n_kv && ok; ++j) {
-                // Ring positions (see the producer): K_j and V_{j-1}.
-                const int iK = j == 0 ? 0 : 2 * j - 1;
-                const int iV = j == 0 ? 0 : (j - 1 == n_kv - 1 ? 2 * n_kv - 1 : 2 * j);
-                const int slotK = iK % NSLOT, slotV = iV % NSLOT;
-                if (j < n_kv && !mbar_wait_bounded(&kv_full[slotK], (iK / NSLOT) & 1, abort_flag, p.timeout_ns)) {
+                // Ring positions (see the producer): K_j at 2j-1 (K_0 at 0), V_{j-1} at 2j,
+                // except the last V, which follows the last K at 2 n_kv - 1.
+                if (j == 1) { slotK = 1 % NSLOT; parK = 1 / NSLOT; slotV = 2 % NSLOT; parV = 2 / NSLOT; }
+                if (j == n_kv && j > 0) { slotV = slotK; parV = parK; }   // position 2 n_kv - 1 = last K + 0
+                const bool k_ready = j == n_kv || mbar_test_wait(&kv_full[slotK], parK & 1);
+                const bool v_ready = j == 0 || mbar_test_wait(&kv_full[slotV], parV & 1);
+                if (!k_ready && !mbar_wait_bounded(&kv_full[slotK], parK & 1, abort_flag, p.timeout_ns)) {
                     atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_TMA); ok = false; break;
                 }
-                if (j > 0 && !mbar_wait_bounded(&kv_full[slotV], (iV / NSLOT) & 1, abort_flag, p.timeout_ns)) {
+                if (!v_ready && !mbar_wait_bounded(&kv_full[slotV], parV & 1, abort_flag, p.timeout_ns)) {
                     atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_TMA); ok = false; break;
                 }
                 tc_fence_after();
-                for (int t = 0; t < nq_active; ++t) {
+                const uint32_t k_lo = kv_lo + slotK * (C::KV_BYTES >> 4) + umma_desc_lbo(16);
+                const uint32_t v_lo = kv_lo + slotV * (C::KV_BYTES >> 4) + umma_desc_lbo(BC * SWB);
+                const uint32_t ppar = (j - 1) & 1;
+#pragma unroll
+                for (int t = 0; t < NQ; ++t) {
+                    if (t >= nq_active) break;
                     const uint32_t tS = tmem + t * BC;
                     const uint32_t tO = tmem + NQ * BC + t * D;
                     if (j > 0) {
-                        if (!mbar_wait_bounded(&p_full[t], (j - 1) & 1, abort_flag, p.timeout_ns)) {
-                            atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_SOFTMAX); ok = false; break;
-                        }
-                        tc_fence_after();
-                        const uint32_t vbase = sKVa + slotV * C::KV_BYTES;
+                        // P_t arrives in two halves (keys [0, BC/2) then [BC/2, BC)): the
+                        // first half of the PV MMAs runs while the softmax finishes the rest.
+                        // Every softmax thread arrives on p_half before p_full, so a
+                        // completed p_full implies p_half.
+                        const bool full_ready = mbar_test_wait(&p_full[t], ppar);
 #pragma unroll
-                        for (int kk = 0; kk < BC / 16; ++kk) {
-                            // A = P_t in TMEM (fp16 pairs over the first BC/2 columns of S_t);
-                            // B = V: MN-major spans of SWE columns, 8-row groups of SWB bytes.
-                            const uint64_t bdesc = umma_desc(vbase + kk * 16 * SWB, BC * SWB, 8 * SWB, lay_qk);
-                            umma_ts(tO, tS + kk * 8, bdesc, idesc_pv, (j > 1 || kk > 0) ? 1u : 0u);
+                        for (int hf = 0; hf < 2; ++hf) {
+                            if (!full_ready) {
+                                if (!mbar_wait_bounded(hf == 0 ? &p_half[t] : &p_full[t], ppar, abort_flag,
+                                                       p.timeout_ns)) {
+                                    atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_SOFTMAX); ok = false; break;
+                                }
+                            }
+                            if (hf == 0 || !full_ready) tc_fence_after();
+#pragma unroll
+                            for (int kk = hf * BC / 32; kk < (hf + 1) * BC / 32; ++kk) {
+                                // A = P_t in TMEM (fp16 pairs over the first BC/2 columns of S_t);
+                                // B = V: MN-major spans of SWE columns, 8-row groups of SWB bytes.
+                                umma_ts(tO, tS + kk * 8, umma_desc_join(v_lo + ((kk * 16 * SWB) >> 4), DESC_HI),
+                                        idesc_pv, (j > 1 || kk > 0) ? 1u : 0u);
+                            }
                         }
+                        if (!ok) break;
                         if (j == n_kv) umma_commit(&o_full[t]);
                         // V_{j-1} is free once the last tile's PV has read it (before QK_B(j)).
                         if (t == nq_active - 1) umma_commit(&kv_empty[slotV]);
                     }
                     if (j < n_kv) {
-                        const uint32_t qbase = sQa + t * C::Q_BYTES;
-                        const uint32_t kbase = sKVa + slotK * C::KV_BYTES;
+                        const uint32_t a_lo = q_lo + t * (C::Q_BYTES >> 4);
 #pragma unroll
                         for (int kk = 0; kk < D / 16; ++kk) {
+                            // K-major, 128-B (or 32-B) swizzle: span s of SWE columns, +32 B per 16 columns.
                             const int span = (kk * 16) / SWE;
                             const int off = ((kk * 16) % SWE) * 2;
-                            const uint64_t adesc = umma_desc(qbase + span * BM * SWB + off, 16, 8 * SWB, lay_qk);
-                            const uint64_t bdesc = umma_desc(kbase + span * BC * SWB + off, 16, 8 * SWB, lay_qk);
-                            umma_ss(tS, adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
+                            umma_ss(tS, umma_desc_join(a_lo + ((span * BM * SWB + off) >> 4), DESC_HI),
+                                    umma_desc_join(k_lo + ((span * BC * SWB + off) >> 4), DESC_HI), idesc_qk,
+                                    kk > 0 ? 1u : 0u);
                         }
                         umma_commit(&s_full[t]);
                     }
                 }
                 if (!ok) break;
                 if (j < n_kv) umma_commit(&kv_empty[slotK]);
+                // Advance both ring positions by two (K_{j+1} at 2j+1, V_j at 2j+2).
+                if (j > 0) {
+                    slotK += 2; if (slotK >= NSLOT) { slotK -= NSLOT; ++parK; }
+                    slotV += 2; if (slotV >= NSLOT) { slotV -= NSLOT; ++parV; }
+                }
             }
             // Every MMA issued above must complete before TMEM is released.
             umma_commit(mma_done);
@@ -353,44 +388,48 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                         l *= f;
                     }
                 }
-                // P = 2^(s*c - m_ref*c): paired FMA, MUFU ex2, paired row-sum adds;
-                // packed to fp16 pairs and written over the first BC/2 TMEM
-                // columns of S_t (this thread's row), the A operand of the PV MMA.
-                const float2 c2 = make_float2(c, c);
-                const float2 neg2 = make_float2(-m_ref * c, -m_ref * c);
-                float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
-                uint32_t pk[BC / 2];
-#pragma unroll
-                for (int i = 0; i < BC; i += 4) {
-                    const float2 x0 = ffma2(make_float2(KF_S(i), KF_S(i + 1)), c2, neg2);
-                    const float2 x1 = ffma2(make_float2(KF_S(i + 2), KF_S(i + 3)), c2, neg2);
-                    const float2 e0 = make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
-                    const float2 e1 = make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
-                    acc0 = fadd2(acc0, e0);
-                    acc1 = fadd2(acc1, e1);
-                    pk[i / 2] = pack_half2(e0.x, e0.y);
-                    pk[i / 2 + 1] = pack_half2(e1.x, e1.y);
-                }
-#undef KF_S
-#pragma unroll
-                for (int cc = 0; cc < BC / 64; ++cc)
-                    tmem_st32(tS + cc * 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[cc * 32]));
-                l += (acc0.x + acc0.y) + (acc1.x + acc1.y);
                 if (rescale) {
                     // O_t is stable here: PV_t(j-1) completed before S_t(j) was committed.
 #pragma unroll
-                    for (int dc = 0; dc < D / OCH; ++dc) {
-                        uint32_t o[OCH];
-                        tmem_ld_chunk<OCH>(tO + dc * OCH, o);
+                    for (int dc = 0; dc < D / RCH; ++dc) {
+                        uint32_t o[RCH];
+                        tmem_ld_chunk<RCH>(tO + dc * RCH, o);
                         tmem_wait_ld();
 #pragma unroll
-                        for (int k = 0; k < OCH; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * f);
-                        tmem_st_chunk<OCH>(tO + dc * OCH, o);
+                        for (int k = 0; k < RCH; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * f);
+                        tmem_st_chunk<RCH>(tO + dc * RCH, o);
                     }
                 }
-                tmem_wait_st();          // P (and any rescaled O) written before the MMA reads them
-                tc_fence_before();
-                mbar_arrive(&p_full[t]);
+                // P = 2^(s*c - m_ref*c): paired FMA, MUFU ex2, paired row-sum adds;
+                // packed to fp16 pairs in place (pair i/2 overwrites scores already
+                // read) and written over the first BC/2 TMEM columns of S_t (this
+                // thread's row), the A operand of the PV MMA.  Each half of the keys
+                // is published on its own barrier (p_half, then p_full).
+                const float2 c2 = make_float2(c, c);
+                const float2 neg2 = make_float2(-m_ref * c, -m_ref * c);
+                float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+                constexpr int HALF = BC / 2;
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+#pragma unroll
+                    for (int i = hf * HALF; i < (hf + 1) * HALF; i += 4) {
+                        const float2 x0 = ffma2(make_float2(KF_S(i), KF_S(i + 1)), c2, neg2);
+                        const float2 x1 = ffma2(make_float2(KF_S(i + 2), KF_S(i + 3)), c2, neg2);
+                        const float2 e0 = make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
+                        const float2 e1 = make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
+                        acc0 = fadd2(acc0, e0);
+                        acc1 = fadd2(acc1, e1);
+                        sr[i / 2] = pack_half2(e0.x, e0.y);
+                        sr[i / 2 + 1] = pack_half2(e1.x, e1.y);
+                    }
+                    tmem_st_chunk<HALF / 2>(tS + hf * (HALF / 2),
+                                            *reinterpret_cast<const uint32_t(*)[HALF / 2]>(&sr[hf * (HALF / 2)]));
+                    tmem_wait_st();      // this half of P (and any rescaled O) written before the MMA reads it
+                    tc_fence_before();
+                    mbar_arrive(hf == 0 ? &p_half[t] : &p_full[t]);
+                }
+#undef KF_S
+                l += (acc0.x + acc0.y) + (acc1.x + acc1.y);
             }
             if (ok) {
                 ok = mbar_wait_bounded(&o_full[t], 0, abort_flag, p.timeout_ns);
