@@ -138,6 +138,22 @@ int make_map(CUtensorMap* map, const void* base, int D, int S, long long BH, int
     return KF_OK;
 }
 
+// 3-D map over a [BH][S][D] fp32 tensor (the output); boxes of 32 x box_rows x 1,
+// 128-B swizzle (D a multiple of 32).
+int make_map_f32(CUtensorMap* map, void* base, int D, int S, long long BH, int box_rows) {
+    auto enc = encode_fn();
+    if (!enc) return cuda_fail(cudaErrorNotSupported);
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(BH)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 4, static_cast<cuuint64_t>(S) * D * 4};
+    cuuint32_t box[3] = {32, static_cast<cuuint32_t>(box_rows), 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return cuda_fail(cudaErrorInvalidValue);
+    return KF_OK;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int validate(const void* Q, const void* K, const void* V, const float* O, int B, int H_q, int H_kv, int S_q,
@@ -314,10 +330,15 @@ int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, 
     // kernel keeps the remaining tile rows zero.
     const int q_box = S_q < C::BM ? S_q : C::BM;
     const int kv_box = S_kv < C::BC ? S_kv : C::BC;
-    CUtensorMap mq, mk, mv;
+    CUtensorMap mq, mk, mv, mo;
     if ((rc = make_map(&mq, Q, D, S_q, static_cast<long long>(B) * H_q, q_box, C::SWB)) != KF_OK) return rc;
     if ((rc = make_map(&mk, K, D, S_kv, static_cast<long long>(B) * H_kv, kv_box, C::SWB)) != KF_OK) return rc;
     if ((rc = make_map(&mv, V, D, S_kv, static_cast<long long>(B) * H_kv, kv_box, C::SWB)) != KF_OK) return rc;
+    if (C::TMA_STORE) {
+        if ((rc = make_map_f32(&mo, O, D, S_q, static_cast<long long>(B) * H_q, q_box)) != KF_OK) return rc;
+    } else {
+        std::memset(&mo, 0, sizeof(mo));
+    }
     kf::PrefillParams p;
     p.O = O;
     p.Mi = Mi;
@@ -343,7 +364,7 @@ int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, 
     p.part = split ? reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kCounterBytes) : nullptr;
     const long long ctas = pl.ctas;
     if (ctas <= 0 || ctas > 0x7fffffffll) return KF_ERR_INVALID_ARG;
-    kf::prefill_fwd_kernel<D><<<static_cast<unsigned>(ctas), C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, p);
+    kf::prefill_fwd_kernel<D><<<static_cast<unsigned>(ctas), C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, mo, p);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KF_OK : cuda_fail(e);
 }

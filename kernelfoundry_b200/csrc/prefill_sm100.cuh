@@ -9,10 +9,9 @@
 //
 // One CTA owns NQ query tiles of 128 rows of one (b, h_q) and streams all of
 // that head's K/V through a ring of shared-memory slots:
-//   warp 0      TMA producer: Q tiles once, then K_0, K_1, V_0, K_2, V_1, ...
-//               (the order the MMAs consume them, so each slot is refilled about
-//               two KV steps ahead of its use) into the ring (3-D tensor maps,
-//               128-B (or 32-B) swizzle, zero fill past S_q / S_kv).
+//   warp 0      TMA producer: Q tiles once, then K_0, V_0, K_1, V_1, ... into
+//               the ring (3-D tensor maps, 128-B (or 32-B) swizzle, zero fill past
+//               S_q / S_kv); every load is issued 1.5-2 KV steps before its use.
 //   warp 1      TMEM owner + single-thread MMA issuer:
 //                 S_t  = Q_t K_j^T        (tcgen05.mma, M=128, N=BC, fp32 in TMEM)
 //                 O_t += P_t V_j          (tcgen05.mma, A = P_t from TMEM, M=128, N=D)
@@ -56,8 +55,24 @@ struct PrefillCfg {
     static constexpr int TMEM_COLS = TMEM_USED <= 32 ? 32 : TMEM_USED <= 64 ? 64 : TMEM_USED <= 128 ? 128
                                    : TMEM_USED <= 256 ? 256 : 512;
     static constexpr int THREADS = 128 * (1 + NQ);
+    // Epilogue: O tile staged in shared memory (128-B swizzled fp32 spans of 32
+    // columns) and written by TMA stores; D = 16 keeps per-thread row stores.
+    static constexpr bool TMA_STORE = D % 32 == 0;
+    static_assert(!TMA_STORE || BM * D * 4 <= (NQ == 2 ? NQ * Q_BYTES : NSLOT * KV_BYTES), "O staging area");
     // Registers after rebalancing (NQ == 2: 384 threads launch with 168 each):
     // control warpgroup 128 x 112 + softmax warpgroups 256 x 192 = 63488 <= 64512.
+    // Scores per 16 whose exp2 runs on the FMA pipe (exp2_poly2) instead of MUFU;
+    // a multiple of 4.  MUFU ex2 issues at a quarter of the FMA rate, so moving a
+    // few exps to the FMA pipe shortens the softmax when MUFU bounds it.
+#ifndef KF_PREFILL_EMU16
+#define KF_PREFILL_EMU16 0
+#endif
+    static constexpr int EMU16 = KF_PREFILL_EMU16;
+    static_assert(EMU16 % 4 == 0 && EMU16 <= 16, "EMU16 must be a multiple of 4");
+#ifndef KF_PREFILL_L2AHEAD
+#define KF_PREFILL_L2AHEAD 4
+#endif
+    static constexpr int L2AHEAD = KF_PREFILL_L2AHEAD;   // KV tiles of L2 prefetch lookahead
     static constexpr bool REBALANCE = NQ == 2;
     static constexpr int REG_CTRL = 112;
     static constexpr int REG_SOFTMAX = 192;
@@ -108,7 +123,8 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, 
 template <int D>
 __global__ void __launch_bounds__(PrefillCfg<D>::THREADS, 1)
 prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmV, const PrefillParams p) {
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                   const PrefillParams p) {
     using C = PrefillCfg<D>;
     constexpr int BM = C::BM, BC = C::BC, NQ = C::NQ, SWB = C::SWB, SWE = C::SWE, NSPAN = C::NSPAN;
     constexpr int NSLOT = C::NSLOT;
@@ -215,13 +231,22 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     break;
                 }
                 mbar_arrive_expect_tx(&kv_full[slot], kv_bytes);
-                // Ring order = MMA consumption order: K_0, K_1, V_0, K_2, V_1, ..., V_{n-1}.
-                const bool is_v = i != 0 && (i == n_loads - 1 || (i & 1) == 0);
-                const int tile = i == 0 ? 0 : (i == n_loads - 1 ? n_kv - 1 : (is_v ? (i - 2) >> 1 : (i + 1) >> 1));
+                // Ring order K_0, V_0, K_1, V_1, ...: a K refill takes the slot of a V freed
+                // mid-step and a V refill that of a K freed at the end of a step, so each
+                // load is issued 1.5 to 2 KV steps before its MMA needs it (TMA loads
+                // from L2 take about one step to land under full load).
+                const bool is_v = (i & 1) != 0;
+                const int tile = i >> 1;
                 const CUtensorMap* map = is_v ? &tmV : &tmK;
                 uint8_t* dst = sKV + slot * C::KV_BYTES;
                 for (int s = 0; s < NSPAN; ++s)
                     tma_load_3d(dst + s * BC * SWB, map, &kv_full[slot], s * SWE, (kt0 + tile) * BC, bh_kv);
+                // Warm L2 with the same operand KF_PREFILL_L2AHEAD tiles ahead: the CTAs of
+                // one KV head stream it in near lockstep, so without this every tile is
+                // a first touch that waits on HBM.
+                if (C::L2AHEAD > 0 && tile + C::L2AHEAD < n_kv)
+                    for (int s = 0; s < NSPAN; ++s)
+                        tma_prefetch_l2_3d(map, s * SWE, (kt0 + tile + C::L2AHEAD) * BC, bh_kv);
                 issued = i + 1;
             }
             if (*abort_flag) {
@@ -250,13 +275,11 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             // thread waits on (~120 cycles even for a completed phase) idles it.  The
             // loop keeps them few: ring slot/phase are counters, K and V are tested
             // together, and a completed p_full makes the p_half wait unnecessary.
-            int slotK = 0, parK = 0;        // ring position of K_j
-            int slotV = 0, parV = 0;        // ring position of V_{j-1}
+            int slotK = 0, parK = 0;        // ring position 2j of K_j
             for (int j = 0; j <= n_kv && ok; ++j) {
-                // Ring positions (see the producer): K_j at 2j-1 (K_0 at 0), V_{j-1} at 2j,
-                // except the last V, which follows the last K at 2 n_kv - 1.
-                if (j == 1) { slotK = 1 % NSLOT; parK = 1 / NSLOT; slotV = 2 % NSLOT; parV = 2 / NSLOT; }
-                if (j == n_kv && j > 0) { slotV = slotK; parV = parK; }   // position 2 n_kv - 1 = last K + 0
+                // V_{j-1} sits at ring position 2j - 1, just before K_j.
+                int slotV = slotK - 1, parV = parK;
+                if (slotV < 0) { slotV += NSLOT; --parV; }
                 const bool k_ready = j == n_kv || mbar_test_wait(&kv_full[slotK], parK & 1);
                 const bool v_ready = j == 0 || mbar_test_wait(&kv_full[slotV], parV & 1);
                 if (!k_ready && !mbar_wait_bounded(&kv_full[slotK], parK & 1, abort_flag, p.timeout_ns)) {
@@ -318,11 +341,8 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 }
                 if (!ok) break;
                 if (j < n_kv) umma_commit(&kv_empty[slotK]);
-                // Advance both ring positions by two (K_{j+1} at 2j+1, V_j at 2j+2).
-                if (j > 0) {
-                    slotK += 2; if (slotK >= NSLOT) { slotK -= NSLOT; ++parK; }
-                    slotV += 2; if (slotV >= NSLOT) { slotV -= NSLOT; ++parV; }
-                }
+                slotK += 2;                      // K_{j+1} at 2j + 2
+                if (slotK >= NSLOT) { slotK -= NSLOT; ++parK; }
             }
             // Every MMA issued above must complete before TMEM is released.
             umma_commit(mma_done);
@@ -415,8 +435,9 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     for (int i = hf * HALF; i < (hf + 1) * HALF; i += 4) {
                         const float2 x0 = ffma2(make_float2(KF_S(i), KF_S(i + 1)), c2, neg2);
                         const float2 x1 = ffma2(make_float2(KF_S(i + 2), KF_S(i + 3)), c2, neg2);
-                        const float2 e0 = make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
-                        const float2 e1 = make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
+                        const bool emu = (i % 16) >= 16 - C::EMU16;    // compile-time per i
+                        const float2 e0 = emu ? exp2_poly2(x0) : make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
+                        const float2 e1 = emu ? exp2_poly2(x1) : make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
                         acc0 = fadd2(acc0, e0);
                         acc1 = fadd2(acc1, e1);
                         sr[i / 2] = pack_half2(e0.x, e0.y);
@@ -513,28 +534,63 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     }
                     if (threadIdx.x == 128) p.counters[su] = 0u;
                 }
-            } else if (ok) {
-                tc_fence_after();
-                const float f = ex2_approx((m_ref - m_true) * c);   // rebase to the true max
-                const float l_true = l * f;
-                const float osc = p.unnormalized ? f : 1.0f / l;
-#pragma unroll
-                for (int dc = 0; dc < D / OCH; ++dc) {
-                    uint32_t o[OCH];
-                    tmem_ld_chunk<OCH>(tO + dc * OCH, o);
-                    tmem_wait_ld();
-                    if (store) {
-#pragma unroll
-                        for (int k = 0; k < OCH; k += 4) {
-                            float4 v = make_float4(__uint_as_float(o[k]) * osc, __uint_as_float(o[k + 1]) * osc,
-                                                   __uint_as_float(o[k + 2]) * osc, __uint_as_float(o[k + 3]) * osc);
-                            *reinterpret_cast<float4*>(orow + dc * OCH + k) = v;
+            } else {
+                // Every thread of the tile reaches this barrier, ok or not, so the staged
+                // epilogue below (which synchronizes the tile's threads) runs for all or none.
+                if constexpr (C::TMA_STORE) ok = named_bar_and(2 + t, 128, ok);
+                if (ok) {
+                    tc_fence_after();
+                    const float f = ex2_approx((m_ref - m_true) * c);   // rebase to the true max
+                    const float l_true = l * f;
+                    const float osc = p.unnormalized ? f : 1.0f / l;
+                    if constexpr (C::TMA_STORE) {
+                        // Stage the O tile in shared memory that no MMA reads any more: the Q
+                        // region for tile 0 (every QK MMA precedes the last PV_0), the K/V ring
+                        // for tile 1 (all MMAs are complete once o_full[1] fired) and for a
+                        // single tile.  Span s of 32 columns holds rows of 128 B with the
+                        // 16-B chunks XOR-swizzled by row % 8 (the map's 128-B swizzle).
+                        uint8_t* sO = (NQ == 2 && t == 0) ? sQ : sKV;
+    #pragma unroll
+                        for (int dc = 0; dc < D / 32; ++dc) {
+                            uint32_t o[32];
+                            tmem_ld32(tO + dc * 32, o);
+                            tmem_wait_ld();
+                            uint8_t* rowp = sO + dc * (BM * 128) + row * 128;
+    #pragma unroll
+                            for (int q = 0; q < 8; ++q) {
+                                const float4 v = make_float4(__uint_as_float(o[4 * q]) * osc, __uint_as_float(o[4 * q + 1]) * osc,
+                                                             __uint_as_float(o[4 * q + 2]) * osc, __uint_as_float(o[4 * q + 3]) * osc);
+                                *reinterpret_cast<float4*>(rowp + ((q ^ (row & 7)) << 4)) = v;
+                            }
+                        }
+                        fence_proxy_async_smem();
+                        named_bar_sync(2 + t, 128);             // this tile's 128 softmax threads
+                        if (row == 0) {
+                            for (int dc = 0; dc < D / 32; ++dc)
+                                tma_store_3d(&tmO, sO + dc * (BM * 128), dc * 32, q_row0 + t * BM, b * p.H_q + h);
+                            bulk_commit_group();
+                            bulk_wait_group_read0();            // shared memory read before the CTA exits
+                        }
+                    } else {
+    #pragma unroll
+                        for (int dc = 0; dc < D / OCH; ++dc) {
+                            uint32_t o[OCH];
+                            tmem_ld_chunk<OCH>(tO + dc * OCH, o);
+                            tmem_wait_ld();
+                            if (store) {
+    #pragma unroll
+                                for (int k = 0; k < OCH; k += 4) {
+                                    float4 v = make_float4(__uint_as_float(o[k]) * osc, __uint_as_float(o[k + 1]) * osc,
+                                                           __uint_as_float(o[k + 2]) * osc, __uint_as_float(o[k + 3]) * osc);
+                                    *reinterpret_cast<float4*>(orow + dc * OCH + k) = v;
+                                }
+                            }
                         }
                     }
-                }
-                if (store) {
-                    if (p.Mi) p.Mi[mi] = m_true * p.scale;
-                    if (p.Li) p.Li[mi] = l_true;
+                    if (store) {
+                        if (p.Mi) p.Mi[mi] = m_true * p.scale;
+                        if (p.Li) p.Li[mi] = l_true;
+                    }
                 }
             }
             tc_fence_before();
