@@ -351,7 +351,11 @@ def run_extras(args, rank, world, dev, peaks):
 
 
 def run_long_decode_split(args, rank, world, dev, peaks):
-    """C5 across the N GPUs: KV split by ranges, partials + one all-gather + LSE merge."""
+    """C5 across the N GPUs: KV split by ranges, partials + one all-gather + LSE merge.
+
+    Timed two ways, max over ranks: host-driven calls, and the same step (partial
+    kernel, NCCL all-gather, combine kernel) captured once in a CUDA graph and
+    replayed (device time, the number a decode loop that replays graphs sees)."""
     import torch
     import torch.distributed as dist
 
@@ -365,14 +369,46 @@ def run_long_decode_split(args, rank, world, dev, peaks):
     gen.manual_seed(6006 + rank)
     k = rand_f16((1, H_KV, hi - lo, D), gen, dev)
     v = rand_f16((1, H_KV, hi - lo, D), gen, dev)
-    buf = torch.empty(world * (H_Q * D + 2 * H_Q), dtype=torch.float32, device=dev)
+    n = (H_Q * (D + 2) + 3) // 4 * 4
+    buf = torch.empty(world * n, dtype=torch.float32, device=dev)
+    out = torch.empty((1, H_Q, 1, D), dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
+    iters = max(10, min(args.steps, 50))
+
+    def step(_):
+        long_decode_forward(q, k, v, gather_buf=buf, out=out)
+
     dist.barrier(device_ids=[dev.index])
-    ms = time_loop(lambda i: long_decode_forward(q, k, v, gather_buf=buf), max(10, min(args.steps, 50)), 3, stream)
-    (ms,) = max_over_ranks([ms], world, dev)
-    gbs = decode_bytes(1, H_Q, H_KV, S_kv, D) / (ms * 1e-3) / 1e9
-    return {"us": round(ms * 1e3, 2), "GB/s_total": round(gbs, 1), "GB/s_per_gpu": round(gbs / world, 1),
-            "frac_hbm_per_gpu": round(gbs / world / peaks["hbm_gbs"], 3), "collective": "1x all_gather (NCCL)"}
+    host_ms = time_loop(step, iters, 3, stream)
+    # CUDA graph: warm-up outside capture (NCCL communicator, workspace), then capture.
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        for i in range(3):
+            step(i)
+    stream.wait_stream(side)
+    torch.cuda.synchronize()
+    dist.barrier(device_ids=[dev.index])
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step(0)
+    g.replay()
+    torch.cuda.synchronize()
+    dist.barrier(device_ids=[dev.index])
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(iters):
+        g.replay()
+    e1.record(stream)
+    e1.synchronize()
+    graph_ms = e0.elapsed_time(e1) / iters
+    del g                                   # graphs holding NCCL work go before the process group
+    torch.cuda.synchronize()
+    host_ms, graph_ms = max_over_ranks([host_ms, graph_ms], world, dev)
+    gbs = decode_bytes(1, H_Q, H_KV, S_kv, D) / (graph_ms * 1e-3) / 1e9
+    return {"us": round(graph_ms * 1e3, 2), "host_call_us": round(host_ms * 1e3, 2), "GB/s_total": round(gbs, 1),
+            "GB/s_per_gpu": round(gbs / world, 1), "frac_hbm_per_gpu": round(gbs / world / peaks["hbm_gbs"], 3),
+            "collective": "1x all_gather (NCCL), in place; us = CUDA-graph replay"}
 
 
 def cpu_baseline_sample(budget_s=12.0):

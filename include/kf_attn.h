@@ -94,6 +94,16 @@ int kf_attn_combine(const float* O_parts, const float* m_parts, const float* l_p
                     int n_parts, float* O, float* Mi, float* Li,
                     int B, int H_q, int S_q, int D, void* stream);
 
+/* The same merge over partials packed back to back, part g at
+ *   parts + g*part_stride = [O_u: B*H_q*S_q*D][m: B*H_q*S_q][l: B*H_q*S_q],
+ * part_stride >= B*H_q*S_q*(D+2) floats and a multiple of 4: the layout of an
+ * all-gather of each rank's kf_attn_fwd_partial output written into its slot,
+ * merged without an unpacking copy.  No reference counterpart (see
+ * kf_attn_fwd_partial). */
+int kf_attn_combine_packed(const float* parts, long long part_stride, int n_parts,
+                           float* O, float* Mi, float* Li,
+                           int B, int H_q, int S_q, int D, void* stream);
+
 /* Bytes of workspace the call with these arguments would use (0 if none). */
 size_t kf_attn_workspace_bytes(int B, int H_q, int H_kv, int S_q, int S_kv, int D);
 

@@ -12,6 +12,7 @@ include/kf_attn.h); this package is the Python host side.
 """
 from ._lib import KFError, lib  # noqa: F401
 from .attention import (  # noqa: F401
+    combine_packed,
     combine_partials,
     device_error,
     flash_attn_fwd,

@@ -30,6 +30,7 @@ __all__ = [
     "flash_attn_fwd",
     "flash_attn_partial",
     "combine_partials",
+    "combine_packed",
     "plan",
     "workspace_bytes",
     "device_error",
@@ -124,13 +125,22 @@ def flash_attn_fwd(q, k, v, *, out=None, return_lse=False, workspace=None):
     return (out, Mi, Li) if return_lse else out
 
 
-def flash_attn_partial(q, k, v, *, workspace=None):
-    """(O_u, m, l) over the given K/V: O_u = sum exp(s - m) v, m = max s, l = sum exp(s - m)."""
+def flash_attn_partial(q, k, v, *, workspace=None, out=None):
+    """(O_u, m, l) over the given K/V: O_u = sum exp(s - m) v, m = max s, l = sum exp(s - m).
+
+    `out` = (O_u [B,H_q,S_q,D], m [B,H_q,S_q], l [B,H_q,S_q]) contiguous fp32 views to
+    write into (e.g. this rank's slot of an all-gather buffer)."""
     B, H_q, H_kv, S_q, S_kv, D = _check_qkv(q, k, v)
     dev = q.device
-    O_u = torch.empty((B, H_q, S_q, D), dtype=torch.float32, device=dev)
-    m = torch.empty((B, H_q, S_q), dtype=torch.float32, device=dev)
-    l = torch.empty_like(m)
+    if out is None:
+        O_u = torch.empty((B, H_q, S_q, D), dtype=torch.float32, device=dev)
+        m = torch.empty((B, H_q, S_q), dtype=torch.float32, device=dev)
+        l = torch.empty_like(m)
+    else:
+        O_u, m, l = out
+        for t, shp in ((O_u, (B, H_q, S_q, D)), (m, (B, H_q, S_q)), (l, (B, H_q, S_q))):
+            if tuple(t.shape) != shp or t.dtype != torch.float32 or not t.is_contiguous() or t.device != dev:
+                raise ValueError(f"out tensors must be contiguous fp32 {shp} on {dev}")
     with torch.cuda.device(dev):
         if workspace is None:
             workspace = _workspace(dev, workspace_bytes(B, H_q, H_kv, S_q, S_kv, D))
@@ -139,6 +149,28 @@ def flash_attn_partial(q, k, v, *, workspace=None):
                                        B, H_q, H_kv, S_q, S_kv, D, _ptr(workspace), wsb, _stream_handle(dev))
     check(rc, "kf_attn_fwd_partial")
     return O_u, m, l
+
+
+def combine_packed(parts, n_parts, part_stride, shape, *, out=None, return_lse=False):
+    """Merge n_parts partials packed back to back in the fp32 buffer `parts`
+    (part g at g*part_stride: [O_u rows*D][m rows][l rows]) into O of `shape` (B,H_q,S_q,D)."""
+    if not parts.is_cuda or parts.dtype != torch.float32 or not parts.is_contiguous():
+        raise ValueError("parts must be a contiguous fp32 CUDA tensor (no CPU path)")
+    B, H_q, S_q, D = shape
+    if parts.numel() < (n_parts - 1) * part_stride + B * H_q * S_q * (D + 2):
+        raise ValueError("parts buffer too small")
+    dev = parts.device
+    if out is None:
+        out = torch.empty((B, H_q, S_q, D), dtype=torch.float32, device=dev)
+    Mi = Li = None
+    if return_lse:
+        Mi = torch.empty((B, H_q, S_q), dtype=torch.float32, device=dev)
+        Li = torch.empty_like(Mi)
+    with torch.cuda.device(dev):
+        rc = lib().kf_attn_combine_packed(_ptr(parts), part_stride, n_parts, _ptr(out), _ptr(Mi), _ptr(Li),
+                                          B, H_q, S_q, D, _stream_handle(dev))
+    check(rc, "kf_attn_combine_packed")
+    return (out, Mi, Li) if return_lse else out
 
 
 def combine_partials(O_parts, m_parts, l_parts, *, out=None, return_lse=False):

@@ -482,7 +482,9 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
 // [G][rows] and [G][rows][D].  Used after the cross-GPU all-gather.
 __global__ void combine_partials_kernel(const float* __restrict__ O_parts, const float* __restrict__ m_parts,
                                         const float* __restrict__ l_parts, int n_parts, long long rows, int D,
+                                        long long stride_o, long long stride_ml,
                                         float* __restrict__ O, float* __restrict__ Mi, float* __restrict__ Li) {
+    // Part g: O at O_parts + g*stride_o ([rows][D]), m/l at m_parts/l_parts + g*stride_ml ([rows]).
     const long long n4 = rows * (D / 4);
     constexpr float LOG2E = 1.4426950408889634f;
     for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < n4;
@@ -490,14 +492,14 @@ __global__ void combine_partials_kernel(const float* __restrict__ O_parts, const
         const long long row = idx / (D / 4);
         const int d = static_cast<int>(idx % (D / 4)) * 4;
         float M = -CUDART_INF_F;
-        for (int g = 0; g < n_parts; ++g) M = fmaxf(M, m_parts[g * rows + row]);
+        for (int g = 0; g < n_parts; ++g) M = fmaxf(M, m_parts[g * stride_ml + row]);
         const float Mu = (M == -CUDART_INF_F) ? 0.f : M;
         float L = 0.f;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int g = 0; g < n_parts; ++g) {
-            const float wt = ex2_approx((m_parts[g * rows + row] - Mu) * LOG2E);
-            L += wt * l_parts[g * rows + row];
-            const float4 v = *reinterpret_cast<const float4*>(O_parts + (g * rows + row) * D + d);
+            const float wt = ex2_approx((m_parts[g * stride_ml + row] - Mu) * LOG2E);
+            L += wt * l_parts[g * stride_ml + row];
+            const float4 v = *reinterpret_cast<const float4*>(O_parts + g * stride_o + row * D + d);
             acc.x += wt * v.x; acc.y += wt * v.y; acc.z += wt * v.z; acc.w += wt * v.w;
         }
         const float inv = 1.f / L;

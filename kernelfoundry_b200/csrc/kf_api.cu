@@ -517,14 +517,10 @@ int kf_attn_fwd_partial(const void* Q, const void* K, const void* V, float* O_u,
     return attn_core(Q, K, V, O_u, m, l, 1, B, H_q, H_kv, S_q, S_kv, D, workspace, workspace_bytes, stream);
 }
 
-int kf_attn_combine(const float* O_parts, const float* m_parts, const float* l_parts, int n_parts, float* O,
-                    float* Mi, float* Li, int B, int H_q, int S_q, int D, void* stream) {
-    if (n_parts <= 0 || B < 0 || H_q <= 0 || S_q < 0) return KF_ERR_INVALID_ARG;
-    if (!(D == 16 || D == 64 || D == 128 || D == 256)) return KF_ERR_UNSUPPORTED_HEAD_DIM;
-    const long long rows = static_cast<long long>(B) * H_q * S_q;
-    if (rows == 0) return KF_OK;
-    if (!O_parts || !m_parts || !l_parts || !O) return KF_ERR_INVALID_ARG;
-    if (!aligned16(O_parts) || !aligned16(O)) return KF_ERR_MISALIGNED;
+namespace {
+int combine_launch(const float* O_parts, const float* m_parts, const float* l_parts, int n_parts,
+                   long long stride_o, long long stride_ml, float* O, float* Mi, float* Li, long long rows, int D,
+                   void* stream) {
     DeviceInfo* di = nullptr;
     int rc = device_info(&di);
     if (rc != KF_OK) return rc;
@@ -534,9 +530,34 @@ int kf_attn_combine(const float* O_parts, const float* m_parts, const float* l_p
     const long long maxb = static_cast<long long>(di->sm_count) * 8;
     if (blocks > maxb) blocks = maxb;
     kf::combine_partials_kernel<<<static_cast<unsigned>(blocks), threads, 0, static_cast<cudaStream_t>(stream)>>>(
-        O_parts, m_parts, l_parts, n_parts, rows, D, O, Mi, Li);
+        O_parts, m_parts, l_parts, n_parts, rows, D, stride_o, stride_ml, O, Mi, Li);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KF_OK : cuda_fail(e);
+}
+}  // namespace
+
+int kf_attn_combine(const float* O_parts, const float* m_parts, const float* l_parts, int n_parts, float* O,
+                    float* Mi, float* Li, int B, int H_q, int S_q, int D, void* stream) {
+    if (n_parts <= 0 || B < 0 || H_q <= 0 || S_q < 0) return KF_ERR_INVALID_ARG;
+    if (!(D == 16 || D == 64 || D == 128 || D == 256)) return KF_ERR_UNSUPPORTED_HEAD_DIM;
+    const long long rows = static_cast<long long>(B) * H_q * S_q;
+    if (rows == 0) return KF_OK;
+    if (!O_parts || !m_parts || !l_parts || !O) return KF_ERR_INVALID_ARG;
+    if (!aligned16(O_parts) || !aligned16(O)) return KF_ERR_MISALIGNED;
+    return combine_launch(O_parts, m_parts, l_parts, n_parts, rows * D, rows, O, Mi, Li, rows, D, stream);
+}
+
+int kf_attn_combine_packed(const float* parts, long long part_stride, int n_parts, float* O, float* Mi, float* Li,
+                           int B, int H_q, int S_q, int D, void* stream) {
+    if (n_parts <= 0 || B < 0 || H_q <= 0 || S_q < 0) return KF_ERR_INVALID_ARG;
+    if (!(D == 16 || D == 64 || D == 128 || D == 256)) return KF_ERR_UNSUPPORTED_HEAD_DIM;
+    const long long rows = static_cast<long long>(B) * H_q * S_q;
+    if (rows == 0) return KF_OK;
+    if (!parts || !O) return KF_ERR_INVALID_ARG;
+    if (part_stride < rows * (D + 2) || part_stride % 4 != 0) return KF_ERR_INVALID_ARG;
+    if (!aligned16(parts) || !aligned16(O)) return KF_ERR_MISALIGNED;
+    return combine_launch(parts, parts + rows * D, parts + rows * D + rows, n_parts, part_stride, part_stride, O, Mi,
+                          Li, rows, D, stream);
 }
 
 size_t kf_attn_workspace_bytes(int B, int H_q, int H_kv, int S_q, int S_kv, int D) {

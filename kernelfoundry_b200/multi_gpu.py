@@ -90,15 +90,43 @@ def _cuda_combine(O_p, m_p, l_p):
 
 def long_decode_forward(q: torch.Tensor, k_shard: torch.Tensor, v_shard: torch.Tensor,
                         group: Optional[dist.ProcessGroup] = None,
-                        partial_fn: Callable = _cuda_partial, combine_fn: Callable = _cuda_combine,
-                        gather_buf: Optional[torch.Tensor] = None) -> torch.Tensor:
+                        partial_fn: Optional[Callable] = None, combine_fn: Optional[Callable] = None,
+                        gather_buf: Optional[torch.Tensor] = None,
+                        out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Attention of q over a KV cache split across the ranks of `group`.
 
     q [B,H_q,S_q,D] is replicated; k_shard/v_shard [B,H_kv,S_r,D] hold this
     rank's contiguous KV range (kv_shard()).  Returns the full O on every rank.
     Every rank makes the same single collective call (all_gather_into_tensor).
+
+    With the CUDA kernels (the default) the partials are written straight into
+    this rank's slot of `gather_buf` ([world * B*H_q*S_q*(D+2)] fp32, reusable
+    across calls), gathered in place and merged from the packed layout: one
+    partial launch, one all-gather, one combine launch and no host-side copies,
+    so a decode step can be captured in a CUDA graph.  `partial_fn` /
+    `combine_fn` substitute the compute (tests on CPU ranks).
     """
     world = dist.get_world_size(group) if dist.is_initialized() else 1
+    if partial_fn is None and combine_fn is None:
+        from .attention import combine_packed, flash_attn_partial
+
+        B, H_q, S_q, D = q.shape
+        rows = B * H_q * S_q
+        n = rows * (D + 2)
+        n = (n + 3) // 4 * 4                      # 16-byte aligned slots
+        rank = dist.get_rank(group) if world > 1 else 0
+        if gather_buf is None or gather_buf.numel() != world * n or gather_buf.device != q.device:
+            gather_buf = torch.empty(world * n, dtype=torch.float32, device=q.device)
+        slot = gather_buf[rank * n:(rank + 1) * n]
+        O_u = slot[:rows * D].view(B, H_q, S_q, D)
+        m = slot[rows * D:rows * D + rows].view(B, H_q, S_q)
+        l = slot[rows * D + rows:rows * (D + 2)].view(B, H_q, S_q)
+        flash_attn_partial(q, k_shard, v_shard, out=(O_u, m, l))
+        if world > 1:
+            dist.all_gather_into_tensor(gather_buf, slot, group=group)   # in place: slot is this rank's part
+        return combine_packed(gather_buf, world, n, (B, H_q, S_q, D), out=out)
+    partial_fn = partial_fn or _cuda_partial
+    combine_fn = combine_fn or _cuda_combine
     O_u, m, l = partial_fn(q, k_shard, v_shard)
     if world == 1:
         return combine_fn(O_u.unsqueeze(0), m.unsqueeze(0), l.unsqueeze(0))

@@ -94,6 +94,16 @@ def test_argument_validation_without_gpu(kf_lib):
     assert kf_lib.kf_attn_combine(FAKE, FAKE, FAKE, 2, FAKE, None, None, 1, 4, 8, 48, None) \
         == L.KF_ERR_UNSUPPORTED_HEAD_DIM
     assert kf_lib.kf_attn_combine(FAKE, FAKE, FAKE, 2, FAKE, None, None, 0, 4, 8, 64, None) == L.KF_OK
+    # Packed combine: part stride below rows*(D+2) or not a multiple of 4 is rejected before any launch.
+    assert kf_lib.kf_attn_combine_packed(FAKE, 4 * 8 * 66 - 4, 2, FAKE, None, None, 1, 4, 8, 64, None) \
+        == L.KF_ERR_INVALID_ARG
+    assert kf_lib.kf_attn_combine_packed(FAKE, 4 * 8 * 66 + 2, 2, FAKE, None, None, 1, 4, 8, 64, None) \
+        == L.KF_ERR_INVALID_ARG
+    assert kf_lib.kf_attn_combine_packed(FAKE, 4 * 8 * 66, 0, FAKE, None, None, 1, 4, 8, 64, None) \
+        == L.KF_ERR_INVALID_ARG
+    assert kf_lib.kf_attn_combine_packed(FAKE, 4 * 8 * 50, 2, FAKE, None, None, 1, 4, 8, 48, None) \
+        == L.KF_ERR_UNSUPPORTED_HEAD_DIM
+    assert kf_lib.kf_attn_combine_packed(FAKE, 4 * 8 * 66, 2, FAKE, None, None, 0, 4, 8, 64, None) == L.KF_OK
     assert kf_lib.kf_attn_workspace_bytes(1, 6, 4, 1, 100, 128) == 0
     assert kf_lib.kf_launch_flash_attn(FAKE, FAKE, FAKE, FAKE, 1, 16, 1, 1, 48, None) \
         == L.KF_ERR_UNSUPPORTED_HEAD_DIM

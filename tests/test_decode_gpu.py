@@ -108,3 +108,50 @@ def test_partials_and_combine_match_full(cuda):
     assert_close(out.cpu().numpy(), O, "combined")
     assert np.abs(Mi.cpu().numpy() - rMi).max() < 1e-3
     assert np.abs(Li.cpu().numpy() / rLi - 1).max() < 1e-3
+
+
+def test_combine_packed_matches_combine(cuda):
+    """Partials written into the slots of one packed buffer ([O_u | m | l] per part, as an
+    all-gather leaves them) merge to the same result as the stacked form."""
+    import torch
+
+    from kernelfoundry_b200 import combine_packed, combine_partials, flash_attn_partial
+
+    Q, K, V = normal_qkv(2, 16, 4, 1, 9000, 128, seed=123)
+    q = to_dev(Q, cuda)
+    B, H_q, S_q, D = Q.shape
+    rows = B * H_q * S_q
+    n = (rows * (D + 2) + 3) // 4 * 4
+    cuts = [0, 3000, 3001, 9000]
+    G = len(cuts) - 1
+    buf = torch.full((G * n,), float("nan"), dtype=torch.float32, device=cuda)
+    stacked = []
+    for g, (lo, hi) in enumerate(zip(cuts[:-1], cuts[1:])):
+        k = to_dev(K[:, :, lo:hi].copy(), cuda)
+        v = to_dev(V[:, :, lo:hi].copy(), cuda)
+        slot = buf[g * n:(g + 1) * n]
+        views = (slot[:rows * D].view(B, H_q, S_q, D), slot[rows * D:rows * D + rows].view(B, H_q, S_q),
+                 slot[rows * D + rows:rows * (D + 2)].view(B, H_q, S_q))
+        flash_attn_partial(q, k, v, out=views)
+        stacked.append(flash_attn_partial(q, k, v))
+    got, Mi, Li = combine_packed(buf, G, n, (B, H_q, S_q, D), return_lse=True)
+    ref = combine_partials(torch.stack([s[0] for s in stacked]), torch.stack([s[1] for s in stacked]),
+                           torch.stack([s[2] for s in stacked]))
+    assert torch.equal(got, ref)                       # same arithmetic, same order: bit-exact
+    O, rMi, rLi = oracle64(Q, K, V)
+    assert_close(got.cpu().numpy(), O, "packed")
+    assert np.abs(Mi.cpu().numpy() - rMi).max() < 1e-3
+    assert np.abs(Li.cpu().numpy() / rLi - 1).max() < 1e-3
+
+
+def test_long_decode_forward_single_process(cuda):
+    """The in-place (partial -> slot -> packed combine) path with one rank == full attention."""
+    import torch
+
+    from kernelfoundry_b200.multi_gpu import long_decode_forward
+
+    Q, K, V = normal_qkv(1, 32, 8, 1, 20000, 128, seed=321)
+    out = torch.empty((1, 32, 1, 128), dtype=torch.float32, device=cuda)
+    got = long_decode_forward(*(to_dev(x, cuda) for x in (Q, K, V)), out=out)
+    assert got.data_ptr() == out.data_ptr()
+    assert_close(out.cpu().numpy(), oracle64(Q, K, V)[0], "long decode, one rank")
