@@ -334,6 +334,8 @@ int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, 
     if ((rc = make_map(&mq, Q, D, S_q, static_cast<long long>(B) * H_q, q_box, C::SWB)) != KF_OK) return rc;
     if ((rc = make_map(&mk, K, D, S_kv, static_cast<long long>(B) * H_kv, kv_box, C::SWB)) != KF_OK) return rc;
     if ((rc = make_map(&mv, V, D, S_kv, static_cast<long long>(B) * H_kv, kv_box, C::SWB)) != KF_OK) return rc;
+    CUtensorMap mp;
+    std::memset(&mp, 0, sizeof(mp));
     if (C::TMA_STORE) {
         if ((rc = make_map_f32(&mo, O, D, S_q, static_cast<long long>(B) * H_q, q_box)) != KF_OK) return rc;
     } else {
@@ -362,9 +364,14 @@ int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, 
     const bool split = pl.pf_plain < pl.pf_units;
     p.counters = split ? static_cast<unsigned*>(ws) : nullptr;
     p.part = split ? reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kCounterBytes) : nullptr;
+    if (split && C::TMA_STORE) {
+        // Partial O_u slots as a [rows][D] fp32 tensor, written by the chunks' TMA stores.
+        const long long slot_rows = static_cast<long long>(pl.pf_units - pl.pf_plain) * pl.pf_k * C::NQ * C::BM;
+        if ((rc = make_map_f32(&mp, p.part, D, static_cast<int>(slot_rows), 1, C::BM)) != KF_OK) return rc;
+    }
     const long long ctas = pl.ctas;
     if (ctas <= 0 || ctas > 0x7fffffffll) return KF_ERR_INVALID_ARG;
-    kf::prefill_fwd_kernel<D><<<static_cast<unsigned>(ctas), C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, mo, p);
+    kf::prefill_fwd_kernel<D><<<static_cast<unsigned>(ctas), C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, mo, mp, p);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KF_OK : cuda_fail(e);
 }

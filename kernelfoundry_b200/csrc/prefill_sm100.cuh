@@ -124,7 +124,7 @@ template <int D>
 __global__ void __launch_bounds__(PrefillCfg<D>::THREADS, 1)
 prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
-                   const PrefillParams p) {
+                   const __grid_constant__ CUtensorMap tmP, const PrefillParams p) {
     using C = PrefillCfg<D>;
     constexpr int BM = C::BM, BC = C::BC, NQ = C::NQ, SWB = C::SWB, SWE = C::SWE, NSPAN = C::NSPAN;
     constexpr int NSLOT = C::NSLOT;
@@ -462,25 +462,51 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             float* orow = p.O + ((static_cast<size_t>(b) * p.H_q + h) * p.S_q + (store ? qrow : 0)) * D;
             const size_t mi = (static_cast<size_t>(b) * p.H_q + h) * p.S_q + (store ? qrow : 0);
             if (split) {
-                // KV chunk of a split unit: write this row's partial (O_u, m, l)
-                // relative to its own max; the last chunk to finish merges them.
+                // KV chunk of a split unit: write this tile's partial (O_u, m, l) relative
+                // to its own max; the last chunk to finish merges the unit's partials.
                 // Layout: O_u [split unit][chunk][ROWS][D], then (m, l) [..][ROWS][2].
                 const int su = unit - p.n_plain;
                 constexpr int ROWS = NQ * BM;
                 const size_t n_slots = static_cast<size_t>(p.n_units - p.n_plain) * p.split_k * ROWS;
-                const size_t slot0 = static_cast<size_t>(su) * p.split_k * ROWS + t * BM + row;   // chunk 0
-                const size_t my_slot = slot0 + static_cast<size_t>(chunk) * ROWS;
-                float* part_ml = p.part + n_slots * D;
+                const size_t unit0 = static_cast<size_t>(su) * p.split_k * ROWS;           // chunk 0, row 0
+                const size_t tile0 = unit0 + static_cast<size_t>(chunk) * ROWS + t * BM;   // this tile's rows
+                float2* part_ml = reinterpret_cast<float2*>(p.part + n_slots * D);
+                if constexpr (C::TMA_STORE) ok = named_bar_and(2 + t, 128, ok);
                 if (ok) {
                     tc_fence_after();
                     const float f = ex2_approx((m_ref - m_true) * c);
-                    float* prow = p.part + my_slot * D;
+                    if constexpr (C::TMA_STORE) {
+                        // Staged like the final epilogue, then TMA-stored into the partial
+                        // slots; the stores must be complete (not only read) before the ticket.
+                        uint8_t* sO = (NQ == 2 && t == 0) ? sQ : sKV;
 #pragma unroll
-                    for (int dc = 0; dc < D / OCH; ++dc) {
-                        uint32_t o[OCH];
-                        tmem_ld_chunk<OCH>(tO + dc * OCH, o);
-                        tmem_wait_ld();
-                        if (store) {
+                        for (int dc = 0; dc < D / 32; ++dc) {
+                            uint32_t o[32];
+                            tmem_ld32(tO + dc * 32, o);
+                            tmem_wait_ld();
+                            uint8_t* rowp = sO + dc * (BM * 128) + row * 128;
+#pragma unroll
+                            for (int q = 0; q < 8; ++q)
+                                *reinterpret_cast<float4*>(rowp + ((q ^ (row & 7)) << 4)) =
+                                    make_float4(__uint_as_float(o[4 * q]) * f, __uint_as_float(o[4 * q + 1]) * f,
+                                                __uint_as_float(o[4 * q + 2]) * f, __uint_as_float(o[4 * q + 3]) * f);
+                        }
+                        fence_proxy_async_smem();
+                        named_bar_sync(2 + t, 128);
+                        if (row == 0) {
+                            for (int dc = 0; dc < D / 32; ++dc)
+                                tma_store_3d(&tmP, sO + dc * (BM * 128), dc * 32, static_cast<int>(tile0), 0);
+                            bulk_commit_group();
+                            bulk_wait_group0();
+                            fence_proxy_async_global();
+                        }
+                    } else {
+                        float* prow = p.part + (tile0 + row) * D;
+#pragma unroll
+                        for (int dc = 0; dc < D / OCH; ++dc) {
+                            uint32_t o[OCH];
+                            tmem_ld_chunk<OCH>(tO + dc * OCH, o);
+                            tmem_wait_ld();
 #pragma unroll
                             for (int k = 0; k < OCH; k += 4)
                                 *reinterpret_cast<float4*>(prow + dc * OCH + k) =
@@ -488,7 +514,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                                                 __uint_as_float(o[k + 2]) * f, __uint_as_float(o[k + 3]) * f);
                         }
                     }
-                    if (store) *reinterpret_cast<float2*>(part_ml + my_slot * 2) = make_float2(m_true, l * f);
+                    part_ml[tile0 + row] = make_float2(m_true, l * f);
                 }
                 __threadfence();
                 named_bar_sync(1, 128 * nq_active);     // every active softmax thread, ok or not
@@ -499,38 +525,73 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 named_bar_sync(1, 128 * nq_active);
                 if (*ticket_last) {
                     __threadfence();
-                    if (store) {
-                        // split_k <= 4 (host plan): all loads of a row are independent.
-                        float2 ml[4];
+                    // Merge, one warp per 32 consecutive rows: lane i computes the weights of
+                    // row i from the chunks' (m, l); then for each row the lanes read the
+                    // chunks' O_u rows (coalesced, several rows in flight) and write O.
+                    const int wi = warp - 4;                      // 0 .. 4*nq_active-1
+                    const int r = wi * 32 + lane;                 // row of the unit this lane weighs
+                    float2 ml[4];
 #pragma unroll
-                        for (int c2 = 0; c2 < 4; ++c2)
-                            ml[c2] = c2 < p.split_k ? __ldcg(reinterpret_cast<const float2*>(part_ml) + slot0 + c2 * ROWS)
-                                                    : make_float2(-CUDART_INF_F, 0.f);
-                        const float M = fmaxf(fmaxf(ml[0].x, ml[1].x), fmaxf(ml[2].x, ml[3].x));
-                        float w[4], L = 0.f;
+                    for (int c2 = 0; c2 < 4; ++c2)
+                        ml[c2] = c2 < p.split_k ? __ldcg(part_ml + unit0 + static_cast<size_t>(c2) * ROWS + r)
+                                                : make_float2(-CUDART_INF_F, 0.f);
+                    const float M = fmaxf(fmaxf(ml[0].x, ml[1].x), fmaxf(ml[2].x, ml[3].x));
+                    float w[4], L = 0.f;
 #pragma unroll
-                        for (int c2 = 0; c2 < 4; ++c2) {
-                            w[c2] = c2 < p.split_k ? ex2_approx((ml[c2].x - M) * c) : 0.f;
-                            L += w[c2] * ml[c2].y;
-                        }
-                        const float osc = p.unnormalized ? 1.0f : 1.0f / L;
+                    for (int c2 = 0; c2 < 4; ++c2) {
+                        w[c2] = c2 < p.split_k ? ex2_approx((ml[c2].x - M) * c) : 0.f;
+                        L += w[c2] * ml[c2].y;
+                    }
+                    const float osc = p.unnormalized ? 1.0f : 1.0f / L;
 #pragma unroll
-                        for (int c2 = 0; c2 < 4; ++c2) w[c2] *= osc;
-#pragma unroll 4
-                        for (int d = 0; d < D; d += 4) {
-                            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int c2 = 0; c2 < 4; ++c2) w[c2] *= osc;
+                    const int qrow_l = q_row0 + r;
+                    if (qrow_l < p.S_q) {
+                        const size_t mi_l = (static_cast<size_t>(b) * p.H_q + h) * p.S_q + qrow_l;
+                        if (p.Mi) p.Mi[mi_l] = M * p.scale;
+                        if (p.Li) p.Li[mi_l] = L;
+                    }
+                    const float* part_o = p.part + unit0 * D;
+                    float* obase = p.O + ((static_cast<size_t>(b) * p.H_q + h) * p.S_q) * D;
+                    constexpr int RU = D <= 128 ? 8 : 4;          // rows in flight per lane
+#pragma unroll 1
+                    for (int j0 = 0; j0 < 32; j0 += RU) {
+                        float4 acc[RU][(D / 4 + 31) / 32];
 #pragma unroll
-                            for (int c2 = 0; c2 < 4; ++c2) {
-                                if (c2 < p.split_k) {
-                                    const float4 v = __ldcg(reinterpret_cast<const float4*>(
-                                        p.part + (slot0 + static_cast<size_t>(c2) * ROWS) * D + d));
-                                    acc.x += w[c2] * v.x; acc.y += w[c2] * v.y; acc.z += w[c2] * v.z; acc.w += w[c2] * v.w;
+                        for (int u = 0; u < RU; ++u) {
+                            const int rr = wi * 32 + j0 + u;
+                            float wj[4];
+#pragma unroll
+                            for (int c2 = 0; c2 < 4; ++c2) wj[c2] = __shfl_sync(0xffffffffu, w[c2], j0 + u);
+#pragma unroll
+                            for (int ci = 0; ci < (D / 4 + 31) / 32; ++ci) {
+                                const int cidx = lane + ci * 32;
+                                acc[u][ci] = make_float4(0.f, 0.f, 0.f, 0.f);
+                                if (cidx < D / 4) {
+#pragma unroll
+                                    for (int c2 = 0; c2 < 4; ++c2) {
+                                        if (c2 < p.split_k) {
+                                            const float4 v = __ldcg(reinterpret_cast<const float4*>(
+                                                part_o + (static_cast<size_t>(c2) * ROWS + rr) * D) + cidx);
+                                            acc[u][ci].x += wj[c2] * v.x; acc[u][ci].y += wj[c2] * v.y;
+                                            acc[u][ci].z += wj[c2] * v.z; acc[u][ci].w += wj[c2] * v.w;
+                                        }
+                                    }
                                 }
                             }
-                            *reinterpret_cast<float4*>(orow + d) = acc;
                         }
-                        if (p.Mi) p.Mi[mi] = M * p.scale;
-                        if (p.Li) p.Li[mi] = L;
+#pragma unroll
+                        for (int u = 0; u < RU; ++u) {
+                            const int qr = q_row0 + wi * 32 + j0 + u;
+                            if (qr < p.S_q) {
+#pragma unroll
+                                for (int ci = 0; ci < (D / 4 + 31) / 32; ++ci) {
+                                    const int cidx = lane + ci * 32;
+                                    if (cidx < D / 4)
+                                        reinterpret_cast<float4*>(obase + static_cast<size_t>(qr) * D)[cidx] = acc[u][ci];
+                                }
+                            }
+                        }
                     }
                     if (threadIdx.x == 128) p.counters[su] = 0u;
                 }
