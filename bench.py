@@ -46,6 +46,13 @@ def prefill_flops(B, H_q, S_q, S_kv, D_):
     return 4.0 * B * H_q * S_q * S_kv * D_
 
 
+def causal_flops(B, H_q, S_q, S_kv, D_):
+    """4*D per visible (query, key) pair under the bottom-right causal mask."""
+    off = S_kv - S_q
+    pairs = sum(min(S_kv, off + i + 1) for i in range(S_q))
+    return 4.0 * B * H_q * pairs * D_
+
+
 def decode_bytes(B, H_q, H_kv, S_kv, D_):
     return 2.0 * B * H_kv * S_kv * D_ * 2 + 2.0 * B * H_q * D_ + 4.0 * B * H_q * D_
 
@@ -308,7 +315,7 @@ def run_extras(args, rank, world, dev, peaks):
     iters = max(10, min(args.steps, 50))
     out = {}
 
-    def bench_cfg(B, Hq, Hkv, Sq, Skv, Dh):
+    def bench_cfg(B, Hq, Hkv, Sq, Skv, Dh, causal=False):
         one = (B * Hq * Sq * Dh * 2 + 2 * B * Hkv * Skv * Dh * 2 + B * Hq * Sq * Dh * 4)
         rot = max(1, min(16, -(-2 * l2 // one) + 1)) if one < 2 * l2 else 1
         qs = [rand_f16((B, Hq, Sq, Dh), gen, dev) for _ in range(rot)]
@@ -318,7 +325,7 @@ def run_extras(args, rank, world, dev, peaks):
 
         def f(i):
             j = i % rot
-            flash_attn_fwd(qs[j], ks[j], vs[j], out=os_[j])
+            flash_attn_fwd(qs[j], ks[j], vs[j], out=os_[j], causal=causal)
 
         host_ms = time_loop(f, iters, 3, stream)
         n_calls = rot * max(1, 8 // rot)
@@ -346,6 +353,11 @@ def run_extras(args, rank, world, dev, peaks):
     ms, rot, pl = bench_cfg(1, H_Q, H_KV, 512, 512, D)
     tf = prefill_flops(1, H_Q, 512, 512, D) / (ms * 1e-3) / 1e12
     out["prefill_S512_B1"] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 1)}
+    ms, rot, pl = bench_cfg(1, H_Q, H_KV, S, S, D, causal=True)
+    tf = causal_flops(1, H_Q, S, S, D) / (ms * 1e-3) / 1e12
+    out["prefill_causal_S4096_B1"] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 1),
+                                      "frac_tensor": round(tf / peaks["bf16_tflops"], 3),
+                                      "flops": "4*D per visible (query, key) pair"}
     torch.cuda.empty_cache()
     return out
 
@@ -553,6 +565,8 @@ CASES = {
     "decode_B16": (16, H_Q, H_KV, 1, 4096, D),
     "decode_B64": (64, H_Q, H_KV, 1, 4096, D),
     "long_decode_C5": (1, H_Q, H_KV, 1, 131072, D),
+    "prefill_C2_causal": (1, H_Q, H_KV, S, S, D),
+    "prefill_C2_B8_causal": (8, H_Q, H_KV, S, S, D),
 }
 
 
@@ -574,10 +588,13 @@ def run_case(args):
     k = rand_f16((B, Hkv, Skv, Dh), gen, dev)
     v = rand_f16((B, Hkv, Skv, Dh), gen, dev)
     o = torch.empty((B, Hq, Sq, Dh), dtype=torch.float32, device=dev)
-    ms = time_loop(lambda i: flash_attn_fwd(q, k, v, out=o), args.steps, args.warmup, torch.cuda.current_stream(dev))
+    causal = args.case.endswith("_causal")
+    ms = time_loop(lambda i: flash_attn_fwd(q, k, v, out=o, causal=causal), args.steps, args.warmup,
+                   torch.cuda.current_stream(dev))
     line = {"case": args.case, "shape": [B, Hq, Hkv, Sq, Skv, Dh], "ms": round(ms, 5), "plan": plan(B, Hq, Hkv, Sq, Skv, Dh)}
     if Sq > 1:
-        line["TFLOP/s"] = round(prefill_flops(B, Hq, Sq, Skv, Dh) / (ms * 1e-3) / 1e12, 1)
+        fl = (causal_flops if causal else prefill_flops)(B, Hq, Sq, Skv, Dh)
+        line["TFLOP/s"] = round(fl / (ms * 1e-3) / 1e12, 1)
     else:
         line["GB/s"] = round(decode_bytes(B, Hq, Hkv, Skv, Dh) / (ms * 1e-3) / 1e9, 1)
     print(json.dumps(line), flush=True)

@@ -74,6 +74,21 @@ int kf_attn_fwd_lse(const void* Q, const void* K, const void* V, float* O,
                     int B, int H_q, int H_kv, int S_q, int S_kv, int D,
                     void* workspace, size_t workspace_bytes, void* stream);
 
+/* Flags for kf_attn_fwd_ex. */
+#define KF_FLAG_CAUSAL 1u   /* bottom-right causal mask (below) */
+
+/* kf_attn_fwd_lse with options (Mi/Li may be NULL).  KF_FLAG_CAUSAL: query row i
+ * of S_q sits at absolute position S_kv - S_q + i and attends keys
+ * j <= S_kv - S_q + i (chunked prefill over a KV cache; S_q == S_kv is the usual
+ * lower-triangular mask, S_q == 1 keeps every key); requires S_q <= S_kv, else
+ * KF_ERR_INVALID_ARG.  Unknown flag bits are KF_ERR_INVALID_ARG.  No reference
+ * counterpart: the reference has no mask and names it as required for decoder
+ * use (docs/flash_attn.md:105). */
+int kf_attn_fwd_ex(const void* Q, const void* K, const void* V,
+                   float* O, float* Mi, float* Li,
+                   int B, int H_q, int H_kv, int S_q, int S_kv, int D, unsigned flags,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
 /* Partial attention over the given K/V (e.g. one GPU's slice of a long KV
  * cache): O_u = sum_j exp(s_j - m) v_j (un-normalised), m = max_j s_j,
  * l = sum_j exp(s_j - m), with s_j the scaled scores.  Merge partials of

@@ -19,10 +19,12 @@ KF_ERR_DEVICE_TIMEOUT = 5
 KF_ERR_UNSUPPORTED_DEVICE = 6
 KF_ERR_WORKSPACE = 7
 
+KF_FLAG_CAUSAL = 1
+
 # Every symbol include/kf_attn.h declares.
 EXPORTED = [
     "kf_strerror", "kf_last_cuda_error", "kf_version",
-    "kf_attn_fwd", "kf_attn_fwd_lse", "kf_attn_fwd_partial", "kf_attn_combine", "kf_attn_combine_packed",
+    "kf_attn_fwd", "kf_attn_fwd_lse", "kf_attn_fwd_ex", "kf_attn_fwd_partial", "kf_attn_combine", "kf_attn_combine_packed",
     "kf_attn_workspace_bytes", "kf_attn_workspace_init", "kf_attn_plan",
     "kf_launch_flash_attn", "kf_attn_fwd_noalloc", "kf_device_error", "kf_set_wait_timeout_ns",
     "kf_selftest_wait_timeout",
@@ -62,6 +64,8 @@ def lib():
     L.kf_attn_fwd.restype = I
     L.kf_attn_fwd_lse.argtypes = [P, P, P, P, P, P, I, I, I, I, I, I, P, Z, P]
     L.kf_attn_fwd_lse.restype = I
+    L.kf_attn_fwd_ex.argtypes = [P, P, P, P, P, P, I, I, I, I, I, I, ctypes.c_uint, P, Z, P]
+    L.kf_attn_fwd_ex.restype = I
     L.kf_attn_fwd_partial.argtypes = [P, P, P, P, P, P, I, I, I, I, I, I, P, Z, P]
     L.kf_attn_fwd_partial.restype = I
     L.kf_attn_combine.argtypes = [P, P, P, I, P, P, P, I, I, I, I, P]

@@ -23,7 +23,7 @@ import threading
 
 import torch
 
-from ._lib import KFError, check, lib
+from ._lib import KF_FLAG_CAUSAL, KFError, check, lib
 
 __all__ = [
     "launch_flash_attn",
@@ -100,12 +100,14 @@ def plan(B, H_q, H_kv, S_q, S_kv, D, workspace_bytes=2**62):
     return {"path": "prefill" if path.value == 0 else "decode", "n_split": ns.value, "ctas": ctas.value}
 
 
-def flash_attn_fwd(q, k, v, *, out=None, return_lse=False, workspace=None):
+def flash_attn_fwd(q, k, v, *, out=None, return_lse=False, workspace=None, causal=False):
     """O = softmax(Q K^T / sqrt(D)) V per head; GQA head map h_kv = h_q // (H_q // H_kv).
 
     q [B,H_q,S_q,D] fp16, k/v [B,H_kv,S_kv,D] fp16 (CUDA, contiguous) ->
     O [B,H_q,S_q,D] fp32.  With ``return_lse`` also returns (Mi, Li), the
     reference kernel's row max of the scaled scores and sum of exp(s - Mi).
+    ``causal``: bottom-right causal mask, query i attends keys j <= S_kv - S_q + i
+    (needs S_q <= S_kv); an extension, the reference has no mask.
     """
     B, H_q, H_kv, S_q, S_kv, D = _check_qkv(q, k, v)
     dev = q.device
@@ -119,9 +121,10 @@ def flash_attn_fwd(q, k, v, *, out=None, return_lse=False, workspace=None):
         if workspace is None:
             workspace = _workspace(dev, workspace_bytes(B, H_q, H_kv, S_q, S_kv, D))
         wsb = workspace.numel() if workspace is not None else 0
-        rc = lib().kf_attn_fwd_lse(_ptr(q), _ptr(k), _ptr(v), _ptr(out), _ptr(Mi), _ptr(Li),
-                                   B, H_q, H_kv, S_q, S_kv, D, _ptr(workspace), wsb, _stream_handle(dev))
-    check(rc, "kf_attn_fwd_lse")
+        rc = lib().kf_attn_fwd_ex(_ptr(q), _ptr(k), _ptr(v), _ptr(out), _ptr(Mi), _ptr(Li),
+                                  B, H_q, H_kv, S_q, S_kv, D, KF_FLAG_CAUSAL if causal else 0,
+                                  _ptr(workspace), wsb, _stream_handle(dev))
+    check(rc, "kf_attn_fwd_ex")
     return (out, Mi, Li) if return_lse else out
 
 

@@ -213,9 +213,11 @@ int decode_bps(int D, int mt, int* bps) {
 }
 
 int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_bytes, int sm_count,
-              int blocks_per_sm, Plan* pl) {
+              int blocks_per_sm, Plan* pl, bool causal = false) {
     const int G = H_q / H_kv;
-    if (!use_decode(G, S_q, D)) {
+    // Causal with several query rows takes the prefill kernel (the decode kernel has
+    // no per-row mask); with one row the mask keeps every key, so decode is exact.
+    if (!use_decode(G, S_q, D) || (causal && S_q > 1)) {
         pl->path = 0;
         const int rows_per_cta = (D <= 128 ? 2 : 1) * 128;
         const int bc = D <= 128 ? 128 : 64;
@@ -229,7 +231,7 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
         const int cap = sm_count;
         const int rem = static_cast<int>(units % cap);
         const int n_kv = (S_kv + bc - 1) / bc;
-        int k = rem > 0 ? cap / rem : 1;
+        int k = (rem > 0 && !causal) ? cap / rem : 1;   // causal units differ in size: no split
         k = k > 4 ? 4 : k;
         k = k > n_kv / 2 ? n_kv / 2 : k;
         if (k >= 2) {
@@ -303,28 +305,31 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
     return KF_OK;
 }
 
-int plan_for_call(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_bytes, Plan* pl) {
+int plan_for_call(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_bytes, Plan* pl,
+                  bool causal = false) {
     DeviceInfo* di = nullptr;
     int rc = device_info(&di);
     if (rc != KF_OK) return rc;
     const int G = H_q / H_kv;
     int bps = 1;
-    if (use_decode(G, S_q, D)) {
+    if (use_decode(G, S_q, D) && !(causal && S_q > 1)) {
         const int R = G * S_q;
         const int mt = R <= 16 ? 1 : decode_max_mt(D);
         rc = decode_bps(D, mt, &bps);
         if (rc != KF_OK) return rc;
     }
-    return make_plan(B, H_q, H_kv, S_q, S_kv, D, ws_bytes, di->sm_count, bps, pl);
+    return make_plan(B, H_q, H_kv, S_q, S_kv, D, ws_bytes, di->sm_count, bps, pl, causal);
 }
 
 // ------------------------------------------------------------------ launches
 template <int D>
 int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, float* O, float* Mi, float* Li,
-                   int unnorm, int B, int H_q, int H_kv, int S_q, int S_kv, void* ws, cudaStream_t s) {
+                   int unnorm, int B, int H_q, int H_kv, int S_q, int S_kv, void* ws, cudaStream_t s,
+                   bool causal) {
     using C = kf::PrefillCfg<D>;
     int bps = 0;
-    int rc = kernel_setup<kf::prefill_fwd_kernel<D>>(C::SMEM_BYTES, C::THREADS, &bps);
+    int rc = causal ? kernel_setup<kf::prefill_fwd_kernel<D, true>>(C::SMEM_BYTES, C::THREADS, &bps)
+                    : kernel_setup<kf::prefill_fwd_kernel<D, false>>(C::SMEM_BYTES, C::THREADS, &bps);
     if (rc != KF_OK) return rc;
     // A TMA box may not exceed the tensor: short sequences load S rows and the
     // kernel keeps the remaining tile rows zero.
@@ -357,6 +362,8 @@ int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, 
     p.q_box = q_box;
     p.kv_box = kv_box;
     p.n_qblk = pl.pf_qblk;
+    p.B_H = B * H_q;
+    p.kv_off = S_kv - S_q;
     p.n_units = pl.pf_units;
     p.n_plain = pl.pf_plain;
     p.split_k = pl.pf_k;
@@ -371,7 +378,10 @@ int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, 
     }
     const long long ctas = pl.ctas;
     if (ctas <= 0 || ctas > 0x7fffffffll) return KF_ERR_INVALID_ARG;
-    kf::prefill_fwd_kernel<D><<<static_cast<unsigned>(ctas), C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, mo, mp, p);
+    if (causal)
+        kf::prefill_fwd_kernel<D, true><<<static_cast<unsigned>(ctas), C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, mo, mp, p);
+    else
+        kf::prefill_fwd_kernel<D, false><<<static_cast<unsigned>(ctas), C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, mo, mp, p);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KF_OK : cuda_fail(e);
 }
@@ -430,21 +440,25 @@ int launch_decode(const Plan& pl, int D, const void* Q, const void* K, const voi
 }
 
 int attn_core(const void* Q, const void* K, const void* V, float* O, float* Mi, float* Li, int unnorm, int B,
-              int H_q, int H_kv, int S_q, int S_kv, int D, void* ws, size_t ws_bytes, void* stream) {
+              int H_q, int H_kv, int S_q, int S_kv, int D, void* ws, size_t ws_bytes, void* stream,
+              unsigned flags = 0) {
     int rc = validate(Q, K, V, O, B, H_q, H_kv, S_q, S_kv, D);
     if (rc != KF_OK) return rc;
+    if (flags & ~static_cast<unsigned>(KF_FLAG_CAUSAL)) return KF_ERR_INVALID_ARG;
+    const bool causal = (flags & KF_FLAG_CAUSAL) != 0;
+    if (causal && S_q > S_kv) return KF_ERR_INVALID_ARG;   // rows with no visible key
     if (B == 0 || S_q == 0) return KF_OK;
     if (!ws) ws_bytes = 0;
     if (ws && !aligned16(ws)) return KF_ERR_MISALIGNED;
     Plan pl;
-    if ((rc = plan_for_call(B, H_q, H_kv, S_q, S_kv, D, ws_bytes, &pl)) != KF_OK) return rc;
+    if ((rc = plan_for_call(B, H_q, H_kv, S_q, S_kv, D, ws_bytes, &pl, causal)) != KF_OK) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (pl.path == 0) {
         switch (D) {
-            case 16: return launch_prefill<16>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s);
-            case 64: return launch_prefill<64>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s);
-            case 128: return launch_prefill<128>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s);
-            default: return launch_prefill<256>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s);
+            case 16: return launch_prefill<16>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s, causal);
+            case 64: return launch_prefill<64>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s, causal);
+            case 128: return launch_prefill<128>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s, causal);
+            default: return launch_prefill<256>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s, causal);
         }
     }
     return launch_decode(pl, D, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, pl.n_split > 1 ? ws : nullptr, s);
@@ -516,6 +530,12 @@ int kf_attn_fwd(const void* Q, const void* K, const void* V, float* O, int B, in
 int kf_attn_fwd_lse(const void* Q, const void* K, const void* V, float* O, float* Mi, float* Li, int B, int H_q,
                     int H_kv, int S_q, int S_kv, int D, void* workspace, size_t workspace_bytes, void* stream) {
     return attn_core(Q, K, V, O, Mi, Li, 0, B, H_q, H_kv, S_q, S_kv, D, workspace, workspace_bytes, stream);
+}
+
+int kf_attn_fwd_ex(const void* Q, const void* K, const void* V, float* O, float* Mi, float* Li, int B, int H_q,
+                   int H_kv, int S_q, int S_kv, int D, unsigned flags, void* workspace, size_t workspace_bytes,
+                   void* stream) {
+    return attn_core(Q, K, V, O, Mi, Li, 0, B, H_q, H_kv, S_q, S_kv, D, workspace, workspace_bytes, stream, flags);
 }
 
 int kf_attn_fwd_partial(const void* Q, const void* K, const void* V, float* O_u, float* m, float* l, int B, int H_q,

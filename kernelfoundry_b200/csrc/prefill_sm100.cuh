@@ -88,6 +88,7 @@ struct PrefillParams {
     float* Mi;   // nullable
     float* Li;   // nullable
     int H_q, H_kv, S_q, S_kv, G;
+    int B_H;            // B * H_q
     float scale_log2;   // (1/sqrt(D)) * log2(e)
     float scale;        // 1/sqrt(D)
     int unnormalized;   // 1: write O_u = sum exp(s - Mi) v (partial form), Mi/Li required
@@ -99,6 +100,7 @@ struct PrefillParams {
     // each taking `per` KV tiles, which write softmax partials to `part` and the
     // last to finish (ticket in `counters`) merges them into O.
     int n_qblk;         // 256-row blocks per (b, h_q)
+    int kv_off;         // S_kv - S_q (>= 0); causal kernels: query i sees keys j <= i + kv_off
     int n_units, n_plain, split_k, per;
     float* part;        // [n_units - n_plain][split_k][NQ*BM][D + 2]
     unsigned* counters; // one ticket per split unit, zero between calls
@@ -120,7 +122,9 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, 
     return mbar_wait_bounded(bar, parity, &dummy, timeout_ns);
 }
 
-template <int D>
+// CAUSAL: bottom-right causal mask (PrefillParams::kv_off); a separate instantiation
+// so the unmasked kernel carries none of its registers.
+template <int D, bool CAUSAL>
 __global__ void __launch_bounds__(PrefillCfg<D>::THREADS, 1)
 prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
@@ -160,16 +164,23 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         chunk = (cta - p.n_plain) % p.split_k;
     }
     const bool split = unit >= p.n_plain;
-    const int qblk = unit % p.n_qblk;
-    const int h = (unit / p.n_qblk) % p.H_q;
-    const int b = unit / (p.n_qblk * p.H_q);
+    // Causal: heaviest query blocks (most visible keys) first, (b, h) fastest, so the
+    // long units start in the first wave; otherwise the query block is fastest.
+    const int qblk = CAUSAL ? p.n_qblk - 1 - unit / p.B_H : unit % p.n_qblk;
+    const int h = CAUSAL ? (unit % p.B_H) % p.H_q : (unit / p.n_qblk) % p.H_q;
+    const int b = CAUSAL ? (unit % p.B_H) / p.H_q : unit / (p.n_qblk * p.H_q);
     const int h_kv = h / p.G;
     const int q_row0 = qblk * NQ * BM;
     const int rows_left = p.S_q - q_row0;
     const int nq_active = rows_left >= NQ * BM ? NQ : (rows_left + BM - 1) / BM;
     const int n_kv_all = (p.S_kv + BC - 1) / BC;
     const int kt0 = split ? chunk * p.per : 0;                                  // first KV tile
-    const int n_kv = split ? min(p.per, n_kv_all - kt0) : n_kv_all;            // KV tiles of this CTA
+    int n_kv = split ? min(p.per, n_kv_all - kt0) : n_kv_all;                  // KV tiles of this CTA
+    if constexpr (CAUSAL) {
+        // Keys up to the unit's last (valid) query row + kv_off; the split path is off.
+        const int last_row = min(q_row0 + NQ * BM, p.S_q) - 1;
+        n_kv = min(n_kv_all, (last_row + p.kv_off) / BC + 1);
+    }
 
     if (threadIdx.x == 0) {
         for (int t = 0; t < NQ; ++t) {
@@ -361,6 +372,8 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             const uint32_t tS = tl + t * BC;
             const uint32_t tO = tl + NQ * BC + t * D;
             const float c = p.scale_log2;
+            // Causal: keys of tile j visible to this row are those below diag - j*BC.
+            const int diag = CAUSAL ? q_row0 + t * BM + row + p.kv_off - kt0 * BC + 1 : 0;
             float m_ref = -CUDART_INF_F, m_true = -CUDART_INF_F, l = 0.f;
             bool ok = true;
             for (int j = 0; j < n_kv; ++j) {
@@ -373,7 +386,10 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 for (int cc = 0; cc < BC / 32; ++cc)
                     tmem_ld32(tS + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[cc * 32]));
                 tmem_wait_ld();
-                const int kv_valid = p.S_kv - (kt0 + j) * BC;
+                // Keys of this tile visible to this row: past S_kv (ragged end) and, with
+                // the causal mask, past the row's diagonal read as -inf.
+                int kv_valid = p.S_kv - (kt0 + j) * BC;
+                if constexpr (CAUSAL) kv_valid = min(kv_valid, diag - j * BC);
                 if (kv_valid < BC) {
 #pragma unroll
                     for (int cc = 0; cc < BC; ++cc)

@@ -90,6 +90,44 @@ def reference_attn_lse(Q: np.ndarray, K: np.ndarray, V: np.ndarray):
     return O, Mi, Li
 
 
+def causal_attn_lse(Q: np.ndarray, K: np.ndarray, V: np.ndarray):
+    """Causal (O, Mi, Li): extension with no reference counterpart -- the reference
+    lists the missing causal mask as the gap for decoder use (docs/flash_attn.md:105).
+
+    Bottom-right aligned, as in chunked prefill over a KV cache: query row i of S_q
+    sits at absolute position S_kv - S_q + i and attends keys j <= S_kv - S_q + i.
+    Every row sees at least key 0 when S_q <= S_kv (required).  Same scores, Mi and
+    Li as reference_attn_lse restricted to the visible keys.
+    """
+    B, H_q, H_kv, D = _check_shapes(Q, K, V)
+    S_q, S_kv = Q.shape[2], K.shape[2]
+    if S_q > S_kv:
+        raise ValueError("causal attention needs S_q <= S_kv")
+    gqa = H_q // H_kv
+    scale = 1.0 / np.sqrt(float(D))
+    visible = np.arange(S_kv)[None, :] <= (S_kv - S_q + np.arange(S_q))[:, None]     # [S_q, S_kv]
+    O = np.zeros_like(Q)
+    Mi = np.zeros((B, H_q, S_q), dtype=Q.dtype)
+    Li = np.zeros((B, H_q, S_q), dtype=Q.dtype)
+    for b in range(B):
+        for h in range(H_q):
+            hk = h // gqa
+            scores = np.where(visible, Q[b, h] @ K[b, hk].T * scale, -np.inf)
+            m = scores.max(axis=-1, keepdims=True)
+            P = np.exp(scores - m)
+            l = P.sum(axis=-1, keepdims=True)
+            O[b, h] = (P / l) @ V[b, hk]
+            Mi[b, h] = m[:, 0]
+            Li[b, h] = l[:, 0]
+    return O, Mi, Li
+
+
+def causal_pairs(S_q: int, S_kv: int) -> int:
+    """Number of visible (query, key) pairs under the bottom-right causal mask."""
+    off = S_kv - S_q
+    return sum(min(S_kv, off + i + 1) for i in range(S_q))
+
+
 def attn_partial(Q: np.ndarray, K: np.ndarray, V: np.ndarray, kv_lo: int, kv_hi: int):
     """Softmax partials over keys [kv_lo, kv_hi).
 

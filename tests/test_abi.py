@@ -94,6 +94,12 @@ def test_argument_validation_without_gpu(kf_lib):
     assert kf_lib.kf_attn_combine(FAKE, FAKE, FAKE, 2, FAKE, None, None, 1, 4, 8, 48, None) \
         == L.KF_ERR_UNSUPPORTED_HEAD_DIM
     assert kf_lib.kf_attn_combine(FAKE, FAKE, FAKE, 2, FAKE, None, None, 0, 4, 8, 64, None) == L.KF_OK
+    # kf_attn_fwd_ex: unknown flag bits and causal with S_q > S_kv are rejected before any launch.
+    assert kf_lib.kf_attn_fwd_ex(FAKE, FAKE, FAKE, FAKE, None, None, 1, 4, 2, 8, 8, 64, 2, None, 0, None) \
+        == L.KF_ERR_INVALID_ARG
+    assert kf_lib.kf_attn_fwd_ex(FAKE, FAKE, FAKE, FAKE, None, None, 1, 4, 2, 9, 8, 64, L.KF_FLAG_CAUSAL, None, 0,
+                                 None) == L.KF_ERR_INVALID_ARG
+    assert kf_lib.kf_attn_fwd_ex(FAKE, FAKE, FAKE, FAKE, None, None, 0, 4, 2, 9, 8, 64, 0, None, 0, None) == L.KF_OK
     # Packed combine: part stride below rows*(D+2) or not a multiple of 4 is rejected before any launch.
     assert kf_lib.kf_attn_combine_packed(FAKE, 4 * 8 * 66 - 4, 2, FAKE, None, None, 1, 4, 8, 64, None) \
         == L.KF_ERR_INVALID_ARG

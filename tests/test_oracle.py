@@ -129,3 +129,30 @@ def test_planted_mistake_is_caught(sdpa_golden):
         wrong[0, h] = (p / p.sum(-1, keepdims=True)) @ V[0, h % H_kv]
     max_abs, _ = error_stats(wrong, sdpa_golden[f"{name}/O_ref64"])
     assert max_abs > 1e-2
+
+
+def test_causal_oracle_against_independent_forms():
+    """The causal restatement agrees with (1) torch SDPA is_causal in fp64 for S_q == S_kv
+    (an independent implementation) and (2) per-row plain attention over the visible keys
+    for S_q < S_kv (bottom-right alignment)."""
+    import torch
+
+    from oracle.attn_oracle import causal_attn_lse, causal_pairs, normal_qkv, reference_attn_lse
+
+    Q, K, V = (x.astype(np.float64) for x in normal_qkv(1, 4, 2, 33, 33, 16, seed=5))
+    O, Mi, Li = causal_attn_lse(Q, K, V)
+    Kr = np.repeat(K, 2, axis=1)
+    Vr = np.repeat(V, 2, axis=1)
+    ref = torch.nn.functional.scaled_dot_product_attention(
+        torch.from_numpy(Q), torch.from_numpy(Kr), torch.from_numpy(Vr), is_causal=True).numpy()
+    assert np.abs(O - ref).max() < 1e-12
+    Q, K, V = (x.astype(np.float64) for x in normal_qkv(1, 2, 1, 5, 19, 16, seed=6))
+    O, Mi, Li = causal_attn_lse(Q, K, V)
+    for i in range(5):
+        hi = 19 - 5 + i + 1
+        o, mi, li = reference_attn_lse(Q[:, :, i:i + 1], K[:, :, :hi], V[:, :, :hi])
+        assert np.abs(O[:, :, i:i + 1] - o).max() < 1e-12
+        assert np.abs(Mi[:, :, i] - mi[:, :, 0]).max() < 1e-12 and np.abs(Li[:, :, i] - li[:, :, 0]).max() < 1e-12
+    assert causal_pairs(4, 4) == 10 and causal_pairs(2, 5) == 4 + 5
+    with pytest.raises(ValueError):
+        causal_attn_lse(*normal_qkv(1, 1, 1, 5, 4, 16, seed=1))

@@ -169,3 +169,37 @@ def test_matches_reference_cuda_kernel(cuda, shape):
     assert ma <= 2e-3 and rl <= 1e-3, (ma, rl)
     assert np.abs(Mi - ref_mi).max() < 1e-3
     assert np.abs(Li / ref_li - 1).max() < 1e-3
+
+
+CAUSAL = [
+    (1, 32, 8, 4096, 4096, 128),      # C2 with the mask
+    (2, 8, 2, 300, 1000, 128),        # chunk of 300 queries at the end of a 1000-key cache
+    (1, 4, 1, 129, 129, 64),
+    (1, 2, 1, 257, 300, 256),
+    (1, 2, 2, 1000, 1000, 16),
+    (1, 32, 8, 7, 2048, 128),         # few queries: decode-sized, but the mask needs the prefill kernel
+    (3, 8, 8, 1, 777, 128),           # one query sees every key: decode kernel, same as unmasked
+]
+
+
+@pytest.mark.parametrize("shape", CAUSAL, ids=lambda s: "B{}_Hq{}_Hkv{}_Sq{}_Skv{}_D{}".format(*s))
+def test_causal_matches_oracle(cuda, shape):
+    from oracle.attn_oracle import causal_attn_lse
+
+    from kernelfoundry_b200 import flash_attn_fwd
+
+    Q, K, V = normal_qkv(*shape, seed=11 * sum(shape))
+    got, Mi, Li = (t.cpu().numpy() for t in flash_attn_fwd(*(to_dev(x, cuda) for x in (Q, K, V)),
+                                                            causal=True, return_lse=True))
+    O, rMi, rLi = causal_attn_lse(*(x.astype(np.float64) for x in (Q, K, V)))
+    assert_close(got, O, f"causal {shape}")
+    assert np.abs(Mi - rMi).max() < 1e-3
+    assert np.abs(Li / rLi - 1).max() < 1e-3
+
+
+def test_causal_rejects_more_queries_than_keys(cuda):
+    from kernelfoundry_b200 import KFError, flash_attn_fwd
+
+    Q, K, V = normal_qkv(1, 2, 1, 65, 64, 64, seed=1)
+    with pytest.raises(KFError):
+        flash_attn_fwd(*(to_dev(x, cuda) for x in (Q, K, V)), causal=True)
