@@ -353,6 +353,7 @@ def run_extras(args, rank, world, dev, peaks):
     ms, rot, pl = bench_cfg(1, H_Q, H_KV, 512, 512, D)
     tf = prefill_flops(1, H_Q, 512, 512, D) / (ms * 1e-3) / 1e12
     out["prefill_S512_B1"] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 1)}
+    out.update(bench_paged(stream, gen, dev, peaks, l2, iters))
     ms, rot, pl = bench_cfg(1, H_Q, H_KV, S, S, D, causal=True)
     tf = causal_flops(1, H_Q, S, S, D) / (ms * 1e-3) / 1e12
     out["prefill_causal_S4096_B1"] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 1),
@@ -360,6 +361,42 @@ def run_extras(args, rank, world, dev, peaks):
                                       "flops": "4*D per visible (query, key) pair"}
     torch.cuda.empty_cache()
     return out
+
+
+def bench_paged(stream, gen, dev, peaks, l2, iters):
+    """Decode B=16 KV=4096 over a paged cache (block 16, randomly permuted pages), as
+    the reference's paged benchmark lays it out; same bytes formula as contiguous decode."""
+    import torch
+
+    from kernelfoundry_b200 import flash_attn_paged
+
+    B, bs = 16, 16
+    nb = S // bs
+    one = 2 * B * nb * H_KV * bs * D * 2
+    rot = max(1, min(8, -(-2 * l2 // one) + 1))
+    sets = []
+    for r in range(rot):
+        pk = rand_f16((B * nb + 7, H_KV, bs, D), gen, dev)
+        pv = rand_f16((B * nb + 7, H_KV, bs, D), gen, dev)
+        perm = torch.randperm(B * nb + 7, generator=torch.Generator().manual_seed(r))[:B * nb]
+        table = perm.to(torch.int32).reshape(B, nb).to(dev)
+        seq = torch.full((B,), S, dtype=torch.int32, device=dev)
+        q = rand_f16((B, H_Q, 1, D), gen, dev)
+        o = torch.empty((B, H_Q, 1, D), dtype=torch.float32, device=dev)
+        sets.append((q, pk, pv, table, seq, o))
+
+    def f(i):
+        q, pk, pv, table, seq, o = sets[i % rot]
+        flash_attn_paged(q, pk, pv, table, seq, out=o)
+
+    host_ms = time_loop(f, iters, 3, stream)
+    n_calls = rot * max(1, 8 // rot)
+    ms = time_graph(f, n_calls, max(2, iters // n_calls), stream)
+    gbs = decode_bytes(B, H_Q, H_KV, S, D) / (ms * 1e-3) / 1e9
+    del sets
+    return {"paged_decode_kv4096_B16_bs16": {"us": round(ms * 1e3, 2), "GB/s": round(gbs, 1),
+                                             "frac_hbm": round(gbs / peaks["hbm_gbs"], 3),
+                                             "host_call_us": round(host_ms * 1e3, 2), "rotated_sets": rot}}
 
 
 def run_long_decode_split(args, rank, world, dev, peaks):

@@ -89,6 +89,27 @@ int kf_attn_fwd_ex(const void* Q, const void* K, const void* V,
                    int B, int H_q, int H_kv, int S_q, int S_kv, int D, unsigned flags,
                    void* workspace, size_t workspace_bytes, void* stream);
 
+/* Decode over a paged KV cache (decode shapes: H_q/H_kv * S_q as for the decode
+ * kernel, else KF_ERR_INVALID_ARG).  Pools K_pool/V_pool are fp16
+ * [n_blocks][H_kv][block_size][D] (the layout of the reference's paged
+ * benchmark, reference_benchmarks/bench_flash_attn2.py:153-215); logical block j
+ * of sequence b lives at pool block block_table[b*max_blocks + j] (int32);
+ * sequence b has seq_lens[b] keys (int32, device memory, clamped to
+ * [0, max_blocks*block_size]; 0 gives O = 0).  block_size is a power of two in
+ * [16, 256].  Q/O/Mi/Li as kf_attn_fwd_lse (non-causal: every query row sees the
+ * sequence's keys).  Table entries past a sequence's last block are not read; an
+ * entry outside [0, n_blocks) reads zeros.  Workspace as kf_attn_fwd, sized by
+ * kf_attn_paged_workspace_bytes.  The reference has only the gather-then-attend
+ * path; this reads the pages inside the kernel. */
+int kf_attn_fwd_paged(const void* Q, const void* K_pool, const void* V_pool,
+                      const int* block_table, const int* seq_lens,
+                      float* O, float* Mi, float* Li,
+                      int B, int H_q, int H_kv, int S_q, int D,
+                      int n_blocks, int block_size, int max_blocks,
+                      void* workspace, size_t workspace_bytes, void* stream);
+size_t kf_attn_paged_workspace_bytes(int B, int H_q, int H_kv, int S_q, int D,
+                                     int block_size, int max_blocks);
+
 /* Partial attention over the given K/V (e.g. one GPU's slice of a long KV
  * cache): O_u = sum_j exp(s_j - m) v_j (un-normalised), m = max_j s_j,
  * l = sum_j exp(s_j - m), with s_j the scaled scores.  Merge partials of

@@ -16,6 +16,7 @@ from .attention import (  # noqa: F401
     combine_partials,
     device_error,
     flash_attn_fwd,
+    flash_attn_paged,
     flash_attn_partial,
     launch_flash_attn,
     plan,

@@ -24,7 +24,7 @@ KF_FLAG_CAUSAL = 1
 # Every symbol include/kf_attn.h declares.
 EXPORTED = [
     "kf_strerror", "kf_last_cuda_error", "kf_version",
-    "kf_attn_fwd", "kf_attn_fwd_lse", "kf_attn_fwd_ex", "kf_attn_fwd_partial", "kf_attn_combine", "kf_attn_combine_packed",
+    "kf_attn_fwd", "kf_attn_fwd_lse", "kf_attn_fwd_ex", "kf_attn_fwd_paged", "kf_attn_paged_workspace_bytes", "kf_attn_fwd_partial", "kf_attn_combine", "kf_attn_combine_packed",
     "kf_attn_workspace_bytes", "kf_attn_workspace_init", "kf_attn_plan",
     "kf_launch_flash_attn", "kf_attn_fwd_noalloc", "kf_device_error", "kf_set_wait_timeout_ns",
     "kf_selftest_wait_timeout",
@@ -66,6 +66,10 @@ def lib():
     L.kf_attn_fwd_lse.restype = I
     L.kf_attn_fwd_ex.argtypes = [P, P, P, P, P, P, I, I, I, I, I, I, ctypes.c_uint, P, Z, P]
     L.kf_attn_fwd_ex.restype = I
+    L.kf_attn_fwd_paged.argtypes = [P, P, P, P, P, P, P, P, I, I, I, I, I, I, I, I, P, Z, P]
+    L.kf_attn_fwd_paged.restype = I
+    L.kf_attn_paged_workspace_bytes.argtypes = [I, I, I, I, I, I, I]
+    L.kf_attn_paged_workspace_bytes.restype = Z
     L.kf_attn_fwd_partial.argtypes = [P, P, P, P, P, P, I, I, I, I, I, I, P, Z, P]
     L.kf_attn_fwd_partial.restype = I
     L.kf_attn_combine.argtypes = [P, P, P, I, P, P, P, I, I, I, I, P]

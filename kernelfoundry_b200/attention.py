@@ -31,6 +31,7 @@ __all__ = [
     "flash_attn_partial",
     "combine_partials",
     "combine_packed",
+    "flash_attn_paged",
     "plan",
     "workspace_bytes",
     "device_error",
@@ -152,6 +153,45 @@ def flash_attn_partial(q, k, v, *, workspace=None, out=None):
                                        B, H_q, H_kv, S_q, S_kv, D, _ptr(workspace), wsb, _stream_handle(dev))
     check(rc, "kf_attn_fwd_partial")
     return O_u, m, l
+
+
+def flash_attn_paged(q, k_pool, v_pool, block_table, seq_lens, *, out=None, return_lse=False, workspace=None):
+    """Decode attention over a paged KV cache.
+
+    q [B,H_q,S_q,D] fp16; k_pool/v_pool [n_blocks,H_kv,block_size,D] fp16;
+    block_table [B,max_blocks] int32 (pool block of each logical block);
+    seq_lens [B] int32 (keys per sequence).  Every query row sees its sequence's
+    keys (decode shapes: H_q/H_kv * S_q small).  -> O [B,H_q,S_q,D] fp32."""
+    for t, name in ((q, "q"), (k_pool, "k_pool"), (v_pool, "v_pool")):
+        if not t.is_cuda or t.dtype != torch.float16 or not t.is_contiguous() or t.dim() != 4:
+            raise ValueError(f"{name} must be a contiguous 4-D fp16 CUDA tensor (no CPU path)")
+    for t, name, nd in ((block_table, "block_table", 2), (seq_lens, "seq_lens", 1)):
+        if not t.is_cuda or t.dtype != torch.int32 or not t.is_contiguous() or t.dim() != nd:
+            raise ValueError(f"{name} must be a contiguous {nd}-D int32 CUDA tensor")
+    B, H_q, S_q, D = q.shape
+    n_blocks, H_kv, block_size, D2 = k_pool.shape
+    if tuple(v_pool.shape) != tuple(k_pool.shape) or D2 != D:
+        raise ValueError("pool shapes must match [n_blocks, H_kv, block_size, D]")
+    if block_table.shape[0] != B or seq_lens.shape[0] != B:
+        raise ValueError("block_table / seq_lens must have B rows")
+    max_blocks = block_table.shape[1]
+    dev = q.device
+    if out is None:
+        out = torch.empty((B, H_q, S_q, D), dtype=torch.float32, device=dev)
+    Mi = Li = None
+    if return_lse:
+        Mi = torch.empty((B, H_q, S_q), dtype=torch.float32, device=dev)
+        Li = torch.empty_like(Mi)
+    with torch.cuda.device(dev):
+        if workspace is None:
+            workspace = _workspace(dev, int(lib().kf_attn_paged_workspace_bytes(B, H_q, H_kv, S_q, D, block_size,
+                                                                                max_blocks)))
+        wsb = workspace.numel() if workspace is not None else 0
+        rc = lib().kf_attn_fwd_paged(_ptr(q), _ptr(k_pool), _ptr(v_pool), _ptr(block_table), _ptr(seq_lens),
+                                     _ptr(out), _ptr(Mi), _ptr(Li), B, H_q, H_kv, S_q, D, n_blocks, block_size,
+                                     max_blocks, _ptr(workspace), wsb, _stream_handle(dev))
+    check(rc, "kf_attn_fwd_paged")
+    return (out, Mi, Li) if return_lse else out
 
 
 def combine_packed(parts, n_parts, part_stride, shape, *, out=None, return_lse=False):

@@ -70,9 +70,17 @@ struct DecodeParams {
     int unnormalized;
     int kv_box;            // rows per K/V TMA box: min(TK, S_kv)
     unsigned long long timeout_ns;
+    // Paged KV (PAGED kernels): K/V pools [n_blocks][H_kv][block_size][D], logical
+    // block j of sequence b at pool block block_table[b * max_blocks + j], and
+    // seq_lens[b] keys in sequence b (clamped to [0, max_blocks * block_size]).
+    const int* block_table;
+    const int* seq_lens;
+    int max_blocks, block_size;
 };
 
-template <int D, int MT>
+// PAGED: K/V come from block pools through a per-sequence block table (the maps
+// are 3-D over (D, block_size, n_blocks * H_kv)); sequences have their own lengths.
+template <int D, int MT, bool PAGED = false>
 __global__ void __launch_bounds__(DecodeCfg<D, MT>::THREADS)
 decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                   const DecodeParams p) {
@@ -101,8 +109,10 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
     // Global row index (over B*H_q*S_q) of this CTA's local row 0.
     const size_t row_base = (static_cast<size_t>(b) * p.H_q + static_cast<size_t>(hk) * p.G) * p.S_q + r0;
     const int kv_lo = split * p.chunk;
-    const int kv_hi = min(p.S_kv, kv_lo + p.chunk);
-    const int n_st = (kv_hi - kv_lo + TK - 1) / TK;
+    int S_b = p.S_kv;                          // keys of this sequence
+    if constexpr (PAGED) S_b = min(max(__ldg(p.seq_lens + b), 0), p.max_blocks * p.block_size);
+    const int kv_hi = min(S_b, kv_lo + p.chunk);
+    const int n_st = kv_hi > kv_lo ? (kv_hi - kv_lo + TK - 1) / TK : 0;   // 0: an empty split
     const float c = p.scale_log2;
 
     if (tid == 0) {
@@ -145,7 +155,67 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         for (int n = 0; n < D / 8; ++n) o[mt][n][0] = o[mt][n][1] = o[mt][n][2] = o[mt][n][3] = 0.f;
     }
 
-    if (warp == NW) {
+    if (warp == NW && PAGED) {
+        // ------------------------------------------------------------ TMA producer (paged)
+        // The whole warp walks the stages; lanes hold the pool-block ids of 32
+        // consecutive logical blocks (one coalesced load), lane 0 issues the copies.
+        if (lane == 0) {
+            tma_prefetch_desc(&tmK);
+            tma_prefetch_desc(&tmV);
+        }
+        const uint64_t pol = l2_policy_evict_first();
+        const int BS = p.block_size;
+        const int box = BS < TK ? BS : TK;
+        const int n_blk = BS < TK ? TK / BS : 1;                 // pool blocks per stage
+        const int used_blocks = (S_b + BS - 1) / BS;             // logical blocks holding keys
+        const int* bt = p.block_table + static_cast<size_t>(b) * p.max_blocks;
+        int cache_base = -(1 << 30), cache_val = -1;
+        int issued = 0;
+        for (int i = 0; i < n_st; ++i) {
+            const int slot = i % NSTAGE, round = i / NSTAGE;
+            bool ok = true;
+            if (round > 0 && lane == 0)
+                ok = mbar_wait_bounded(&empty[slot], (round - 1) & 1, abort_flag, p.timeout_ns);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) {
+                if (lane == 0) atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_SOFTMAX);
+                break;
+            }
+            const int row = kv_lo + i * TK;
+            const int lb0 = row / BS;
+            const int r_in = BS < TK ? 0 : row % BS;
+            if (lb0 < cache_base || lb0 + n_blk > cache_base + 32) {
+                cache_base = lb0;
+                const int lb = lb0 + lane;
+                // Blocks past the sequence's last one read as -1: the copy then starts at
+                // a negative coordinate and fills zeros (the table there may be stale).
+                cache_val = lb < used_blocks ? __ldg(bt + lb) : -1;
+            }
+            if (lane == 0) mbar_arrive_expect_tx(&full[slot], 2 * NSPAN * TK * SWB);
+            uint8_t* dK = sBig + slot * C::STAGE_BYTES;
+            uint8_t* dV = dK + C::TILE_BYTES;
+            for (int k = 0; k < n_blk; ++k) {
+                const int pb = __shfl_sync(0xffffffffu, cache_val, lb0 + k - cache_base);
+                if (lane == 0) {
+                    const int c2 = pb * p.H_kv + hk;
+#pragma unroll
+                    for (int s2 = 0; s2 < NSPAN; ++s2) {
+                        // Rows k*box .. of the stage: a multiple of 8 rows keeps the swizzle
+                        // pattern of one whole-tile box.
+                        tma_load_3d_hint(dK + s2 * TK * SWB + k * box * SWB, &tmK, &full[slot], s2 * SWE, r_in, c2, pol);
+                        tma_load_3d_hint(dV + s2 * TK * SWB + k * box * SWB, &tmV, &full[slot], s2 * SWE, r_in, c2, pol);
+                    }
+                }
+            }
+            issued = i + 1;
+        }
+        if (lane == 0 && *abort_flag) {
+            const int first = issued > NSTAGE ? issued - NSTAGE : 0;
+            int dummy = 0;
+            for (int i = first; i < issued; ++i)
+                mbar_wait_bounded(&full[i % NSTAGE], (i / NSTAGE) & 1, &dummy, p.timeout_ns);
+        }
+    } else if (warp == NW) {
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
             tma_prefetch_desc(&tmK);
@@ -264,6 +334,14 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
                 const int vrow = warp * 16 + lr + ((lm & 1) << 3);
                 const int vcol = dp * 16 + ((lm >> 1) << 3);
                 ldmatrix_x4_trans(sV + swz_offset<SWB>(TK, vrow, vcol), b0a, b1a, b0b, b1b);
+                if (PAGED && i == n_st - 1) {
+                    // P is 0 for keys past the end, but 0 * (Inf or NaN) is not: clear the V
+                    // halves of those keys (this lane's keys 2cq, 2cq+1, 2cq+8, 2cq+9).
+                    const int k0 = kv_lo + i * TK + warp * 16 + 2 * cq;
+                    const uint32_t m0 = (k0 < kv_hi ? 0x0000ffffu : 0u) | (k0 + 1 < kv_hi ? 0xffff0000u : 0u);
+                    const uint32_t m1 = (k0 + 8 < kv_hi ? 0x0000ffffu : 0u) | (k0 + 9 < kv_hi ? 0xffff0000u : 0u);
+                    b0a &= m0; b0b &= m0; b1a &= m1; b1b &= m1;
+                }
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt) {
                     mma_16816(o[mt][2 * dp], pa[mt][0], pa[mt][1], pa[mt][2], pa[mt][3], b0a, b1a);
@@ -332,7 +410,7 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
                 const float4 v = *reinterpret_cast<const float4*>(red_o + (w * QROWS + row) * D + d);
                 acc.x += wt * v.x; acc.y += wt * v.y; acc.z += wt * v.z; acc.w += wt * v.w;
             }
-            const float sc = p.unnormalized ? 1.f : 1.f / Lrow[row];
+            const float sc = p.unnormalized ? 1.f : (Lrow[row] > 0.f ? 1.f / Lrow[row] : 0.f);
             acc.x *= sc; acc.y *= sc; acc.z *= sc; acc.w *= sc;
             *reinterpret_cast<float4*>(p.O + (row_base + row) * D + d) = acc;
         }
@@ -463,7 +541,7 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
             const int it = tid + k * C::THREADS;
             if (it < items) {
                 const int r = it / (D / 4), d = (it % (D / 4)) * 4;
-                const float sc = p.unnormalized ? 1.f : 1.f / sL[r];
+                const float sc = p.unnormalized ? 1.f : (sL[r] > 0.f ? 1.f / sL[r] : 0.f);
                 *reinterpret_cast<float4*>(p.O + (row_base + r) * D + d) =
                     make_float4(acc[k].x * sc, acc[k].y * sc, acc[k].z * sc, acc[k].w * sc);
             }

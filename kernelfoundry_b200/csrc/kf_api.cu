@@ -386,18 +386,39 @@ int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, 
     return e == cudaSuccess ? KF_OK : cuda_fail(e);
 }
 
+// Paged KV description (kf_attn_fwd_paged); null for contiguous K/V.
+struct Paged {
+    const int* block_table;
+    const int* seq_lens;
+    int n_blocks, block_size, max_blocks;
+};
+
 template <int D, int MT>
 int launch_decode_t(const Plan& pl, const void* Q, const void* K, const void* V, float* O, float* Mi, float* Li,
-                    int unnorm, int B, int H_q, int H_kv, int S_q, int S_kv, void* ws, cudaStream_t s) {
+                    int unnorm, int B, int H_q, int H_kv, int S_q, int S_kv, void* ws, cudaStream_t s,
+                    const Paged* pg) {
     using C = kf::DecodeCfg<D, MT>;
     int bps = 0;
-    int rc = kernel_setup<kf::decode_fwd_kernel<D, MT>>(C::SMEM_BYTES, C::THREADS, &bps);
+    int rc = pg ? kernel_setup<kf::decode_fwd_kernel<D, MT, true>>(C::SMEM_BYTES, C::THREADS, &bps)
+                : kernel_setup<kf::decode_fwd_kernel<D, MT, false>>(C::SMEM_BYTES, C::THREADS, &bps);
     if (rc != KF_OK) return rc;
     const int kv_box = S_kv < C::TK ? S_kv : C::TK;
     CUtensorMap mk, mv;
-    if ((rc = make_map(&mk, K, D, S_kv, static_cast<long long>(B) * H_kv, kv_box, C::SWB)) != KF_OK) return rc;
-    if ((rc = make_map(&mv, V, D, S_kv, static_cast<long long>(B) * H_kv, kv_box, C::SWB)) != KF_OK) return rc;
+    if (pg) {
+        // Pools [n_blocks][H_kv][block_size][D]: 3-D maps (D, block_size, n_blocks * H_kv).
+        const int box = pg->block_size < C::TK ? pg->block_size : C::TK;
+        const long long planes = static_cast<long long>(pg->n_blocks) * H_kv;
+        if ((rc = make_map(&mk, K, D, pg->block_size, planes, box, C::SWB)) != KF_OK) return rc;
+        if ((rc = make_map(&mv, V, D, pg->block_size, planes, box, C::SWB)) != KF_OK) return rc;
+    } else {
+        if ((rc = make_map(&mk, K, D, S_kv, static_cast<long long>(B) * H_kv, kv_box, C::SWB)) != KF_OK) return rc;
+        if ((rc = make_map(&mv, V, D, S_kv, static_cast<long long>(B) * H_kv, kv_box, C::SWB)) != KF_OK) return rc;
+    }
     kf::DecodeParams p;
+    p.block_table = pg ? pg->block_table : nullptr;
+    p.seq_lens = pg ? pg->seq_lens : nullptr;
+    p.max_blocks = pg ? pg->max_blocks : 0;
+    p.block_size = pg ? pg->block_size : 0;
     p.Q = static_cast<const uint16_t*>(Q);
     p.O = O;
     p.Mi = Mi;
@@ -419,17 +440,21 @@ int launch_decode_t(const Plan& pl, const void* Q, const void* K, const void* V,
     p.scale_log2 = p.scale * 1.4426950408889634f;
     p.unnormalized = unnorm;
     p.timeout_ns = g_timeout_ns.load();
-    p.kv_box = kv_box;
+    p.kv_box = pg ? C::TK : kv_box;
     dim3 grid(pl.n_split, H_kv * pl.n_rg, B);
-    kf::decode_fwd_kernel<D, MT><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
+    if (pg)
+        kf::decode_fwd_kernel<D, MT, true><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
+    else
+        kf::decode_fwd_kernel<D, MT, false><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KF_OK : cuda_fail(e);
 }
 
 int launch_decode(const Plan& pl, int D, const void* Q, const void* K, const void* V, float* O, float* Mi,
-                  float* Li, int unnorm, int B, int H_q, int H_kv, int S_q, int S_kv, void* ws, cudaStream_t s) {
+                  float* Li, int unnorm, int B, int H_q, int H_kv, int S_q, int S_kv, void* ws, cudaStream_t s,
+                  const Paged* pg = nullptr) {
 #define KF_DEC(DV, MTV) \
-    return launch_decode_t<DV, MTV>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s)
+    return launch_decode_t<DV, MTV>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s, pg)
     switch (D) {
         case 16: if (pl.mt == 2) KF_DEC(16, 2); KF_DEC(16, 1);
         case 64: if (pl.mt == 2) KF_DEC(64, 2); KF_DEC(64, 1);
@@ -462,6 +487,33 @@ int attn_core(const void* Q, const void* K, const void* V, float* O, float* Mi, 
         }
     }
     return launch_decode(pl, D, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, pl.n_split > 1 ? ws : nullptr, s);
+}
+
+int paged_core(const void* Q, const void* K_pool, const void* V_pool, const int* block_table, const int* seq_lens,
+               float* O, float* Mi, float* Li, int B, int H_q, int H_kv, int S_q, int D, int n_blocks,
+               int block_size, int max_blocks, void* ws, size_t ws_bytes, void* stream) {
+    if (B < 0 || S_q < 0 || H_q <= 0 || H_kv <= 0 || H_q % H_kv != 0) return KF_ERR_INVALID_ARG;
+    if (!(D == 16 || D == 64 || D == 128 || D == 256)) return KF_ERR_UNSUPPORTED_HEAD_DIM;
+    if (n_blocks <= 0 || max_blocks <= 0) return KF_ERR_INVALID_ARG;
+    // block_size: a power of two in [16, 256] (a stage of 64 rows is whole blocks or part of one).
+    if (block_size < 16 || block_size > 256 || (block_size & (block_size - 1))) return KF_ERR_INVALID_ARG;
+    if (static_cast<long long>(n_blocks) * H_kv >= (1ll << 31) ||
+        static_cast<long long>(max_blocks) * block_size >= (1ll << 31))
+        return KF_ERR_INVALID_ARG;
+    if (!use_decode(H_q / H_kv, S_q, D)) return KF_ERR_INVALID_ARG;    // decode shapes only
+    if (B == 0 || S_q == 0) return KF_OK;
+    if (!Q || !K_pool || !V_pool || !block_table || !seq_lens || !O) return KF_ERR_INVALID_ARG;
+    if (!aligned16(Q) || !aligned16(K_pool) || !aligned16(V_pool) || !aligned16(O)) return KF_ERR_MISALIGNED;
+    if (!ws) ws_bytes = 0;
+    if (ws && !aligned16(ws)) return KF_ERR_MISALIGNED;
+    const int S_max = max_blocks * block_size;
+    Plan pl;
+    int rc = plan_for_call(B, H_q, H_kv, S_q, S_max, D, ws_bytes, &pl);
+    if (rc != KF_OK) return rc;
+    if (pl.path != 1) return KF_ERR_INVALID_ARG;
+    const Paged pg{block_table, seq_lens, n_blocks, block_size, max_blocks};
+    return launch_decode(pl, D, Q, K_pool, V_pool, O, Mi, Li, 0, B, H_q, H_kv, S_q, S_max,
+                         pl.n_split > 1 ? ws : nullptr, static_cast<cudaStream_t>(stream), &pg);
 }
 
 // ------------------------------------------------------------------ fixed scratch (kf_attn_fwd_noalloc)
@@ -536,6 +588,20 @@ int kf_attn_fwd_ex(const void* Q, const void* K, const void* V, float* O, float*
                    int H_kv, int S_q, int S_kv, int D, unsigned flags, void* workspace, size_t workspace_bytes,
                    void* stream) {
     return attn_core(Q, K, V, O, Mi, Li, 0, B, H_q, H_kv, S_q, S_kv, D, workspace, workspace_bytes, stream, flags);
+}
+
+int kf_attn_fwd_paged(const void* Q, const void* K_pool, const void* V_pool, const int* block_table,
+                      const int* seq_lens, float* O, float* Mi, float* Li, int B, int H_q, int H_kv, int S_q, int D,
+                      int n_blocks, int block_size, int max_blocks, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+    return paged_core(Q, K_pool, V_pool, block_table, seq_lens, O, Mi, Li, B, H_q, H_kv, S_q, D, n_blocks, block_size,
+                      max_blocks, workspace, workspace_bytes, stream);
+}
+
+size_t kf_attn_paged_workspace_bytes(int B, int H_q, int H_kv, int S_q, int D, int block_size, int max_blocks) {
+    if (B <= 0 || S_q <= 0 || H_q <= 0 || H_kv <= 0 || H_q % H_kv != 0 || max_blocks <= 0 || block_size <= 0) return 0;
+    if (!use_decode(H_q / H_kv, S_q, D)) return 0;
+    return kf_attn_workspace_bytes(B, H_q, H_kv, S_q, max_blocks * block_size, D);
 }
 
 int kf_attn_fwd_partial(const void* Q, const void* K, const void* V, float* O_u, float* m, float* l, int B, int H_q,

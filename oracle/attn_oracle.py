@@ -122,6 +122,32 @@ def causal_attn_lse(Q: np.ndarray, K: np.ndarray, V: np.ndarray):
     return O, Mi, Li
 
 
+def paged_attn_lse(Q, K_pool, V_pool, block_table, seq_lens, block_size):
+    """(O, Mi, Li) over a paged KV cache: sequence b's keys are the first seq_lens[b]
+    rows of its logical blocks, block j stored at pool block block_table[b, j] of
+    K_pool/V_pool [n_blocks, H_kv, block_size, D] (the page layout of the reference's
+    paged benchmark, reference_benchmarks/bench_flash_attn2.py:153-215, gathered the
+    way its naive path gathers them).  A sequence with no keys gives O = 0,
+    Mi = -inf, Li = 0.
+    """
+    B, H_q, S_q, D = Q.shape
+    H_kv = K_pool.shape[1]
+    O = np.zeros_like(Q)
+    Mi = np.full((B, H_q, S_q), -np.inf, dtype=Q.dtype)
+    Li = np.zeros((B, H_q, S_q), dtype=Q.dtype)
+    for b in range(B):
+        n = int(seq_lens[b])
+        if n <= 0:
+            continue
+        nb = (n + block_size - 1) // block_size
+        blocks = [int(x) for x in block_table[b, :nb]]
+        Kb = np.concatenate([K_pool[pb] for pb in blocks], axis=1)[:, :n][None]     # [1, H_kv, n, D]
+        Vb = np.concatenate([V_pool[pb] for pb in blocks], axis=1)[:, :n][None]
+        o, mi, li = reference_attn_lse(Q[b:b + 1], Kb, Vb)
+        O[b], Mi[b], Li[b] = o[0], mi[0], li[0]
+    return O, Mi, Li
+
+
 def causal_pairs(S_q: int, S_kv: int) -> int:
     """Number of visible (query, key) pairs under the bottom-right causal mask."""
     off = S_kv - S_q

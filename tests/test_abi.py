@@ -100,6 +100,18 @@ def test_argument_validation_without_gpu(kf_lib):
     assert kf_lib.kf_attn_fwd_ex(FAKE, FAKE, FAKE, FAKE, None, None, 1, 4, 2, 9, 8, 64, L.KF_FLAG_CAUSAL, None, 0,
                                  None) == L.KF_ERR_INVALID_ARG
     assert kf_lib.kf_attn_fwd_ex(FAKE, FAKE, FAKE, FAKE, None, None, 0, 4, 2, 9, 8, 64, 0, None, 0, None) == L.KF_OK
+    # Paged decode: bad block sizes, non-decode shapes and a zero pool are rejected before any launch.
+    def _paged(B=2, Hq=8, Hkv=2, Sq=1, D=128, nb=64, bs=16, mb=8):
+        return kf_lib.kf_attn_fwd_paged(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, None, None, B, Hq, Hkv, Sq, D, nb, bs, mb,
+                                        None, 0, None)
+    assert _paged(bs=24) == L.KF_ERR_INVALID_ARG
+    assert _paged(bs=8) == L.KF_ERR_INVALID_ARG
+    assert _paged(bs=512) == L.KF_ERR_INVALID_ARG
+    assert _paged(nb=0) == L.KF_ERR_INVALID_ARG
+    assert _paged(Sq=64) == L.KF_ERR_INVALID_ARG            # 4 x 64 rows: not a decode shape
+    assert _paged(D=48) == L.KF_ERR_UNSUPPORTED_HEAD_DIM
+    assert _paged(B=0) == L.KF_OK
+    assert kf_lib.kf_attn_paged_workspace_bytes(1, 8, 2, 64, 128, 16, 8) == 0
     # Packed combine: part stride below rows*(D+2) or not a multiple of 4 is rejected before any launch.
     assert kf_lib.kf_attn_combine_packed(FAKE, 4 * 8 * 66 - 4, 2, FAKE, None, None, 1, 4, 8, 64, None) \
         == L.KF_ERR_INVALID_ARG
