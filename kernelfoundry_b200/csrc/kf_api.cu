@@ -377,8 +377,15 @@ int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, 
         const long long slot_rows = static_cast<long long>(pl.pf_units - pl.pf_plain) * pl.pf_k * C::NQ * C::BM;
         if ((rc = make_map_f32(&mp, p.part, D, static_cast<int>(slot_rows), 1, C::BM)) != KF_OK) return rc;
     }
-    const long long ctas = pl.ctas;
-    if (ctas <= 0 || ctas > 0x7fffffffll) return KF_ERR_INVALID_ARG;
+    const long long n_items = pl.ctas;          // whole units + KV chunks of split units
+    if (n_items <= 0 || n_items > 0x7fffffffll) return KF_ERR_INVALID_ARG;
+    p.n_items = static_cast<int>(n_items);
+    // Persistent CTAs (one per SM, striding over the items) when every tile is full
+    // size; short sequences rely on zero-filled tile rows, so each CTA then takes one item.
+    DeviceInfo* di = nullptr;
+    if ((rc = device_info(&di)) != KF_OK) return rc;
+    const bool persistent = q_box == C::BM && kv_box == C::BC;
+    const long long ctas = persistent && n_items > di->sm_count ? di->sm_count : n_items;
     if (causal)
         kf::prefill_fwd_kernel<D, true><<<static_cast<unsigned>(ctas), C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, mo, mp, p);
     else

@@ -102,6 +102,7 @@ struct PrefillParams {
     int n_qblk;         // 256-row blocks per (b, h_q)
     int kv_off;         // S_kv - S_q (>= 0); causal kernels: query i sees keys j <= i + kv_off
     int n_units, n_plain, split_k, per;
+    int n_items;        // n_plain + (n_units - n_plain) * split_k; CTAs stride over them
     float* part;        // [n_units - n_plain][split_k][NQ*BM][D + 2]
     unsigned* counters; // one ticket per split unit, zero between calls
     unsigned long long timeout_ns;
@@ -122,6 +123,88 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, 
     return mbar_wait_bounded(bar, parity, &dummy, timeout_ns);
 }
 
+// One work item of the 1-D list: whole units [0, n_plain) (b, h, 256-row block),
+// then the KV chunks of the split units.
+struct PrefillItem {
+    int unit, chunk, qblk, h, b, h_kv, q_row0, nq_active, kt0, n_kv;
+    bool split;
+};
+
+template <int D, bool CAUSAL>
+__device__ __forceinline__ PrefillItem prefill_item(const PrefillParams& p, int item) {
+    using C = PrefillCfg<D>;
+    PrefillItem it;
+    it.chunk = 0;
+    if (item < p.n_plain) {
+        it.unit = item;
+    } else {
+        it.unit = p.n_plain + (item - p.n_plain) / p.split_k;
+        it.chunk = (item - p.n_plain) % p.split_k;
+    }
+    it.split = it.unit >= p.n_plain;
+    // Causal: heaviest query blocks (most visible keys) first, (b, h) fastest, so the
+    // long units start first; otherwise the query block is fastest.
+    it.qblk = CAUSAL ? p.n_qblk - 1 - it.unit / p.B_H : it.unit % p.n_qblk;
+    it.h = CAUSAL ? (it.unit % p.B_H) % p.H_q : (it.unit / p.n_qblk) % p.H_q;
+    it.b = CAUSAL ? (it.unit % p.B_H) / p.H_q : it.unit / (p.n_qblk * p.H_q);
+    it.h_kv = it.h / p.G;
+    it.q_row0 = it.qblk * C::NQ * C::BM;
+    const int rows_left = p.S_q - it.q_row0;
+    it.nq_active = rows_left >= C::NQ * C::BM ? C::NQ : (rows_left + C::BM - 1) / C::BM;
+    const int n_kv_all = (p.S_kv + C::BC - 1) / C::BC;
+    it.kt0 = it.split ? it.chunk * p.per : 0;                                         // first KV tile
+    it.n_kv = it.split ? min(p.per, n_kv_all - it.kt0) : n_kv_all;                   // KV tiles of the item
+    if constexpr (CAUSAL) {
+        // Keys up to the unit's last (valid) query row + kv_off; the split path is off.
+        const int last_row = min(it.q_row0 + C::NQ * C::BM, p.S_q) - 1;
+        it.n_kv = min(n_kv_all, (last_row + p.kv_off) / C::BC + 1);
+    }
+    return it;
+}
+
+// Writes a tile's O (scaled by sc) from TMEM through a free K/V ring slot: passes of
+// the slot's size, each staged as 128-B swizzled fp32 spans of 32 columns (the
+// map's swizzle) and TMA-stored; rows past the tensor are dropped.  Called by the
+// tile's 128 softmax threads; named barrier `bar` orders the passes.  With
+// `complete`, thread row 0 waits until the stores are written, else until read.
+template <int D, int BM, int SLOT_BYTES>
+__device__ __forceinline__ void stage_store_tile(uint8_t* slot, uint32_t tO, int row, int bar, float sc,
+                                                 const CUtensorMap* map, int c1, int c2, bool complete) {
+    constexpr int SPAN = BM * 128;
+    constexpr int SPP = SLOT_BYTES / SPAN;                // spans per pass
+    static_assert(SPP >= 1 && (D / 32) % SPP == 0, "staging slot");
+    constexpr int NPASS = (D / 32) / SPP;
+#pragma unroll 1
+    for (int ps = 0; ps < NPASS; ++ps) {
+#pragma unroll
+        for (int k = 0; k < SPP; ++k) {
+            uint32_t o[32];
+            tmem_ld32(tO + (ps * SPP + k) * 32, o);
+            tmem_wait_ld();
+            uint8_t* rowp = slot + k * SPAN + row * 128;
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+                *reinterpret_cast<float4*>(rowp + ((q ^ (row & 7)) << 4)) =
+                    make_float4(__uint_as_float(o[4 * q]) * sc, __uint_as_float(o[4 * q + 1]) * sc,
+                                __uint_as_float(o[4 * q + 2]) * sc, __uint_as_float(o[4 * q + 3]) * sc);
+        }
+        fence_proxy_async_smem();
+        named_bar_sync(bar, 128);
+        if (row == 0) {
+            for (int k = 0; k < SPP; ++k) tma_store_3d(map, slot + k * SPAN, (ps * SPP + k) * 32, c1, c2);
+            bulk_commit_group();
+            if (complete && ps + 1 == NPASS) bulk_wait_group0(); else bulk_wait_group_read0();
+        }
+        if (ps + 1 < NPASS) named_bar_sync(bar, 128);      // slot read: next pass may write it
+    }
+}
+
+// Persistent CTAs: CTA c takes one item per round of gridDim.x items (snake order).  The K/V ring, TMEM and
+// every barrier carry over from item to item (parities are running counts): the
+// next item's Q loads as soon as the last QK MMA of the current one completes, its
+// first K/V tiles stream while the current item finishes, and each tile's epilogue
+// stages O through the ring slot of the item's last K (tile 0) or V (tile 1) tile,
+// which the producer refills only after that epilogue's stores have read it.
 // CAUSAL: bottom-right causal mask (PrefillParams::kv_off); a separate instantiation
 // so the unmasked kernel carries none of its registers.
 template <int D, bool CAUSAL>
@@ -145,42 +228,23 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     uint64_t* p_full = s_full + NQ;
     uint64_t* p_half = p_full + NQ;
     uint64_t* o_full = p_half + NQ;
-    uint64_t* kv_full = o_full + NQ;
+    uint64_t* stage_free = o_full + NQ;      // tile t's epilogue has read its staging slot
+    uint64_t* kv_full = stage_free + NQ;
     uint64_t* kv_empty = kv_full + NSLOT;
-    uint64_t* mma_done = kv_empty + NSLOT;
+    uint64_t* q_empty = kv_empty + NSLOT;    // the item's last QK MMA completed
+    uint64_t* mma_done = q_empty + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* ticket_last = abort_flag + 1;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    // Work item of this CTA: a whole unit, or one KV chunk of a split unit.
-    const int cta = blockIdx.x;
-    int unit, chunk = 0;
-    if (cta < p.n_plain) {
-        unit = cta;
-    } else {
-        unit = p.n_plain + (cta - p.n_plain) / p.split_k;
-        chunk = (cta - p.n_plain) % p.split_k;
-    }
-    const bool split = unit >= p.n_plain;
-    // Causal: heaviest query blocks (most visible keys) first, (b, h) fastest, so the
-    // long units start in the first wave; otherwise the query block is fastest.
-    const int qblk = CAUSAL ? p.n_qblk - 1 - unit / p.B_H : unit % p.n_qblk;
-    const int h = CAUSAL ? (unit % p.B_H) % p.H_q : (unit / p.n_qblk) % p.H_q;
-    const int b = CAUSAL ? (unit % p.B_H) / p.H_q : unit / (p.n_qblk * p.H_q);
-    const int h_kv = h / p.G;
-    const int q_row0 = qblk * NQ * BM;
-    const int rows_left = p.S_q - q_row0;
-    const int nq_active = rows_left >= NQ * BM ? NQ : (rows_left + BM - 1) / BM;
-    const int n_kv_all = (p.S_kv + BC - 1) / BC;
-    const int kt0 = split ? chunk * p.per : 0;                                  // first KV tile
-    int n_kv = split ? min(p.per, n_kv_all - kt0) : n_kv_all;                  // KV tiles of this CTA
-    if constexpr (CAUSAL) {
-        // Keys up to the unit's last (valid) query row + kv_off; the split path is off.
-        const int last_row = min(q_row0 + NQ * BM, p.S_q) - 1;
-        n_kv = min(n_kv_all, (last_row + p.kv_off) / BC + 1);
-    }
+    // Item of round r of this CTA: rounds alternate direction over the CTAs (snake
+    // order), so with items sorted heaviest first (causal) every CTA's total balances.
+    auto prefill_item_index = [](int r) {
+        const int G = static_cast<int>(gridDim.x), c = static_cast<int>(blockIdx.x);
+        return r * G + ((r & 1) ? G - 1 - c : c);
+    };
 
     if (threadIdx.x == 0) {
         for (int t = 0; t < NQ; ++t) {
@@ -189,11 +253,13 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             mbar_init(&p_full[t], 128);
             mbar_init(&p_half[t], 128);
             mbar_init(&o_full[t], 1);
+            mbar_init(&stage_free[t], 1);
         }
         for (int s = 0; s < NSLOT; ++s) {
             mbar_init(&kv_full[s], 1);
             mbar_init(&kv_empty[s], 1);
         }
+        mbar_init(q_empty, 1);
         mbar_init(mma_done, 1);
         *abort_flag = 0;
         *ticket_last = 0;
@@ -201,7 +267,8 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     }
     if (p.q_box < BM || p.kv_box < BC) {
         // Short sequence: TMA writes only the first box rows of each tile; the
-        // remaining rows must read as zero (zero V rows keep 0 * V finite).
+        // remaining rows must read as zero (zero V rows keep 0 * V finite).  The
+        // host then gives every CTA a single item, so no epilogue staging lands here.
         for (int i = threadIdx.x; i < (NQ * C::Q_BYTES + NSLOT * C::KV_BYTES) / 16;
              i += blockDim.x)
             reinterpret_cast<uint4*>(sQ)[i] = make_uint4(0, 0, 0, 0);
@@ -223,48 +290,81 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             tma_prefetch_desc(&tmQ);
             tma_prefetch_desc(&tmK);
             tma_prefetch_desc(&tmV);
-            const int bh_q = b * p.H_q + h;
-            const int bh_kv = b * p.H_kv + h_kv;
             const uint32_t q_bytes = NSPAN * p.q_box * SWB;
             const uint32_t kv_bytes = NSPAN * p.kv_box * SWB;
-            for (int t = 0; t < nq_active; ++t) {
-                mbar_arrive_expect_tx(&q_full[t], q_bytes);
-                for (int s = 0; s < NSPAN; ++s)
-                    tma_load_3d(sQ + t * C::Q_BYTES + s * BM * SWB, &tmQ, &q_full[t], s * SWE, q_row0 + t * BM, bh_q);
-            }
-            const int n_loads = 2 * n_kv;
-            int issued = 0;
-            for (int i = 0; i < n_loads; ++i) {
-                const int slot = i % NSLOT;
-                const int round = i / NSLOT;
-                if (round > 0 && !mbar_wait_bounded(&kv_empty[slot], (round - 1) & 1, abort_flag, p.timeout_ns)) {
-                    atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_MMA);
-                    break;
+            int pos = 0;                          // ring position of the next K/V load
+            int n_done = 0;                       // items whose loads this thread issued
+            uint32_t pend[NQ];                    // slots tile t's epilogue may still be reading
+            int st_cnt[NQ], q_cnt[NQ];
+#pragma unroll
+            for (int t = 0; t < NQ; ++t) { pend[t] = 0u; st_cnt[t] = 0; q_cnt[t] = 0; }
+            bool ok = true;
+            for (int rnd = 0; rnd * static_cast<int>(gridDim.x) < p.n_items && ok; ++rnd) {
+                const int item = prefill_item_index(rnd);
+                if (item >= p.n_items) continue;
+                const PrefillItem it = prefill_item<D, CAUSAL>(p, item);
+                const int bh_q = it.b * p.H_q + it.h;
+                const int bh_kv = it.b * p.H_kv + it.h_kv;
+                // Q of this item once the previous item's QK MMAs stopped reading Q.
+                if (n_done > 0 && !mbar_wait_bounded(q_empty, (n_done - 1) & 1, abort_flag, p.timeout_ns)) {
+                    atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_MMA); ok = false; break;
                 }
-                mbar_arrive_expect_tx(&kv_full[slot], kv_bytes);
-                // Ring order K_0, V_0, K_1, V_1, ...: a K refill takes the slot of a V freed
-                // mid-step and a V refill that of a K freed at the end of a step, so each
-                // load is issued 1.5 to 2 KV steps before its MMA needs it (TMA loads
-                // from L2 take about one step to land under full load).
-                const bool is_v = (i & 1) != 0;
-                const int tile = i >> 1;
-                const CUtensorMap* map = is_v ? &tmV : &tmK;
-                uint8_t* dst = sKV + slot * C::KV_BYTES;
-                for (int s = 0; s < NSPAN; ++s)
-                    tma_load_3d(dst + s * BC * SWB, map, &kv_full[slot], s * SWE, (kt0 + tile) * BC, bh_kv);
-                // Warm L2 with the same operand KF_PREFILL_L2AHEAD tiles ahead: the CTAs of
-                // one KV head stream it in near lockstep, so without this every tile is
-                // a first touch that waits on HBM.
-                if (C::L2AHEAD > 0 && tile + C::L2AHEAD < n_kv)
+                for (int t = 0; t < it.nq_active; ++t) {
+                    mbar_arrive_expect_tx(&q_full[t], q_bytes);
                     for (int s = 0; s < NSPAN; ++s)
-                        tma_prefetch_l2_3d(map, s * SWE, (kt0 + tile + C::L2AHEAD) * BC, bh_kv);
-                issued = i + 1;
+                        tma_load_3d(sQ + t * C::Q_BYTES + s * BM * SWB, &tmQ, &q_full[t], s * SWE,
+                                    it.q_row0 + t * BM, bh_q);
+                    ++q_cnt[t];
+                }
+                for (int i = 0; i < 2 * it.n_kv; ++i, ++pos) {
+                    const int slot = pos % NSLOT;
+                    const int round = pos / NSLOT;
+                    if (round > 0 && !mbar_wait_bounded(&kv_empty[slot], (round - 1) & 1, abort_flag, p.timeout_ns)) {
+                        atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_MMA); ok = false; break;
+                    }
+#pragma unroll
+                    for (int t = 0; t < NQ; ++t) {
+                        if ((pend[t] >> slot) & 1u) {
+                            if (!mbar_wait_bounded(&stage_free[t], st_cnt[t] & 1, abort_flag, p.timeout_ns)) {
+                                atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_SOFTMAX); ok = false; break;
+                            }
+                            ++st_cnt[t];
+                            pend[t] &= ~(1u << slot);
+                        }
+                    }
+                    if (!ok) break;
+                    mbar_arrive_expect_tx(&kv_full[slot], kv_bytes);
+                    // Ring order K_0, V_0, K_1, V_1, ...: a K refill takes the slot of a V freed
+                    // mid-step and a V refill that of a K freed at the end of a step, so each
+                    // load is issued 1.5 to 2 KV steps before its MMA needs it (TMA loads
+                    // from L2 take about one step to land under full load).
+                    const bool is_v = (i & 1) != 0;
+                    const int tile = i >> 1;
+                    const CUtensorMap* map = is_v ? &tmV : &tmK;
+                    uint8_t* dst = sKV + slot * C::KV_BYTES;
+                    for (int s = 0; s < NSPAN; ++s)
+                        tma_load_3d(dst + s * BC * SWB, map, &kv_full[slot], s * SWE, (it.kt0 + tile) * BC, bh_kv);
+                    // Warm L2 with the same operand L2AHEAD tiles ahead: the CTAs of one KV
+                    // head stream it in near lockstep, so without this every tile is a
+                    // first touch that waits on HBM.
+                    if (C::L2AHEAD > 0 && tile + C::L2AHEAD < it.n_kv)
+                        for (int s = 0; s < NSPAN; ++s)
+                            tma_prefetch_l2_3d(map, s * SWE, (it.kt0 + tile + C::L2AHEAD) * BC, bh_kv);
+                }
+                if (!ok) break;
+                if constexpr (C::TMA_STORE) {
+                    // The item's epilogue stages tile 0 in the slot of its last K and tile 1
+                    // in the slot of its last V.
+                    pend[0] |= 1u << ((pos - 2) % NSLOT);
+                    if (NQ == 2 && it.nq_active == 2) pend[NQ - 1] |= 1u << ((pos - 1) % NSLOT);
+                }
+                ++n_done;
             }
             if (*abort_flag) {
                 // Drain: every copy this thread issued must land before the CTA exits.
-                for (int t = 0; t < nq_active; ++t) mbar_wait_drain(&q_full[t], 0, p.timeout_ns);
-                const int first = issued > NSLOT ? issued - NSLOT : 0;
-                for (int i = first; i < issued; ++i)
+                for (int t = 0; t < NQ; ++t)
+                    if (q_cnt[t] > 0) mbar_wait_drain(&q_full[t], (q_cnt[t] - 1) & 1, p.timeout_ns);
+                for (int i = pos > NSLOT ? pos - NSLOT : 0; i < pos; ++i)
                     mbar_wait_drain(&kv_full[i % NSLOT], (i / NSLOT) & 1, p.timeout_ns);
             }
         }
@@ -279,81 +379,100 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             constexpr uint32_t DESC_HI = umma_desc_hi(8 * SWB, umma_layout_code(SWB));
             const uint32_t q_lo = (smem_u32(sQ) >> 4) + umma_desc_lbo(16);
             const uint32_t kv_lo = smem_u32(sKV) >> 4;
-            bool ok = true;
-            for (int t = 0; t < nq_active && ok; ++t) ok = mbar_wait_bounded(&q_full[t], 0, abort_flag, p.timeout_ns);
-            if (!ok) atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_TMA);
             // The tensor core queues only a few MMAs, so every barrier round trip this
             // thread waits on (~120 cycles even for a completed phase) idles it.  The
             // loop keeps them few: ring slot/phase are counters, K and V are tested
             // together, and a completed p_full makes the p_half wait unnecessary.
-            int slotK = 0, parK = 0;        // ring position 2j of K_j
-            for (int j = 0; j <= n_kv && ok; ++j) {
-                // V_{j-1} sits at ring position 2j - 1, just before K_j.
-                int slotV = slotK - 1, parV = parK;
-                if (slotV < 0) { slotV += NSLOT; --parV; }
-                const bool k_ready = j == n_kv || mbar_test_wait(&kv_full[slotK], parK & 1);
-                const bool v_ready = j == 0 || mbar_test_wait(&kv_full[slotV], parV & 1);
-                if (!k_ready && !mbar_wait_bounded(&kv_full[slotK], parK & 1, abort_flag, p.timeout_ns)) {
-                    atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_TMA); ok = false; break;
-                }
-                if (!v_ready && !mbar_wait_bounded(&kv_full[slotV], parV & 1, abort_flag, p.timeout_ns)) {
-                    atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_TMA); ok = false; break;
-                }
-                tc_fence_after();
-                const uint32_t k_lo = kv_lo + slotK * (C::KV_BYTES >> 4) + umma_desc_lbo(16);
-                const uint32_t v_lo = kv_lo + slotV * (C::KV_BYTES >> 4) + umma_desc_lbo(BC * SWB);
-                const uint32_t ppar = (j - 1) & 1;
+            int slotK = 0, parK = 0;        // ring position of the item's K_j
+            int q_cnt[NQ], steps[NQ];       // q_full completions, KV steps done, per tile
 #pragma unroll
-                for (int t = 0; t < NQ; ++t) {
-                    if (t >= nq_active) break;
-                    const uint32_t tS = tmem + t * BC;
-                    const uint32_t tO = tmem + NQ * BC + t * D;
-                    if (j > 0) {
-                        // P_t arrives in two halves (keys [0, BC/2) then [BC/2, BC)): the
-                        // first half of the PV MMAs runs while the softmax finishes the rest.
-                        // Every softmax thread arrives on p_half before p_full, so a
-                        // completed p_full implies p_half.
-                        const bool full_ready = mbar_test_wait(&p_full[t], ppar);
+            for (int t = 0; t < NQ; ++t) { q_cnt[t] = 0; steps[t] = 0; }
+            bool ok = true;
+            for (int rnd = 0; rnd * static_cast<int>(gridDim.x) < p.n_items && ok; ++rnd) {
+                const int item = prefill_item_index(rnd);
+                if (item >= p.n_items) continue;
+                const PrefillItem it = prefill_item<D, CAUSAL>(p, item);
+                const int n_kv = it.n_kv, nq_active = it.nq_active;
+                for (int t = 0; t < nq_active && ok; ++t) {
+                    ok = mbar_wait_bounded(&q_full[t], q_cnt[t] & 1, abort_flag, p.timeout_ns);
+                    ++q_cnt[t];
+                }
+                if (!ok) { atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_TMA); break; }
+                for (int j = 0; j <= n_kv && ok; ++j) {
+                    // V_{j-1} sits at ring position 2j - 1 of the item, just before K_j.
+                    int slotV = slotK - 1, parV = parK;
+                    if (slotV < 0) { slotV += NSLOT; --parV; }
+                    const bool k_ready = j == n_kv || mbar_test_wait(&kv_full[slotK], parK & 1);
+                    const bool v_ready = j == 0 || mbar_test_wait(&kv_full[slotV], parV & 1);
+                    if (!k_ready && !mbar_wait_bounded(&kv_full[slotK], parK & 1, abort_flag, p.timeout_ns)) {
+                        atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_TMA); ok = false; break;
+                    }
+                    if (!v_ready && !mbar_wait_bounded(&kv_full[slotV], parV & 1, abort_flag, p.timeout_ns)) {
+                        atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_TMA); ok = false; break;
+                    }
+                    tc_fence_after();
+                    const uint32_t k_lo = kv_lo + slotK * (C::KV_BYTES >> 4) + umma_desc_lbo(16);
+                    const uint32_t v_lo = kv_lo + slotV * (C::KV_BYTES >> 4) + umma_desc_lbo(BC * SWB);
 #pragma unroll
-                        for (int hf = 0; hf < 2; ++hf) {
-                            if (!full_ready) {
-                                if (!mbar_wait_bounded(hf == 0 ? &p_half[t] : &p_full[t], ppar, abort_flag,
-                                                       p.timeout_ns)) {
-                                    atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_SOFTMAX); ok = false; break;
+                    for (int t = 0; t < NQ; ++t) {
+                        if (t >= nq_active) break;
+                        const uint32_t tS = tmem + t * BC;
+                        const uint32_t tO = tmem + NQ * BC + t * D;
+                        if (j > 0) {
+                            // P_t arrives in two halves (keys [0, BC/2) then [BC/2, BC)): the
+                            // first half of the PV MMAs runs while the softmax finishes the rest.
+                            // Every softmax thread arrives on p_half before p_full, so a
+                            // completed p_full implies p_half.  The first PV of an item also
+                            // follows its softmax warpgroup's previous epilogue (which read O_t).
+                            const uint32_t ppar = (steps[t] + j - 1) & 1;
+                            const bool full_ready = mbar_test_wait(&p_full[t], ppar);
+#pragma unroll
+                            for (int hf = 0; hf < 2; ++hf) {
+                                if (!full_ready) {
+                                    if (!mbar_wait_bounded(hf == 0 ? &p_half[t] : &p_full[t], ppar, abort_flag,
+                                                           p.timeout_ns)) {
+                                        atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_SOFTMAX); ok = false; break;
+                                    }
+                                }
+                                if (hf == 0 || !full_ready) tc_fence_after();
+#pragma unroll
+                                for (int kk = hf * BC / 32; kk < (hf + 1) * BC / 32; ++kk) {
+                                    // A = P_t in TMEM (fp16 pairs over the first BC/2 columns of S_t);
+                                    // B = V: MN-major spans of SWE columns, 8-row groups of SWB bytes.
+                                    umma_ts(tO, tS + kk * 8, umma_desc_join(v_lo + ((kk * 16 * SWB) >> 4), DESC_HI),
+                                            idesc_pv, (j > 1 || kk > 0) ? 1u : 0u);
                                 }
                             }
-                            if (hf == 0 || !full_ready) tc_fence_after();
+                            if (!ok) break;
+                            if (j == n_kv) umma_commit(&o_full[t]);
+                            // V_{j-1} is free once the last tile's PV has read it (before QK_B(j)).
+                            if (t == nq_active - 1) umma_commit(&kv_empty[slotV]);
+                        }
+                        if (j < n_kv) {
+                            const uint32_t a_lo = q_lo + t * (C::Q_BYTES >> 4);
 #pragma unroll
-                            for (int kk = hf * BC / 32; kk < (hf + 1) * BC / 32; ++kk) {
-                                // A = P_t in TMEM (fp16 pairs over the first BC/2 columns of S_t);
-                                // B = V: MN-major spans of SWE columns, 8-row groups of SWB bytes.
-                                umma_ts(tO, tS + kk * 8, umma_desc_join(v_lo + ((kk * 16 * SWB) >> 4), DESC_HI),
-                                        idesc_pv, (j > 1 || kk > 0) ? 1u : 0u);
+                            for (int kk = 0; kk < D / 16; ++kk) {
+                                // K-major, 128-B (or 32-B) swizzle: span s of SWE columns, +32 B per 16 columns.
+                                const int span = (kk * 16) / SWE;
+                                const int off = ((kk * 16) % SWE) * 2;
+                                umma_ss(tS, umma_desc_join(a_lo + ((span * BM * SWB + off) >> 4), DESC_HI),
+                                        umma_desc_join(k_lo + ((span * BC * SWB + off) >> 4), DESC_HI), idesc_qk,
+                                        kk > 0 ? 1u : 0u);
                             }
+                            umma_commit(&s_full[t]);
                         }
-                        if (!ok) break;
-                        if (j == n_kv) umma_commit(&o_full[t]);
-                        // V_{j-1} is free once the last tile's PV has read it (before QK_B(j)).
-                        if (t == nq_active - 1) umma_commit(&kv_empty[slotV]);
                     }
+                    if (!ok) break;
+                    if (j == n_kv - 1) umma_commit(q_empty);      // Q is free once these QKs complete
                     if (j < n_kv) {
-                        const uint32_t a_lo = q_lo + t * (C::Q_BYTES >> 4);
-#pragma unroll
-                        for (int kk = 0; kk < D / 16; ++kk) {
-                            // K-major, 128-B (or 32-B) swizzle: span s of SWE columns, +32 B per 16 columns.
-                            const int span = (kk * 16) / SWE;
-                            const int off = ((kk * 16) % SWE) * 2;
-                            umma_ss(tS, umma_desc_join(a_lo + ((span * BM * SWB + off) >> 4), DESC_HI),
-                                    umma_desc_join(k_lo + ((span * BC * SWB + off) >> 4), DESC_HI), idesc_qk,
-                                    kk > 0 ? 1u : 0u);
-                        }
-                        umma_commit(&s_full[t]);
+                        umma_commit(&kv_empty[slotK]);
+                        slotK += 2;                  // K_{j+1} at 2j + 2
+                        if (slotK >= NSLOT) { slotK -= NSLOT; ++parK; }
                     }
                 }
-                if (!ok) break;
-                if (j < n_kv) umma_commit(&kv_empty[slotK]);
-                slotK += 2;                      // K_{j+1} at 2j + 2
-                if (slotK >= NSLOT) { slotK -= NSLOT; ++parK; }
+#pragma unroll
+                for (int t = 0; t < NQ; ++t)
+                    if (t < nq_active) steps[t] += n_kv;
             }
             // Every MMA issued above must complete before TMEM is released.
             umma_commit(mma_done);
@@ -367,112 +486,128 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         const int t = (warp - 4) >> 2;
         const int wq = warp & 3;                 // TMEM sub-partition of this warp
         const int row = wq * 32 + lane;          // query row within the tile
-        if (t < nq_active) {
-            const uint32_t tl = tmem + (static_cast<uint32_t>(wq * 32) << 16);
-            const uint32_t tS = tl + t * BC;
-            const uint32_t tO = tl + NQ * BC + t * D;
-            const float c = p.scale_log2;
+        const uint32_t tl = tmem + (static_cast<uint32_t>(wq * 32) << 16);
+        const uint32_t tS = tl + t * BC;
+        const uint32_t tO = tl + NQ * BC + t * D;
+        const float c = p.scale_log2;
+        int pos = 0;                             // ring position of the item's K_0
+        int sst = 0, o_cnt = 0;                  // this tile's KV steps and o_full completions
+        bool ok = true;
+        for (int rnd = 0; rnd * static_cast<int>(gridDim.x) < p.n_items && ok; ++rnd) {
+            const int item = prefill_item_index(rnd);
+            if (item >= p.n_items) continue;
+            const PrefillItem it = prefill_item<D, CAUSAL>(p, item);
+            const int n_kv = it.n_kv, nq_active = it.nq_active, q_row0 = it.q_row0, kt0 = it.kt0;
+            const int b = it.b, h = it.h, unit = it.unit, chunk = it.chunk;
+            const bool split = it.split;
+            const int pos0 = pos;
+            pos += 2 * n_kv;
+            if (t >= nq_active) continue;
             // Causal: keys of tile j visible to this row are those below diag - j*BC.
             const int diag = CAUSAL ? q_row0 + t * BM + row + p.kv_off - kt0 * BC + 1 : 0;
             float m_ref = -CUDART_INF_F, m_true = -CUDART_INF_F, l = 0.f;
-            bool ok = true;
             for (int j = 0; j < n_kv; ++j) {
-                ok = mbar_wait_bounded(&s_full[t], j & 1, abort_flag, p.timeout_ns);
-                ok = __all_sync(0xffffffffu, ok);
-                if (!ok) { atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_MMA); break; }
-                tc_fence_after();
-                uint32_t sr[BC];
-#pragma unroll
-                for (int cc = 0; cc < BC / 32; ++cc)
-                    tmem_ld32(tS + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[cc * 32]));
-                tmem_wait_ld();
-                // Keys of this tile visible to this row: past S_kv (ragged end) and, with
-                // the causal mask, past the row's diagonal read as -inf.
-                int kv_valid = p.S_kv - (kt0 + j) * BC;
-                if constexpr (CAUSAL) kv_valid = min(kv_valid, diag - j * BC);
-                if (kv_valid < BC) {
-#pragma unroll
-                    for (int cc = 0; cc < BC; ++cc)
-                        if (cc >= kv_valid) sr[cc] = __float_as_uint(-CUDART_INF_F);
-                }
-#define KF_S(i) __uint_as_float(sr[i])
-                // Row max: three-input max, four independent chains.
-                float mx0 = KF_S(0), mx1 = KF_S(1), mx2 = KF_S(2), mx3 = KF_S(3);
-#pragma unroll
-                for (int cc = 4; cc + 8 <= BC; cc += 8) {
-                    mx0 = fmax3f(mx0, KF_S(cc), KF_S(cc + 1));
-                    mx1 = fmax3f(mx1, KF_S(cc + 2), KF_S(cc + 3));
-                    mx2 = fmax3f(mx2, KF_S(cc + 4), KF_S(cc + 5));
-                    mx3 = fmax3f(mx3, KF_S(cc + 6), KF_S(cc + 7));
-                }
-                mx0 = fmax3f(mx0, KF_S(BC - 4), KF_S(BC - 3));
-                mx1 = fmax3f(mx1, KF_S(BC - 2), KF_S(BC - 1));
-                const float m_new = fmax3f(m_true, fmaxf(mx0, mx1), fmaxf(mx2, mx3));
-                m_true = m_new;
-                // Lazy rescale: keep the reference max unless the row max grew by
-                // more than 2^8 (P <= 256 stays exact enough in fp16, l and O in fp32).
-                bool rescale = false;
-                float f = 1.0f;
-                if (j == 0) {
-                    m_ref = m_new;
-                } else {
-                    const bool need = (m_new - m_ref) * c > 8.0f;
-                    rescale = __any_sync(0xffffffffu, need);
-                    if (need) {
-                        f = ex2_approx((m_ref - m_new) * c);
+                    ok = mbar_wait_bounded(&s_full[t], (sst + j) & 1, abort_flag, p.timeout_ns);
+                    ok = __all_sync(0xffffffffu, ok);
+                    if (!ok) { atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_MMA); break; }
+                    tc_fence_after();
+                    uint32_t sr[BC];
+    #pragma unroll
+                    for (int cc = 0; cc < BC / 32; ++cc)
+                        tmem_ld32(tS + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[cc * 32]));
+                    tmem_wait_ld();
+                    // Keys of this tile visible to this row: past S_kv (ragged end) and, with
+                    // the causal mask, past the row's diagonal read as -inf.
+                    int kv_valid = p.S_kv - (kt0 + j) * BC;
+                    if constexpr (CAUSAL) kv_valid = min(kv_valid, diag - j * BC);
+                    if (kv_valid < BC) {
+    #pragma unroll
+                        for (int cc = 0; cc < BC; ++cc)
+                            if (cc >= kv_valid) sr[cc] = __float_as_uint(-CUDART_INF_F);
+                    }
+    #define KF_S(i) __uint_as_float(sr[i])
+                    // Row max: three-input max, four independent chains.
+                    float mx0 = KF_S(0), mx1 = KF_S(1), mx2 = KF_S(2), mx3 = KF_S(3);
+    #pragma unroll
+                    for (int cc = 4; cc + 8 <= BC; cc += 8) {
+                        mx0 = fmax3f(mx0, KF_S(cc), KF_S(cc + 1));
+                        mx1 = fmax3f(mx1, KF_S(cc + 2), KF_S(cc + 3));
+                        mx2 = fmax3f(mx2, KF_S(cc + 4), KF_S(cc + 5));
+                        mx3 = fmax3f(mx3, KF_S(cc + 6), KF_S(cc + 7));
+                    }
+                    mx0 = fmax3f(mx0, KF_S(BC - 4), KF_S(BC - 3));
+                    mx1 = fmax3f(mx1, KF_S(BC - 2), KF_S(BC - 1));
+                    const float m_new = fmax3f(m_true, fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+                    m_true = m_new;
+                    // Lazy rescale: keep the reference max unless the row max grew by
+                    // more than 2^8 (P <= 256 stays exact enough in fp16, l and O in fp32).
+                    bool rescale = false;
+                    float f = 1.0f;
+                    if (j == 0) {
                         m_ref = m_new;
-                        l *= f;
+                    } else {
+                        const bool need = (m_new - m_ref) * c > 8.0f;
+                        rescale = __any_sync(0xffffffffu, need);
+                        if (need) {
+                            f = ex2_approx((m_ref - m_new) * c);
+                            m_ref = m_new;
+                            l *= f;
+                        }
                     }
-                }
-                if (rescale) {
-                    // O_t is stable here: PV_t(j-1) completed before S_t(j) was committed.
-#pragma unroll
-                    for (int dc = 0; dc < D / RCH; ++dc) {
-                        uint32_t o[RCH];
-                        tmem_ld_chunk<RCH>(tO + dc * RCH, o);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int k = 0; k < RCH; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * f);
-                        tmem_st_chunk<RCH>(tO + dc * RCH, o);
+                    if (rescale) {
+                        // O_t is stable here: PV_t(j-1) completed before S_t(j) was committed.
+    #pragma unroll
+                        for (int dc = 0; dc < D / RCH; ++dc) {
+                            uint32_t o[RCH];
+                            tmem_ld_chunk<RCH>(tO + dc * RCH, o);
+                            tmem_wait_ld();
+    #pragma unroll
+                            for (int k = 0; k < RCH; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * f);
+                            tmem_st_chunk<RCH>(tO + dc * RCH, o);
+                        }
                     }
-                }
-                // P = 2^(s*c - m_ref*c): paired FMA, MUFU ex2, paired row-sum adds;
-                // packed to fp16 pairs in place (pair i/2 overwrites scores already
-                // read) and written over the first BC/2 TMEM columns of S_t (this
-                // thread's row), the A operand of the PV MMA.  Each half of the keys
-                // is published on its own barrier (p_half, then p_full).
-                const float2 c2 = make_float2(c, c);
-                const float2 neg2 = make_float2(-m_ref * c, -m_ref * c);
-                float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
-                constexpr int HALF = BC / 2;
-#pragma unroll
-                for (int hf = 0; hf < 2; ++hf) {
-#pragma unroll
-                    for (int i = hf * HALF; i < (hf + 1) * HALF; i += 4) {
-                        const float2 x0 = ffma2(make_float2(KF_S(i), KF_S(i + 1)), c2, neg2);
-                        const float2 x1 = ffma2(make_float2(KF_S(i + 2), KF_S(i + 3)), c2, neg2);
-                        const bool emu = (i % 16) >= 16 - C::EMU16;    // compile-time per i
-                        const float2 e0 = emu ? exp2_poly2(x0) : make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
-                        const float2 e1 = emu ? exp2_poly2(x1) : make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
-                        acc0 = fadd2(acc0, e0);
-                        acc1 = fadd2(acc1, e1);
-                        sr[i / 2] = pack_half2(e0.x, e0.y);
-                        sr[i / 2 + 1] = pack_half2(e1.x, e1.y);
+                    // P = 2^(s*c - m_ref*c): paired FMA, MUFU ex2, paired row-sum adds;
+                    // packed to fp16 pairs in place (pair i/2 overwrites scores already
+                    // read) and written over the first BC/2 TMEM columns of S_t (this
+                    // thread's row), the A operand of the PV MMA.  Each half of the keys
+                    // is published on its own barrier (p_half, then p_full).
+                    const float2 c2 = make_float2(c, c);
+                    const float2 neg2 = make_float2(-m_ref * c, -m_ref * c);
+                    float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+                    constexpr int HALF = BC / 2;
+    #pragma unroll
+                    for (int hf = 0; hf < 2; ++hf) {
+    #pragma unroll
+                        for (int i = hf * HALF; i < (hf + 1) * HALF; i += 4) {
+                            const float2 x0 = ffma2(make_float2(KF_S(i), KF_S(i + 1)), c2, neg2);
+                            const float2 x1 = ffma2(make_float2(KF_S(i + 2), KF_S(i + 3)), c2, neg2);
+                            const bool emu = (i % 16) >= 16 - C::EMU16;    // compile-time per i
+                            const float2 e0 = emu ? exp2_poly2(x0) : make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
+                            const float2 e1 = emu ? exp2_poly2(x1) : make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
+                            acc0 = fadd2(acc0, e0);
+                            acc1 = fadd2(acc1, e1);
+                            sr[i / 2] = pack_half2(e0.x, e0.y);
+                            sr[i / 2 + 1] = pack_half2(e1.x, e1.y);
+                        }
+                        tmem_st_chunk<HALF / 2>(tS + hf * (HALF / 2),
+                                                *reinterpret_cast<const uint32_t(*)[HALF / 2]>(&sr[hf * (HALF / 2)]));
+                        tmem_wait_st();      // this half of P (and any rescaled O) written before the MMA reads it
+                        tc_fence_before();
+                        mbar_arrive(hf == 0 ? &p_half[t] : &p_full[t]);
                     }
-                    tmem_st_chunk<HALF / 2>(tS + hf * (HALF / 2),
-                                            *reinterpret_cast<const uint32_t(*)[HALF / 2]>(&sr[hf * (HALF / 2)]));
-                    tmem_wait_st();      // this half of P (and any rescaled O) written before the MMA reads it
-                    tc_fence_before();
-                    mbar_arrive(hf == 0 ? &p_half[t] : &p_full[t]);
-                }
-#undef KF_S
-                l += (acc0.x + acc0.y) + (acc1.x + acc1.y);
+    #undef KF_S
+                    l += (acc0.x + acc0.y) + (acc1.x + acc1.y);
             }
+            sst += n_kv;
             if (ok) {
-                ok = mbar_wait_bounded(&o_full[t], 0, abort_flag, p.timeout_ns);
+                ok = mbar_wait_bounded(&o_full[t], o_cnt & 1, abort_flag, p.timeout_ns);
                 ok = __all_sync(0xffffffffu, ok);
                 if (!ok) atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_MMA);
             }
+            ++o_cnt;
+            // Staging slot of this tile: the ring slot of the item's last K (tile 0) or
+            // last V (tile 1); every MMA reading it completed before o_full[t] fired.
+            uint8_t* stage = sKV + ((pos0 + 2 * n_kv - 2 + t) % NSLOT) * C::KV_BYTES;
             const int qrow = q_row0 + t * BM + row;
             const bool store = qrow < p.S_q;
             float* orow = p.O + ((static_cast<size_t>(b) * p.H_q + h) * p.S_q + (store ? qrow : 0)) * D;
@@ -492,29 +627,12 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     tc_fence_after();
                     const float f = ex2_approx((m_ref - m_true) * c);
                     if constexpr (C::TMA_STORE) {
-                        // Staged like the final epilogue, then TMA-stored into the partial
-                        // slots; the stores must be complete (not only read) before the ticket.
-                        uint8_t* sO = (NQ == 2 && t == 0) ? sQ : sKV;
-#pragma unroll
-                        for (int dc = 0; dc < D / 32; ++dc) {
-                            uint32_t o[32];
-                            tmem_ld32(tO + dc * 32, o);
-                            tmem_wait_ld();
-                            uint8_t* rowp = sO + dc * (BM * 128) + row * 128;
-#pragma unroll
-                            for (int q = 0; q < 8; ++q)
-                                *reinterpret_cast<float4*>(rowp + ((q ^ (row & 7)) << 4)) =
-                                    make_float4(__uint_as_float(o[4 * q]) * f, __uint_as_float(o[4 * q + 1]) * f,
-                                                __uint_as_float(o[4 * q + 2]) * f, __uint_as_float(o[4 * q + 3]) * f);
-                        }
-                        fence_proxy_async_smem();
-                        named_bar_sync(2 + t, 128);
+                        // The stores must be complete (not only read) before the ticket.
+                        stage_store_tile<D, BM, C::KV_BYTES>(stage, tO, row, 2 + t, f, &tmP, static_cast<int>(tile0),
+                                                            0, true);
                         if (row == 0) {
-                            for (int dc = 0; dc < D / 32; ++dc)
-                                tma_store_3d(&tmP, sO + dc * (BM * 128), dc * 32, static_cast<int>(tile0), 0);
-                            bulk_commit_group();
-                            bulk_wait_group0();
                             fence_proxy_async_global();
+                            mbar_arrive(&stage_free[t]);
                         }
                     } else {
                         float* prow = p.part + (tile0 + row) * D;
@@ -539,78 +657,79 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     *ticket_last = (tk == static_cast<unsigned>(p.split_k - 1)) ? 1 : 0;
                 }
                 named_bar_sync(1, 128 * nq_active);
-                if (*ticket_last) {
-                    __threadfence();
-                    // Merge, one warp per 32 consecutive rows: lane i computes the weights of
-                    // row i from the chunks' (m, l); then for each row the lanes read the
-                    // chunks' O_u rows (coalesced, several rows in flight) and write O.
-                    const int wi = warp - 4;                      // 0 .. 4*nq_active-1
-                    const int r = wi * 32 + lane;                 // row of the unit this lane weighs
-                    float2 ml[4];
-#pragma unroll
-                    for (int c2 = 0; c2 < 4; ++c2)
-                        ml[c2] = c2 < p.split_k ? __ldcg(part_ml + unit0 + static_cast<size_t>(c2) * ROWS + r)
-                                                : make_float2(-CUDART_INF_F, 0.f);
-                    const float M = fmaxf(fmaxf(ml[0].x, ml[1].x), fmaxf(ml[2].x, ml[3].x));
-                    float w[4], L = 0.f;
-#pragma unroll
-                    for (int c2 = 0; c2 < 4; ++c2) {
-                        w[c2] = c2 < p.split_k ? ex2_approx((ml[c2].x - M) * c) : 0.f;
-                        L += w[c2] * ml[c2].y;
-                    }
-                    const float osc = p.unnormalized ? 1.0f : 1.0f / L;
-#pragma unroll
-                    for (int c2 = 0; c2 < 4; ++c2) w[c2] *= osc;
-                    const int qrow_l = q_row0 + r;
-                    if (qrow_l < p.S_q) {
-                        const size_t mi_l = (static_cast<size_t>(b) * p.H_q + h) * p.S_q + qrow_l;
-                        if (p.Mi) p.Mi[mi_l] = M * p.scale;
-                        if (p.Li) p.Li[mi_l] = L;
-                    }
-                    const float* part_o = p.part + unit0 * D;
-                    float* obase = p.O + ((static_cast<size_t>(b) * p.H_q + h) * p.S_q) * D;
-                    constexpr int RU = D <= 128 ? 8 : 4;          // rows in flight per lane
-#pragma unroll 1
-                    for (int j0 = 0; j0 < 32; j0 += RU) {
-                        float4 acc[RU][(D / 4 + 31) / 32];
-#pragma unroll
-                        for (int u = 0; u < RU; ++u) {
-                            const int rr = wi * 32 + j0 + u;
-                            float wj[4];
-#pragma unroll
-                            for (int c2 = 0; c2 < 4; ++c2) wj[c2] = __shfl_sync(0xffffffffu, w[c2], j0 + u);
-#pragma unroll
-                            for (int ci = 0; ci < (D / 4 + 31) / 32; ++ci) {
-                                const int cidx = lane + ci * 32;
-                                acc[u][ci] = make_float4(0.f, 0.f, 0.f, 0.f);
-                                if (cidx < D / 4) {
-#pragma unroll
-                                    for (int c2 = 0; c2 < 4; ++c2) {
-                                        if (c2 < p.split_k) {
-                                            const float4 v = __ldcg(reinterpret_cast<const float4*>(
-                                                part_o + (static_cast<size_t>(c2) * ROWS + rr) * D) + cidx);
-                                            acc[u][ci].x += wj[c2] * v.x; acc[u][ci].y += wj[c2] * v.y;
-                                            acc[u][ci].z += wj[c2] * v.z; acc[u][ci].w += wj[c2] * v.w;
+                    if (*ticket_last) {
+                        __threadfence();
+                        // Merge, one warp per 32 consecutive rows: lane i computes the weights of
+                        // row i from the chunks' (m, l); then for each row the lanes read the
+                        // chunks' O_u rows (coalesced, several rows in flight) and write O.
+                        const int wi = warp - 4;                      // 0 .. 4*nq_active-1
+                        const int r = wi * 32 + lane;                 // row of the unit this lane weighs
+                        float2 ml[4];
+    #pragma unroll
+                        for (int c2 = 0; c2 < 4; ++c2)
+                            ml[c2] = c2 < p.split_k ? __ldcg(part_ml + unit0 + static_cast<size_t>(c2) * ROWS + r)
+                                                    : make_float2(-CUDART_INF_F, 0.f);
+                        const float M = fmaxf(fmaxf(ml[0].x, ml[1].x), fmaxf(ml[2].x, ml[3].x));
+                        float w[4], L = 0.f;
+    #pragma unroll
+                        for (int c2 = 0; c2 < 4; ++c2) {
+                            w[c2] = c2 < p.split_k ? ex2_approx((ml[c2].x - M) * c) : 0.f;
+                            L += w[c2] * ml[c2].y;
+                        }
+                        const float osc = p.unnormalized ? 1.0f : 1.0f / L;
+    #pragma unroll
+                        for (int c2 = 0; c2 < 4; ++c2) w[c2] *= osc;
+                        const int qrow_l = q_row0 + r;
+                        if (qrow_l < p.S_q) {
+                            const size_t mi_l = (static_cast<size_t>(b) * p.H_q + h) * p.S_q + qrow_l;
+                            if (p.Mi) p.Mi[mi_l] = M * p.scale;
+                            if (p.Li) p.Li[mi_l] = L;
+                        }
+                        const float* part_o = p.part + unit0 * D;
+                        float* obase = p.O + ((static_cast<size_t>(b) * p.H_q + h) * p.S_q) * D;
+                        constexpr int RU = D <= 128 ? 8 : 4;          // rows in flight per lane
+    #pragma unroll 1
+                        for (int j0 = 0; j0 < 32; j0 += RU) {
+                            float4 acc[RU][(D / 4 + 31) / 32];
+    #pragma unroll
+                            for (int u = 0; u < RU; ++u) {
+                                const int rr = wi * 32 + j0 + u;
+                                float wj[4];
+    #pragma unroll
+                                for (int c2 = 0; c2 < 4; ++c2) wj[c2] = __shfl_sync(0xffffffffu, w[c2], j0 + u);
+    #pragma unroll
+                                for (int ci = 0; ci < (D / 4 + 31) / 32; ++ci) {
+                                    const int cidx = lane + ci * 32;
+                                    acc[u][ci] = make_float4(0.f, 0.f, 0.f, 0.f);
+                                    if (cidx < D / 4) {
+    #pragma unroll
+                                        for (int c2 = 0; c2 < 4; ++c2) {
+                                            if (c2 < p.split_k) {
+                                                const float4 v = __ldcg(reinterpret_cast<const float4*>(
+                                                    part_o + (static_cast<size_t>(c2) * ROWS + rr) * D) + cidx);
+                                                acc[u][ci].x += wj[c2] * v.x; acc[u][ci].y += wj[c2] * v.y;
+                                                acc[u][ci].z += wj[c2] * v.z; acc[u][ci].w += wj[c2] * v.w;
+                                            }
                                         }
                                     }
                                 }
                             }
-                        }
-#pragma unroll
-                        for (int u = 0; u < RU; ++u) {
-                            const int qr = q_row0 + wi * 32 + j0 + u;
-                            if (qr < p.S_q) {
-#pragma unroll
-                                for (int ci = 0; ci < (D / 4 + 31) / 32; ++ci) {
-                                    const int cidx = lane + ci * 32;
-                                    if (cidx < D / 4)
-                                        reinterpret_cast<float4*>(obase + static_cast<size_t>(qr) * D)[cidx] = acc[u][ci];
+    #pragma unroll
+                            for (int u = 0; u < RU; ++u) {
+                                const int qr = q_row0 + wi * 32 + j0 + u;
+                                if (qr < p.S_q) {
+    #pragma unroll
+                                    for (int ci = 0; ci < (D / 4 + 31) / 32; ++ci) {
+                                        const int cidx = lane + ci * 32;
+                                        if (cidx < D / 4)
+                                            reinterpret_cast<float4*>(obase + static_cast<size_t>(qr) * D)[cidx] = acc[u][ci];
+                                    }
                                 }
                             }
                         }
+                        if (threadIdx.x == 128) p.counters[su] = 0u;
                     }
-                    if (threadIdx.x == 128) p.counters[su] = 0u;
-                }
+                named_bar_sync(1, 128 * nq_active);     // ticket_last read by all before the next item
             } else {
                 // Every thread of the tile reaches this barrier, ok or not, so the staged
                 // epilogue below (which synchronizes the tile's threads) runs for all or none.
@@ -621,41 +740,17 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     const float l_true = l * f;
                     const float osc = p.unnormalized ? f : 1.0f / l;
                     if constexpr (C::TMA_STORE) {
-                        // Stage the O tile in shared memory that no MMA reads any more: the Q
-                        // region for tile 0 (every QK MMA precedes the last PV_0), the K/V ring
-                        // for tile 1 (all MMAs are complete once o_full[1] fired) and for a
-                        // single tile.  Span s of 32 columns holds rows of 128 B with the
-                        // 16-B chunks XOR-swizzled by row % 8 (the map's 128-B swizzle).
-                        uint8_t* sO = (NQ == 2 && t == 0) ? sQ : sKV;
-    #pragma unroll
-                        for (int dc = 0; dc < D / 32; ++dc) {
-                            uint32_t o[32];
-                            tmem_ld32(tO + dc * 32, o);
-                            tmem_wait_ld();
-                            uint8_t* rowp = sO + dc * (BM * 128) + row * 128;
-    #pragma unroll
-                            for (int q = 0; q < 8; ++q) {
-                                const float4 v = make_float4(__uint_as_float(o[4 * q]) * osc, __uint_as_float(o[4 * q + 1]) * osc,
-                                                             __uint_as_float(o[4 * q + 2]) * osc, __uint_as_float(o[4 * q + 3]) * osc);
-                                *reinterpret_cast<float4*>(rowp + ((q ^ (row & 7)) << 4)) = v;
-                            }
-                        }
-                        fence_proxy_async_smem();
-                        named_bar_sync(2 + t, 128);             // this tile's 128 softmax threads
-                        if (row == 0) {
-                            for (int dc = 0; dc < D / 32; ++dc)
-                                tma_store_3d(&tmO, sO + dc * (BM * 128), dc * 32, q_row0 + t * BM, b * p.H_q + h);
-                            bulk_commit_group();
-                            bulk_wait_group_read0();            // shared memory read before the CTA exits
-                        }
+                        stage_store_tile<D, BM, C::KV_BYTES>(stage, tO, row, 2 + t, osc, &tmO, q_row0 + t * BM,
+                                                            b * p.H_q + h, false);
+                        if (row == 0) mbar_arrive(&stage_free[t]);
                     } else {
-    #pragma unroll
+#pragma unroll
                         for (int dc = 0; dc < D / OCH; ++dc) {
                             uint32_t o[OCH];
                             tmem_ld_chunk<OCH>(tO + dc * OCH, o);
                             tmem_wait_ld();
                             if (store) {
-    #pragma unroll
+#pragma unroll
                                 for (int k = 0; k < OCH; k += 4) {
                                     float4 v = make_float4(__uint_as_float(o[k]) * osc, __uint_as_float(o[k + 1]) * osc,
                                                            __uint_as_float(o[k + 2]) * osc, __uint_as_float(o[k + 3]) * osc);
