@@ -309,7 +309,9 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 if (n_done > 0 && !mbar_wait_bounded(q_empty, (n_done - 1) & 1, abort_flag, p.timeout_ns)) {
                     atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_MMA); ok = false; break;
                 }
-                for (int t = 0; t < it.nq_active; ++t) {
+#pragma unroll
+                for (int t = 0; t < NQ; ++t) {
+                    if (t >= it.nq_active) break;
                     mbar_arrive_expect_tx(&q_full[t], q_bytes);
                     for (int s = 0; s < NSPAN; ++s)
                         tma_load_3d(sQ + t * C::Q_BYTES + s * BM * SWB, &tmQ, &q_full[t], s * SWE,
@@ -362,6 +364,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             }
             if (*abort_flag) {
                 // Drain: every copy this thread issued must land before the CTA exits.
+#pragma unroll
                 for (int t = 0; t < NQ; ++t)
                     if (q_cnt[t] > 0) mbar_wait_drain(&q_full[t], (q_cnt[t] - 1) & 1, p.timeout_ns);
                 for (int i = pos > NSLOT ? pos - NSLOT : 0; i < pos; ++i)
@@ -393,7 +396,9 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 if (item >= p.n_items) continue;
                 const PrefillItem it = prefill_item<D, CAUSAL>(p, item);
                 const int n_kv = it.n_kv, nq_active = it.nq_active;
-                for (int t = 0; t < nq_active && ok; ++t) {
+#pragma unroll
+                for (int t = 0; t < NQ; ++t) {
+                    if (t >= nq_active || !ok) break;
                     ok = mbar_wait_bounded(&q_full[t], q_cnt[t] & 1, abort_flag, p.timeout_ns);
                     ++q_cnt[t];
                 }
