@@ -75,9 +75,14 @@ int kf_attn_fwd_lse(const void* Q, const void* K, const void* V, float* O,
                     void* workspace, size_t workspace_bytes, void* stream);
 
 /* Flags for kf_attn_fwd_ex. */
-#define KF_FLAG_CAUSAL 1u   /* bottom-right causal mask (below) */
+#define KF_FLAG_CAUSAL 1u    /* bottom-right causal mask (below) */
+#define KF_FLAG_OUT_F16 2u   /* O is fp16 (default fp32) */
+#define KF_FLAG_OUT_BF16 4u  /* O is bf16 */
 
-/* kf_attn_fwd_lse with options (Mi/Li may be NULL).  KF_FLAG_CAUSAL: query row i
+/* kf_attn_fwd_lse with options (Mi/Li may be NULL; O points to fp32 data unless an
+ * output flag says otherwise).  KF_FLAG_OUT_F16 / KF_FLAG_OUT_BF16: O is written as
+ * fp16 / bf16 (round to nearest; half the bytes of the reference's fp32 O; Mi/Li
+ * stay fp32; not both).  KF_FLAG_CAUSAL: query row i
  * of S_q sits at absolute position S_kv - S_q + i and attends keys
  * j <= S_kv - S_q + i (chunked prefill over a KV cache; S_q == S_kv is the usual
  * lower-triangular mask, S_q == 1 keeps every key); requires S_q <= S_kv, else
@@ -85,7 +90,7 @@ int kf_attn_fwd_lse(const void* Q, const void* K, const void* V, float* O,
  * counterpart: the reference has no mask and names it as required for decoder
  * use (docs/flash_attn.md:105). */
 int kf_attn_fwd_ex(const void* Q, const void* K, const void* V,
-                   float* O, float* Mi, float* Li,
+                   void* O, float* Mi, float* Li,
                    int B, int H_q, int H_kv, int S_q, int S_kv, int D, unsigned flags,
                    void* workspace, size_t workspace_bytes, void* stream);
 

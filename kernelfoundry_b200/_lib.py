@@ -20,6 +20,8 @@ KF_ERR_UNSUPPORTED_DEVICE = 6
 KF_ERR_WORKSPACE = 7
 
 KF_FLAG_CAUSAL = 1
+KF_FLAG_OUT_F16 = 2
+KF_FLAG_OUT_BF16 = 4
 
 # Every symbol include/kf_attn.h declares.
 EXPORTED = [

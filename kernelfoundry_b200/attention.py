@@ -23,7 +23,7 @@ import threading
 
 import torch
 
-from ._lib import KF_FLAG_CAUSAL, KFError, check, lib
+from ._lib import KF_FLAG_CAUSAL, KF_FLAG_OUT_BF16, KF_FLAG_OUT_F16, KFError, check, lib
 
 __all__ = [
     "launch_flash_attn",
@@ -101,30 +101,40 @@ def plan(B, H_q, H_kv, S_q, S_kv, D, workspace_bytes=2**62):
     return {"path": "prefill" if path.value == 0 else "decode", "n_split": ns.value, "ctas": ctas.value}
 
 
-def flash_attn_fwd(q, k, v, *, out=None, return_lse=False, workspace=None, causal=False):
+_OUT_FLAGS = {torch.float32: 0, torch.float16: KF_FLAG_OUT_F16, torch.bfloat16: KF_FLAG_OUT_BF16}
+
+
+def flash_attn_fwd(q, k, v, *, out=None, return_lse=False, workspace=None, causal=False, out_dtype=None):
     """O = softmax(Q K^T / sqrt(D)) V per head; GQA head map h_kv = h_q // (H_q // H_kv).
 
     q [B,H_q,S_q,D] fp16, k/v [B,H_kv,S_kv,D] fp16 (CUDA, contiguous) ->
     O [B,H_q,S_q,D] fp32.  With ``return_lse`` also returns (Mi, Li), the
     reference kernel's row max of the scaled scores and sum of exp(s - Mi).
     ``causal``: bottom-right causal mask, query i attends keys j <= S_kv - S_q + i
-    (needs S_q <= S_kv); an extension, the reference has no mask.
+    (needs S_q <= S_kv); an extension, the reference has no mask.  ``out_dtype``
+    (or the dtype of ``out``): torch.float32 (the reference's), float16 or bfloat16.
     """
     B, H_q, H_kv, S_q, S_kv, D = _check_qkv(q, k, v)
     dev = q.device
     if out is None:
-        out = torch.empty((B, H_q, S_q, D), dtype=torch.float32, device=dev)
+        out = torch.empty((B, H_q, S_q, D), dtype=out_dtype or torch.float32, device=dev)
+    elif out_dtype is not None and out.dtype != out_dtype:
+        raise ValueError("out and out_dtype disagree")
+    if out.dtype not in _OUT_FLAGS:
+        raise ValueError("output dtype must be float32, float16 or bfloat16")
+    if tuple(out.shape) != (B, H_q, S_q, D) or not out.is_contiguous() or out.device != dev:
+        raise ValueError(f"out must be a contiguous [{B}, {H_q}, {S_q}, {D}] tensor on {dev}")
     Mi = Li = None
     if return_lse:
         Mi = torch.empty((B, H_q, S_q), dtype=torch.float32, device=dev)
         Li = torch.empty_like(Mi)
+    flags = (KF_FLAG_CAUSAL if causal else 0) | _OUT_FLAGS[out.dtype]
     with torch.cuda.device(dev):
         if workspace is None:
             workspace = _workspace(dev, workspace_bytes(B, H_q, H_kv, S_q, S_kv, D))
         wsb = workspace.numel() if workspace is not None else 0
         rc = lib().kf_attn_fwd_ex(_ptr(q), _ptr(k), _ptr(v), _ptr(out), _ptr(Mi), _ptr(Li),
-                                  B, H_q, H_kv, S_q, S_kv, D, KF_FLAG_CAUSAL if causal else 0,
-                                  _ptr(workspace), wsb, _stream_handle(dev))
+                                  B, H_q, H_kv, S_q, S_kv, D, flags, _ptr(workspace), wsb, _stream_handle(dev))
     check(rc, "kf_attn_fwd_ex")
     return (out, Mi, Li) if return_lse else out
 

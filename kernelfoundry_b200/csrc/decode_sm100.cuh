@@ -59,7 +59,7 @@ struct DecodeCfg {
 
 struct DecodeParams {
     const uint16_t* Q;
-    float* O;
+    void* O;               // [rows][D] of out_type (fp32 when unnormalized)
     float* Mi;             // nullable
     float* Li;             // nullable
     float* part_O;         // [rows][n_split][D]   (n_split > 1)
@@ -68,6 +68,7 @@ struct DecodeParams {
     int H_q, H_kv, S_q, S_kv, G, R, n_rg, n_split, chunk;
     float scale_log2, scale;
     int unnormalized;
+    int out_type;          // KF_OUT_F32 / KF_OUT_F16 / KF_OUT_BF16
     int kv_box;            // rows per K/V TMA box: min(TK, S_kv)
     unsigned long long timeout_ns;
     // Paged KV (PAGED kernels): K/V pools [n_blocks][H_kv][block_size][D], logical
@@ -412,7 +413,7 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
             }
             const float sc = p.unnormalized ? 1.f : (Lrow[row] > 0.f ? 1.f / Lrow[row] : 0.f);
             acc.x *= sc; acc.y *= sc; acc.z *= sc; acc.w *= sc;
-            *reinterpret_cast<float4*>(p.O + (row_base + row) * D + d) = acc;
+            store_out4(p.O, (row_base + row) * D + d, acc, p.out_type);
         }
         if (tid < nrows) {
             if (p.Mi) p.Mi[row_base + tid] = Mrow[tid] * p.scale;
@@ -542,8 +543,8 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
             if (it < items) {
                 const int r = it / (D / 4), d = (it % (D / 4)) * 4;
                 const float sc = p.unnormalized ? 1.f : (sL[r] > 0.f ? 1.f / sL[r] : 0.f);
-                *reinterpret_cast<float4*>(p.O + (row_base + r) * D + d) =
-                    make_float4(acc[k].x * sc, acc[k].y * sc, acc[k].z * sc, acc[k].w * sc);
+                store_out4(p.O, (row_base + r) * D + d, make_float4(acc[k].x * sc, acc[k].y * sc, acc[k].z * sc, acc[k].w * sc),
+                           p.out_type);
             }
         }
         if (tid < nrows) {

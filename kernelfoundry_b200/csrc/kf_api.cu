@@ -121,8 +121,9 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// 3-D map over a [BH][S][D] fp16 tensor; boxes of (swizzle span) x box_rows x 1.
-int make_map(CUtensorMap* map, const void* base, int D, int S, long long BH, int box_rows, int swb) {
+// 3-D map over a [BH][S][D] 16-bit tensor (fp16 unless bf16); boxes of (swizzle span) x box_rows x 1.
+int make_map(CUtensorMap* map, const void* base, int D, int S, long long BH, int box_rows, int swb,
+             bool bf16 = false) {
     auto enc = encode_fn();
     if (!enc) return cuda_fail(cudaErrorNotSupported);
     cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(BH)};
@@ -131,9 +132,9 @@ int make_map(CUtensorMap* map, const void* base, int D, int S, long long BH, int
     cuuint32_t estr[3] = {1, 1, 1};
     const CUtensorMapSwizzle sw = swb == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
                                 : swb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
-    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                     const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return cuda_fail(cudaErrorInvalidValue);
     return KF_OK;
 }
@@ -324,9 +325,9 @@ int plan_for_call(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_
 
 // ------------------------------------------------------------------ launches
 template <int D>
-int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, float* O, float* Mi, float* Li,
+int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, void* O, float* Mi, float* Li,
                    int unnorm, int B, int H_q, int H_kv, int S_q, int S_kv, void* ws, cudaStream_t s,
-                   bool causal) {
+                   bool causal, int out_type) {
     using C = kf::PrefillCfg<D>;
     int bps = 0;
     int rc = causal ? kernel_setup<kf::prefill_fwd_kernel<D, true>>(C::SMEM_BYTES, C::THREADS, &bps)
@@ -342,8 +343,13 @@ int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, 
     if ((rc = make_map(&mv, V, D, S_kv, static_cast<long long>(B) * H_kv, kv_box, C::SWB)) != KF_OK) return rc;
     CUtensorMap mp;
     std::memset(&mp, 0, sizeof(mp));
-    if (C::TMA_STORE) {
+    if (C::TMA_STORE && out_type == kf::KF_OUT_F32) {
         if ((rc = make_map_f32(&mo, O, D, S_q, static_cast<long long>(B) * H_q, q_box)) != KF_OK) return rc;
+    } else if (C::TMA_STORE) {
+        // 16-bit O: 64-column (128-B) spans, 128-B swizzle.
+        if ((rc = make_map(&mo, O, D, S_q, static_cast<long long>(B) * H_q, q_box, 128,
+                           out_type == kf::KF_OUT_BF16)) != KF_OK)
+            return rc;
     } else {
         std::memset(&mo, 0, sizeof(mo));
     }
@@ -359,6 +365,7 @@ int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, 
     p.scale = 1.0f / std::sqrt(static_cast<float>(D));
     p.scale_log2 = p.scale * 1.4426950408889634f;
     p.unnormalized = unnorm;
+    p.out_type = out_type;
     p.timeout_ns = g_timeout_ns.load();
     p.q_box = q_box;
     p.kv_box = kv_box;
@@ -402,9 +409,9 @@ struct Paged {
 };
 
 template <int D, int MT>
-int launch_decode_t(const Plan& pl, const void* Q, const void* K, const void* V, float* O, float* Mi, float* Li,
+int launch_decode_t(const Plan& pl, const void* Q, const void* K, const void* V, void* O, float* Mi, float* Li,
                     int unnorm, int B, int H_q, int H_kv, int S_q, int S_kv, void* ws, cudaStream_t s,
-                    const Paged* pg) {
+                    const Paged* pg, int out_type) {
     using C = kf::DecodeCfg<D, MT>;
     int bps = 0;
     int rc = pg ? kernel_setup<kf::decode_fwd_kernel<D, MT, true>>(C::SMEM_BYTES, C::THREADS, &bps)
@@ -447,6 +454,7 @@ int launch_decode_t(const Plan& pl, const void* Q, const void* K, const void* V,
     p.scale = 1.0f / std::sqrt(static_cast<float>(D));
     p.scale_log2 = p.scale * 1.4426950408889634f;
     p.unnormalized = unnorm;
+    p.out_type = out_type;
     p.timeout_ns = g_timeout_ns.load();
     p.kv_box = pg ? C::TK : kv_box;
     dim3 grid(pl.n_split, H_kv * pl.n_rg, B);
@@ -458,11 +466,11 @@ int launch_decode_t(const Plan& pl, const void* Q, const void* K, const void* V,
     return e == cudaSuccess ? KF_OK : cuda_fail(e);
 }
 
-int launch_decode(const Plan& pl, int D, const void* Q, const void* K, const void* V, float* O, float* Mi,
+int launch_decode(const Plan& pl, int D, const void* Q, const void* K, const void* V, void* O, float* Mi,
                   float* Li, int unnorm, int B, int H_q, int H_kv, int S_q, int S_kv, void* ws, cudaStream_t s,
-                  const Paged* pg = nullptr) {
+                  const Paged* pg = nullptr, int out_type = kf::KF_OUT_F32) {
 #define KF_DEC(DV, MTV) \
-    return launch_decode_t<DV, MTV>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s, pg)
+    return launch_decode_t<DV, MTV>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s, pg, out_type)
     switch (D) {
         case 16: if (pl.mt == 2) KF_DEC(16, 2); KF_DEC(16, 1);
         case 64: if (pl.mt == 2) KF_DEC(64, 2); KF_DEC(64, 1);
@@ -472,13 +480,17 @@ int launch_decode(const Plan& pl, int D, const void* Q, const void* K, const voi
 #undef KF_DEC
 }
 
-int attn_core(const void* Q, const void* K, const void* V, float* O, float* Mi, float* Li, int unnorm, int B,
+int attn_core(const void* Q, const void* K, const void* V, void* O, float* Mi, float* Li, int unnorm, int B,
               int H_q, int H_kv, int S_q, int S_kv, int D, void* ws, size_t ws_bytes, void* stream,
               unsigned flags = 0) {
-    int rc = validate(Q, K, V, O, B, H_q, H_kv, S_q, S_kv, D);
+    int rc = validate(Q, K, V, static_cast<const float*>(O), B, H_q, H_kv, S_q, S_kv, D);
     if (rc != KF_OK) return rc;
-    if (flags & ~static_cast<unsigned>(KF_FLAG_CAUSAL)) return KF_ERR_INVALID_ARG;
+    if (flags & ~static_cast<unsigned>(KF_FLAG_CAUSAL | KF_FLAG_OUT_F16 | KF_FLAG_OUT_BF16)) return KF_ERR_INVALID_ARG;
+    if ((flags & KF_FLAG_OUT_F16) && (flags & KF_FLAG_OUT_BF16)) return KF_ERR_INVALID_ARG;
     const bool causal = (flags & KF_FLAG_CAUSAL) != 0;
+    const int out_type = (flags & KF_FLAG_OUT_F16) ? kf::KF_OUT_F16
+                       : (flags & KF_FLAG_OUT_BF16) ? kf::KF_OUT_BF16 : kf::KF_OUT_F32;
+    if (unnorm && out_type != kf::KF_OUT_F32) return KF_ERR_INVALID_ARG;   // partials stay fp32
     if (causal && S_q > S_kv) return KF_ERR_INVALID_ARG;   // rows with no visible key
     if (B == 0 || S_q == 0) return KF_OK;
     if (!ws) ws_bytes = 0;
@@ -488,13 +500,14 @@ int attn_core(const void* Q, const void* K, const void* V, float* O, float* Mi, 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (pl.path == 0) {
         switch (D) {
-            case 16: return launch_prefill<16>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s, causal);
-            case 64: return launch_prefill<64>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s, causal);
-            case 128: return launch_prefill<128>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s, causal);
-            default: return launch_prefill<256>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s, causal);
+            case 16: return launch_prefill<16>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s, causal, out_type);
+            case 64: return launch_prefill<64>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s, causal, out_type);
+            case 128: return launch_prefill<128>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s, causal, out_type);
+            default: return launch_prefill<256>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s, causal, out_type);
         }
     }
-    return launch_decode(pl, D, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, pl.n_split > 1 ? ws : nullptr, s);
+    return launch_decode(pl, D, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, pl.n_split > 1 ? ws : nullptr, s,
+                         nullptr, out_type);
 }
 
 int paged_core(const void* Q, const void* K_pool, const void* V_pool, const int* block_table, const int* seq_lens,
@@ -595,7 +608,7 @@ int kf_attn_fwd_lse(const void* Q, const void* K, const void* V, float* O, float
     return attn_core(Q, K, V, O, Mi, Li, 0, B, H_q, H_kv, S_q, S_kv, D, workspace, workspace_bytes, stream);
 }
 
-int kf_attn_fwd_ex(const void* Q, const void* K, const void* V, float* O, float* Mi, float* Li, int B, int H_q,
+int kf_attn_fwd_ex(const void* Q, const void* K, const void* V, void* O, float* Mi, float* Li, int B, int H_q,
                    int H_kv, int S_q, int S_kv, int D, unsigned flags, void* workspace, size_t workspace_bytes,
                    void* stream) {
     return attn_core(Q, K, V, O, Mi, Li, 0, B, H_q, H_kv, S_q, S_kv, D, workspace, workspace_bytes, stream, flags);

@@ -8,6 +8,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -414,6 +415,29 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ uint32_t pack_bf162(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Output element types (the O tensor of the forward).
+enum : int { KF_OUT_F32 = 0, KF_OUT_F16 = 1, KF_OUT_BF16 = 2 };
+
+// Two outputs packed for a 16-bit output type.
+__device__ __forceinline__ uint32_t pack_out2(float lo, float hi, int out) {
+    return out == KF_OUT_BF16 ? pack_bf162(lo, hi) : pack_half2(lo, hi);
+}
+
+// Four consecutive outputs at element index idx (a multiple of 4) of O.
+__device__ __forceinline__ void store_out4(void* O, size_t idx, float4 v, int out) {
+    if (out == KF_OUT_F32) {
+        *reinterpret_cast<float4*>(static_cast<float*>(O) + idx) = v;
+    } else {
+        *reinterpret_cast<uint2*>(static_cast<uint16_t*>(O) + idx) =
+            make_uint2(pack_out2(v.x, v.y, out), pack_out2(v.z, v.w, out));
+    }
 }
 
 // Byte offset of element (row, col) of a [rows x D] fp16 tile that TMA wrote

@@ -84,7 +84,7 @@ struct PrefillCfg {
 };
 
 struct PrefillParams {
-    float* O;
+    void* O;            // [B,H_q,S_q,D] of out_type (fp32 when unnormalized)
     float* Mi;   // nullable
     float* Li;   // nullable
     int H_q, H_kv, S_q, S_kv, G;
@@ -92,6 +92,7 @@ struct PrefillParams {
     float scale_log2;   // (1/sqrt(D)) * log2(e)
     float scale;        // 1/sqrt(D)
     int unnormalized;   // 1: write O_u = sum exp(s - Mi) v (partial form), Mi/Li required
+    int out_type;       // KF_OUT_F32 / KF_OUT_F16 / KF_OUT_BF16
     int q_box;          // rows per Q TMA box: min(BM, S_q)
     int kv_box;         // rows per K/V TMA box: min(BC, S_kv)
     // Work list (1-D grid).  Unit u = (b, h_q, 256-row block) with the block index
@@ -163,39 +164,63 @@ __device__ __forceinline__ PrefillItem prefill_item(const PrefillParams& p, int 
 }
 
 // Writes a tile's O (scaled by sc) from TMEM through a free K/V ring slot: passes of
-// the slot's size, each staged as 128-B swizzled fp32 spans of 32 columns (the
-// map's swizzle) and TMA-stored; rows past the tensor are dropped.  Called by the
-// tile's 128 softmax threads; named barrier `bar` orders the passes.  With
-// `complete`, thread row 0 waits until the stores are written, else until read.
+// the slot's size, each staged as 128-B swizzled spans (32 fp32 or 64 fp16/bf16
+// columns, the map's box and swizzle) and TMA-stored; rows past the tensor are
+// dropped.  Called by the tile's 128 softmax threads; named barrier `bar` orders the
+// passes.  With `complete`, thread row 0 waits until the stores are written, else
+// until read.
 template <int D, int BM, int SLOT_BYTES>
-__device__ __forceinline__ void stage_store_tile(uint8_t* slot, uint32_t tO, int row, int bar, float sc,
+__device__ __forceinline__ void stage_store_tile(uint8_t* slot, uint32_t tO, int row, int bar, float sc, int out,
                                                  const CUtensorMap* map, int c1, int c2, bool complete) {
     constexpr int SPAN = BM * 128;
     constexpr int SPP = SLOT_BYTES / SPAN;                // spans per pass
-    static_assert(SPP >= 1 && (D / 32) % SPP == 0, "staging slot");
-    constexpr int NPASS = (D / 32) / SPP;
+    static_assert(SPP >= 1, "staging slot");
+    const int cols = out == KF_OUT_F32 ? 32 : 64;         // columns per 128-B span
+    const int n_spans = D / cols;
+    const int n_pass = (n_spans + SPP - 1) / SPP;
 #pragma unroll 1
-    for (int ps = 0; ps < NPASS; ++ps) {
-#pragma unroll
-        for (int k = 0; k < SPP; ++k) {
-            uint32_t o[32];
-            tmem_ld32(tO + (ps * SPP + k) * 32, o);
-            tmem_wait_ld();
+    for (int ps = 0; ps < n_pass; ++ps) {
+        const int k_end = min(SPP, n_spans - ps * SPP);
+#pragma unroll 1
+        for (int k = 0; k < k_end; ++k) {
+            const int sp = ps * SPP + k;
             uint8_t* rowp = slot + k * SPAN + row * 128;
+            if (out == KF_OUT_F32) {
+                uint32_t o[32];
+                tmem_ld32(tO + sp * 32, o);
+                tmem_wait_ld();
 #pragma unroll
-            for (int q = 0; q < 8; ++q)
-                *reinterpret_cast<float4*>(rowp + ((q ^ (row & 7)) << 4)) =
-                    make_float4(__uint_as_float(o[4 * q]) * sc, __uint_as_float(o[4 * q + 1]) * sc,
-                                __uint_as_float(o[4 * q + 2]) * sc, __uint_as_float(o[4 * q + 3]) * sc);
+                for (int q = 0; q < 8; ++q)
+                    *reinterpret_cast<float4*>(rowp + ((q ^ (row & 7)) << 4)) =
+                        make_float4(__uint_as_float(o[4 * q]) * sc, __uint_as_float(o[4 * q + 1]) * sc,
+                                    __uint_as_float(o[4 * q + 2]) * sc, __uint_as_float(o[4 * q + 3]) * sc);
+            } else {
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {              // 32 columns -> 4 chunks of 16 B
+                    uint32_t o[32];
+                    tmem_ld32(tO + sp * 64 + hh * 32, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        uint4 w;
+                        w.x = pack_out2(__uint_as_float(o[8 * q]) * sc, __uint_as_float(o[8 * q + 1]) * sc, out);
+                        w.y = pack_out2(__uint_as_float(o[8 * q + 2]) * sc, __uint_as_float(o[8 * q + 3]) * sc, out);
+                        w.z = pack_out2(__uint_as_float(o[8 * q + 4]) * sc, __uint_as_float(o[8 * q + 5]) * sc, out);
+                        w.w = pack_out2(__uint_as_float(o[8 * q + 6]) * sc, __uint_as_float(o[8 * q + 7]) * sc, out);
+                        const int cq = hh * 4 + q;
+                        *reinterpret_cast<uint4*>(rowp + ((cq ^ (row & 7)) << 4)) = w;
+                    }
+                }
+            }
         }
         fence_proxy_async_smem();
         named_bar_sync(bar, 128);
         if (row == 0) {
-            for (int k = 0; k < SPP; ++k) tma_store_3d(map, slot + k * SPAN, (ps * SPP + k) * 32, c1, c2);
+            for (int k = 0; k < k_end; ++k) tma_store_3d(map, slot + k * SPAN, (ps * SPP + k) * cols, c1, c2);
             bulk_commit_group();
-            if (complete && ps + 1 == NPASS) bulk_wait_group0(); else bulk_wait_group_read0();
+            if (complete && ps + 1 == n_pass) bulk_wait_group0(); else bulk_wait_group_read0();
         }
-        if (ps + 1 < NPASS) named_bar_sync(bar, 128);      // slot read: next pass may write it
+        if (ps + 1 < n_pass) named_bar_sync(bar, 128);    // slot read: next pass may write it
     }
 }
 
@@ -615,7 +640,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             uint8_t* stage = sKV + ((pos0 + 2 * n_kv - 2 + t) % NSLOT) * C::KV_BYTES;
             const int qrow = q_row0 + t * BM + row;
             const bool store = qrow < p.S_q;
-            float* orow = p.O + ((static_cast<size_t>(b) * p.H_q + h) * p.S_q + (store ? qrow : 0)) * D;
+            const size_t orow = ((static_cast<size_t>(b) * p.H_q + h) * p.S_q + (store ? qrow : 0)) * D;   // element index
             const size_t mi = (static_cast<size_t>(b) * p.H_q + h) * p.S_q + (store ? qrow : 0);
             if (split) {
                 // KV chunk of a split unit: write this tile's partial (O_u, m, l) relative
@@ -633,8 +658,8 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     const float f = ex2_approx((m_ref - m_true) * c);
                     if constexpr (C::TMA_STORE) {
                         // The stores must be complete (not only read) before the ticket.
-                        stage_store_tile<D, BM, C::KV_BYTES>(stage, tO, row, 2 + t, f, &tmP, static_cast<int>(tile0),
-                                                            0, true);
+                        stage_store_tile<D, BM, C::KV_BYTES>(stage, tO, row, 2 + t, f, KF_OUT_F32, &tmP,
+                                                            static_cast<int>(tile0), 0, true);
                         if (row == 0) {
                             fence_proxy_async_global();
                             mbar_arrive(&stage_free[t]);
@@ -691,7 +716,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                             if (p.Li) p.Li[mi_l] = L;
                         }
                         const float* part_o = p.part + unit0 * D;
-                        float* obase = p.O + ((static_cast<size_t>(b) * p.H_q + h) * p.S_q) * D;
+                        const size_t obase = ((static_cast<size_t>(b) * p.H_q + h) * p.S_q) * D;       // element index
                         constexpr int RU = D <= 128 ? 8 : 4;          // rows in flight per lane
     #pragma unroll 1
                         for (int j0 = 0; j0 < 32; j0 += RU) {
@@ -727,7 +752,8 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                                     for (int ci = 0; ci < (D / 4 + 31) / 32; ++ci) {
                                         const int cidx = lane + ci * 32;
                                         if (cidx < D / 4)
-                                            reinterpret_cast<float4*>(obase + static_cast<size_t>(qr) * D)[cidx] = acc[u][ci];
+                                            store_out4(p.O, obase + static_cast<size_t>(qr) * D + cidx * 4, acc[u][ci],
+                                                       p.out_type);
                                     }
                                 }
                             }
@@ -745,8 +771,8 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     const float l_true = l * f;
                     const float osc = p.unnormalized ? f : 1.0f / l;
                     if constexpr (C::TMA_STORE) {
-                        stage_store_tile<D, BM, C::KV_BYTES>(stage, tO, row, 2 + t, osc, &tmO, q_row0 + t * BM,
-                                                            b * p.H_q + h, false);
+                        stage_store_tile<D, BM, C::KV_BYTES>(stage, tO, row, 2 + t, osc, p.out_type, &tmO,
+                                                            q_row0 + t * BM, b * p.H_q + h, false);
                         if (row == 0) mbar_arrive(&stage_free[t]);
                     } else {
 #pragma unroll
@@ -759,7 +785,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                                 for (int k = 0; k < OCH; k += 4) {
                                     float4 v = make_float4(__uint_as_float(o[k]) * osc, __uint_as_float(o[k + 1]) * osc,
                                                            __uint_as_float(o[k + 2]) * osc, __uint_as_float(o[k + 3]) * osc);
-                                    *reinterpret_cast<float4*>(orow + dc * OCH + k) = v;
+                                    store_out4(p.O, orow + dc * OCH + k, v, p.out_type);
                                 }
                             }
                         }

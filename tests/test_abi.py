@@ -95,11 +95,13 @@ def test_argument_validation_without_gpu(kf_lib):
         == L.KF_ERR_UNSUPPORTED_HEAD_DIM
     assert kf_lib.kf_attn_combine(FAKE, FAKE, FAKE, 2, FAKE, None, None, 0, 4, 8, 64, None) == L.KF_OK
     # kf_attn_fwd_ex: unknown flag bits and causal with S_q > S_kv are rejected before any launch.
-    assert kf_lib.kf_attn_fwd_ex(FAKE, FAKE, FAKE, FAKE, None, None, 1, 4, 2, 8, 8, 64, 2, None, 0, None) \
+    assert kf_lib.kf_attn_fwd_ex(FAKE, FAKE, FAKE, FAKE, None, None, 1, 4, 2, 8, 8, 64, 8, None, 0, None) \
         == L.KF_ERR_INVALID_ARG
     assert kf_lib.kf_attn_fwd_ex(FAKE, FAKE, FAKE, FAKE, None, None, 1, 4, 2, 9, 8, 64, L.KF_FLAG_CAUSAL, None, 0,
                                  None) == L.KF_ERR_INVALID_ARG
     assert kf_lib.kf_attn_fwd_ex(FAKE, FAKE, FAKE, FAKE, None, None, 0, 4, 2, 9, 8, 64, 0, None, 0, None) == L.KF_OK
+    assert kf_lib.kf_attn_fwd_ex(FAKE, FAKE, FAKE, FAKE, None, None, 1, 4, 2, 8, 8, 64,
+                                 L.KF_FLAG_OUT_F16 | L.KF_FLAG_OUT_BF16, None, 0, None) == L.KF_ERR_INVALID_ARG
     # Paged decode: bad block sizes, non-decode shapes and a zero pool are rejected before any launch.
     def _paged(B=2, Hq=8, Hkv=2, Sq=1, D=128, nb=64, bs=16, mb=8):
         return kf_lib.kf_attn_fwd_paged(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, None, None, B, Hq, Hkv, Sq, D, nb, bs, mb,

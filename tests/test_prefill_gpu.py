@@ -203,3 +203,41 @@ def test_causal_rejects_more_queries_than_keys(cuda):
     Q, K, V = normal_qkv(1, 2, 1, 65, 64, 64, seed=1)
     with pytest.raises(KFError):
         flash_attn_fwd(*(to_dev(x, cuda) for x in (Q, K, V)), causal=True)
+
+
+OUT16 = [
+    (1, 32, 8, 4096, 4096, 128, False),     # C2, tail split: partials fp32, merged O 16-bit
+    (2, 8, 2, 300, 1000, 128, True),
+    (1, 4, 1, 129, 129, 64, False),
+    (1, 2, 1, 257, 300, 256, False),
+    (1, 2, 2, 1000, 1000, 16, True),        # D=16: direct row stores
+    (4, 32, 8, 1, 4096, 128, False),        # decode, one split
+    (1, 32, 8, 1, 131072, 128, False),      # decode with KV split and merge
+]
+
+
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
+@pytest.mark.parametrize("shape", OUT16, ids=lambda s: "B{}_Hq{}_Hkv{}_Sq{}_Skv{}_D{}_c{}".format(*s))
+def test_half_precision_output(cuda, shape, dtype):
+    """O written as fp16 / bf16: the fp32 result rounded to nearest, within one output ulp
+    of the oracle plus the north-star bar."""
+    import torch
+
+    from oracle.attn_oracle import causal_attn_lse
+
+    from kernelfoundry_b200 import flash_attn_fwd
+
+    *dims, causal = shape
+    Q, K, V = normal_qkv(*dims, seed=7 * sum(dims))
+    q, k, v = (to_dev(x, cuda) for x in (Q, K, V))
+    tdt = getattr(torch, dtype)
+    got, Mi, Li = flash_attn_fwd(q, k, v, causal=causal, out_dtype=tdt, return_lse=True)
+    assert got.dtype == tdt
+    f32 = flash_attn_fwd(q, k, v, causal=causal)
+    # Same arithmetic, then one rounding: equals the fp32 output rounded to the type.
+    assert torch.equal(got, f32.to(tdt))
+    ref = (causal_attn_lse if causal else oracle64)(*(x.astype(np.float64) for x in (Q, K, V)))[0]
+    ulp = 2.0 ** -8 if dtype == "bfloat16" else 2.0 ** -11
+    g = got.float().cpu().numpy()
+    assert np.abs(g - ref).max() <= 2e-3 + ulp * np.abs(ref).max()
+    assert np.linalg.norm(g - ref) / np.linalg.norm(ref) <= 1e-3 + ulp
