@@ -155,3 +155,21 @@ def test_long_decode_forward_single_process(cuda):
     got = long_decode_forward(*(to_dev(x, cuda) for x in (Q, K, V)), out=out)
     assert got.data_ptr() == out.data_ptr()
     assert_close(out.cpu().numpy(), oracle64(Q, K, V)[0], "long decode, one rank")
+
+
+@pytest.mark.parametrize("nsplit", ["8", "16", "32"])
+def test_split_merge_paths(cuda, nsplit, monkeypatch):
+    """Forced split counts (KF_DECODE_NSPLIT): the last CTA's ticket merge of 8, 16 and 32
+    partials gives the oracle's result."""
+    import torch
+
+    from kernelfoundry_b200 import flash_attn_fwd, plan
+
+    monkeypatch.setenv("KF_DECODE_NSPLIT", nsplit)
+    Q, K, V = normal_qkv(2, 32, 8, 1, 40000, 128, seed=int(nsplit))
+    assert plan(2, 32, 8, 1, 40000, 128)["n_split"] == int(nsplit)
+    got, Mi, Li = (t.cpu().numpy() for t in flash_attn_fwd(*(to_dev(x, cuda) for x in (Q, K, V)), return_lse=True))
+    O, rMi, rLi = oracle64(Q, K, V)
+    assert_close(got, O, f"nsplit {nsplit}")
+    assert np.abs(Mi - rMi).max() < 1e-3
+    assert np.abs(Li / rLi - 1).max() < 1e-3
