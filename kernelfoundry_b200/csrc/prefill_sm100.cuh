@@ -537,96 +537,96 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             const int diag = CAUSAL ? q_row0 + t * BM + row + p.kv_off - kt0 * BC + 1 : 0;
             float m_ref = -CUDART_INF_F, m_true = -CUDART_INF_F, l = 0.f;
             for (int j = 0; j < n_kv; ++j) {
-                    ok = mbar_wait_bounded(&s_full[t], (sst + j) & 1, abort_flag, p.timeout_ns);
-                    ok = __all_sync(0xffffffffu, ok);
-                    if (!ok) { atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_MMA); break; }
-                    tc_fence_after();
-                    uint32_t sr[BC];
-    #pragma unroll
-                    for (int cc = 0; cc < BC / 32; ++cc)
-                        tmem_ld32(tS + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[cc * 32]));
-                    tmem_wait_ld();
-                    // Keys of this tile visible to this row: past S_kv (ragged end) and, with
-                    // the causal mask, past the row's diagonal read as -inf.
-                    int kv_valid = p.S_kv - (kt0 + j) * BC;
-                    if constexpr (CAUSAL) kv_valid = min(kv_valid, diag - j * BC);
-                    if (kv_valid < BC) {
-    #pragma unroll
-                        for (int cc = 0; cc < BC; ++cc)
-                            if (cc >= kv_valid) sr[cc] = __float_as_uint(-CUDART_INF_F);
-                    }
-    #define KF_S(i) __uint_as_float(sr[i])
-                    // Row max: three-input max, four independent chains.
-                    float mx0 = KF_S(0), mx1 = KF_S(1), mx2 = KF_S(2), mx3 = KF_S(3);
-    #pragma unroll
-                    for (int cc = 4; cc + 8 <= BC; cc += 8) {
-                        mx0 = fmax3f(mx0, KF_S(cc), KF_S(cc + 1));
-                        mx1 = fmax3f(mx1, KF_S(cc + 2), KF_S(cc + 3));
-                        mx2 = fmax3f(mx2, KF_S(cc + 4), KF_S(cc + 5));
-                        mx3 = fmax3f(mx3, KF_S(cc + 6), KF_S(cc + 7));
-                    }
-                    mx0 = fmax3f(mx0, KF_S(BC - 4), KF_S(BC - 3));
-                    mx1 = fmax3f(mx1, KF_S(BC - 2), KF_S(BC - 1));
-                    const float m_new = fmax3f(m_true, fmaxf(mx0, mx1), fmaxf(mx2, mx3));
-                    m_true = m_new;
-                    // Lazy rescale: keep the reference max unless the row max grew by
-                    // more than 2^8 (P <= 256 stays exact enough in fp16, l and O in fp32).
-                    bool rescale = false;
-                    float f = 1.0f;
-                    if (j == 0) {
+                ok = mbar_wait_bounded(&s_full[t], (sst + j) & 1, abort_flag, p.timeout_ns);
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) { atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_MMA); break; }
+                tc_fence_after();
+                uint32_t sr[BC];
+#pragma unroll
+                for (int cc = 0; cc < BC / 32; ++cc)
+                    tmem_ld32(tS + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[cc * 32]));
+                tmem_wait_ld();
+                // Keys of this tile visible to this row: past S_kv (ragged end) and, with
+                // the causal mask, past the row's diagonal read as -inf.
+                int kv_valid = p.S_kv - (kt0 + j) * BC;
+                if constexpr (CAUSAL) kv_valid = min(kv_valid, diag - j * BC);
+                if (kv_valid < BC) {
+#pragma unroll
+                    for (int cc = 0; cc < BC; ++cc)
+                        if (cc >= kv_valid) sr[cc] = __float_as_uint(-CUDART_INF_F);
+                }
+#define KF_S(i) __uint_as_float(sr[i])
+                // Row max: three-input max, four independent chains.
+                float mx0 = KF_S(0), mx1 = KF_S(1), mx2 = KF_S(2), mx3 = KF_S(3);
+#pragma unroll
+                for (int cc = 4; cc + 8 <= BC; cc += 8) {
+                    mx0 = fmax3f(mx0, KF_S(cc), KF_S(cc + 1));
+                    mx1 = fmax3f(mx1, KF_S(cc + 2), KF_S(cc + 3));
+                    mx2 = fmax3f(mx2, KF_S(cc + 4), KF_S(cc + 5));
+                    mx3 = fmax3f(mx3, KF_S(cc + 6), KF_S(cc + 7));
+                }
+                mx0 = fmax3f(mx0, KF_S(BC - 4), KF_S(BC - 3));
+                mx1 = fmax3f(mx1, KF_S(BC - 2), KF_S(BC - 1));
+                const float m_new = fmax3f(m_true, fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+                m_true = m_new;
+                // Lazy rescale: keep the reference max unless the row max grew by
+                // more than 2^8 (P <= 256 stays exact enough in fp16, l and O in fp32).
+                bool rescale = false;
+                float f = 1.0f;
+                if (j == 0) {
+                    m_ref = m_new;
+                } else {
+                    const bool need = (m_new - m_ref) * c > 8.0f;
+                    rescale = __any_sync(0xffffffffu, need);
+                    if (need) {
+                        f = ex2_approx((m_ref - m_new) * c);
                         m_ref = m_new;
-                    } else {
-                        const bool need = (m_new - m_ref) * c > 8.0f;
-                        rescale = __any_sync(0xffffffffu, need);
-                        if (need) {
-                            f = ex2_approx((m_ref - m_new) * c);
-                            m_ref = m_new;
-                            l *= f;
-                        }
+                        l *= f;
                     }
-                    if (rescale) {
-                        // O_t is stable here: PV_t(j-1) completed before S_t(j) was committed.
-    #pragma unroll
-                        for (int dc = 0; dc < D / RCH; ++dc) {
-                            uint32_t o[RCH];
-                            tmem_ld_chunk<RCH>(tO + dc * RCH, o);
-                            tmem_wait_ld();
-    #pragma unroll
-                            for (int k = 0; k < RCH; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * f);
-                            tmem_st_chunk<RCH>(tO + dc * RCH, o);
-                        }
+                }
+                if (rescale) {
+                    // O_t is stable here: PV_t(j-1) completed before S_t(j) was committed.
+#pragma unroll
+                    for (int dc = 0; dc < D / RCH; ++dc) {
+                        uint32_t o[RCH];
+                        tmem_ld_chunk<RCH>(tO + dc * RCH, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int k = 0; k < RCH; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * f);
+                        tmem_st_chunk<RCH>(tO + dc * RCH, o);
                     }
-                    // P = 2^(s*c - m_ref*c): paired FMA, MUFU ex2, paired row-sum adds;
-                    // packed to fp16 pairs in place (pair i/2 overwrites scores already
-                    // read) and written over the first BC/2 TMEM columns of S_t (this
-                    // thread's row), the A operand of the PV MMA.  Each half of the keys
-                    // is published on its own barrier (p_half, then p_full).
-                    const float2 c2 = make_float2(c, c);
-                    const float2 neg2 = make_float2(-m_ref * c, -m_ref * c);
-                    float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
-                    constexpr int HALF = BC / 2;
-    #pragma unroll
-                    for (int hf = 0; hf < 2; ++hf) {
-    #pragma unroll
-                        for (int i = hf * HALF; i < (hf + 1) * HALF; i += 4) {
-                            const float2 x0 = ffma2(make_float2(KF_S(i), KF_S(i + 1)), c2, neg2);
-                            const float2 x1 = ffma2(make_float2(KF_S(i + 2), KF_S(i + 3)), c2, neg2);
-                            const bool emu = (i % 16) >= 16 - C::EMU16;    // compile-time per i
-                            const float2 e0 = emu ? exp2_poly2(x0) : make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
-                            const float2 e1 = emu ? exp2_poly2(x1) : make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
-                            acc0 = fadd2(acc0, e0);
-                            acc1 = fadd2(acc1, e1);
-                            sr[i / 2] = pack_half2(e0.x, e0.y);
-                            sr[i / 2 + 1] = pack_half2(e1.x, e1.y);
-                        }
-                        tmem_st_chunk<HALF / 2>(tS + hf * (HALF / 2),
-                                                *reinterpret_cast<const uint32_t(*)[HALF / 2]>(&sr[hf * (HALF / 2)]));
-                        tmem_wait_st();      // this half of P (and any rescaled O) written before the MMA reads it
-                        tc_fence_before();
-                        mbar_arrive(hf == 0 ? &p_half[t] : &p_full[t]);
+                }
+                // P = 2^(s*c - m_ref*c): paired FMA, MUFU ex2, paired row-sum adds;
+                // packed to fp16 pairs in place (pair i/2 overwrites scores already
+                // read) and written over the first BC/2 TMEM columns of S_t (this
+                // thread's row), the A operand of the PV MMA.  Each half of the keys
+                // is published on its own barrier (p_half, then p_full).
+                const float2 c2 = make_float2(c, c);
+                const float2 neg2 = make_float2(-m_ref * c, -m_ref * c);
+                float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+                constexpr int HALF = BC / 2;
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+#pragma unroll
+                    for (int i = hf * HALF; i < (hf + 1) * HALF; i += 4) {
+                        const float2 x0 = ffma2(make_float2(KF_S(i), KF_S(i + 1)), c2, neg2);
+                        const float2 x1 = ffma2(make_float2(KF_S(i + 2), KF_S(i + 3)), c2, neg2);
+                        const bool emu = (i % 16) >= 16 - C::EMU16;    // compile-time per i
+                        const float2 e0 = emu ? exp2_poly2(x0) : make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
+                        const float2 e1 = emu ? exp2_poly2(x1) : make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
+                        acc0 = fadd2(acc0, e0);
+                        acc1 = fadd2(acc1, e1);
+                        sr[i / 2] = pack_half2(e0.x, e0.y);
+                        sr[i / 2 + 1] = pack_half2(e1.x, e1.y);
                     }
-    #undef KF_S
-                    l += (acc0.x + acc0.y) + (acc1.x + acc1.y);
+                    tmem_st_chunk<HALF / 2>(tS + hf * (HALF / 2),
+                                            *reinterpret_cast<const uint32_t(*)[HALF / 2]>(&sr[hf * (HALF / 2)]));
+                    tmem_wait_st();      // this half of P (and any rescaled O) written before the MMA reads it
+                    tc_fence_before();
+                    mbar_arrive(hf == 0 ? &p_half[t] : &p_full[t]);
+                }
+#undef KF_S
+                l += (acc0.x + acc0.y) + (acc1.x + acc1.y);
             }
             sst += n_kv;
             if (ok) {
@@ -695,19 +695,19 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                         const int wi = warp - 4;                      // 0 .. 4*nq_active-1
                         const int r = wi * 32 + lane;                 // row of the unit this lane weighs
                         float2 ml[4];
-    #pragma unroll
+#pragma unroll
                         for (int c2 = 0; c2 < 4; ++c2)
                             ml[c2] = c2 < p.split_k ? __ldcg(part_ml + unit0 + static_cast<size_t>(c2) * ROWS + r)
                                                     : make_float2(-CUDART_INF_F, 0.f);
                         const float M = fmaxf(fmaxf(ml[0].x, ml[1].x), fmaxf(ml[2].x, ml[3].x));
                         float w[4], L = 0.f;
-    #pragma unroll
+#pragma unroll
                         for (int c2 = 0; c2 < 4; ++c2) {
                             w[c2] = c2 < p.split_k ? ex2_approx((ml[c2].x - M) * c) : 0.f;
                             L += w[c2] * ml[c2].y;
                         }
                         const float osc = p.unnormalized ? 1.0f : 1.0f / L;
-    #pragma unroll
+#pragma unroll
                         for (int c2 = 0; c2 < 4; ++c2) w[c2] *= osc;
                         const int qrow_l = q_row0 + r;
                         if (qrow_l < p.S_q) {
@@ -718,21 +718,21 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                         const float* part_o = p.part + unit0 * D;
                         const size_t obase = ((static_cast<size_t>(b) * p.H_q + h) * p.S_q) * D;       // element index
                         constexpr int RU = D <= 128 ? 8 : 4;          // rows in flight per lane
-    #pragma unroll 1
+#pragma unroll 1
                         for (int j0 = 0; j0 < 32; j0 += RU) {
                             float4 acc[RU][(D / 4 + 31) / 32];
-    #pragma unroll
+#pragma unroll
                             for (int u = 0; u < RU; ++u) {
                                 const int rr = wi * 32 + j0 + u;
                                 float wj[4];
-    #pragma unroll
+#pragma unroll
                                 for (int c2 = 0; c2 < 4; ++c2) wj[c2] = __shfl_sync(0xffffffffu, w[c2], j0 + u);
-    #pragma unroll
+#pragma unroll
                                 for (int ci = 0; ci < (D / 4 + 31) / 32; ++ci) {
                                     const int cidx = lane + ci * 32;
                                     acc[u][ci] = make_float4(0.f, 0.f, 0.f, 0.f);
                                     if (cidx < D / 4) {
-    #pragma unroll
+#pragma unroll
                                         for (int c2 = 0; c2 < 4; ++c2) {
                                             if (c2 < p.split_k) {
                                                 const float4 v = __ldcg(reinterpret_cast<const float4*>(
@@ -744,11 +744,11 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                                     }
                                 }
                             }
-    #pragma unroll
+#pragma unroll
                             for (int u = 0; u < RU; ++u) {
                                 const int qr = q_row0 + wi * 32 + j0 + u;
                                 if (qr < p.S_q) {
-    #pragma unroll
+#pragma unroll
                                     for (int ci = 0; ci < (D / 4 + 31) / 32; ++ci) {
                                         const int cidx = lane + ci * 32;
                                         if (cidx < D / 4)
