@@ -388,30 +388,6 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
     return d;
 }
 
-// 2^x for a pair of arguments on the FMA/ALU pipes instead of MUFU.
-// Method: Cody-Waite style range reduction x = n + r with n = rint(x) (by the
-// 1.5*2^23 rounding constant) and r in [-0.5, 0.5]; 2^r by a degree-3
-// polynomial fitted here for minimum relative error (Chebyshev-node least
-// squares refined by Lawson iterations; max relative error 7.5e-5 in fp32,
-// below the 4.9e-4 rounding of the fp16 P it feeds); 2^n applied by adding
-// n to the exponent field.  Valid for x <= 8 (callers guarantee it); x is
-// clamped at -125 so the result stays a normal float (~2^-125, i.e. 0 in fp16).
-__device__ __forceinline__ float2 exp2_poly2(float2 x) {
-    constexpr float kRound = 12582912.0f;   // 1.5 * 2^23
-    constexpr float c0 = 0.9999280571937561f, c1 = 0.6932609677314758f;
-    constexpr float c2 = 0.2426111251115799f, c3 = 0.0551716648042202f;
-    x.x = fmaxf(x.x, -125.0f);
-    x.y = fmaxf(x.y, -125.0f);
-    const float2 t = fadd2(x, make_float2(kRound, kRound));          // low mantissa bits hold n
-    const float2 nf = fadd2(t, make_float2(-kRound, -kRound));
-    const float2 r = ffma2(nf, make_float2(-1.0f, -1.0f), x);         // r = x - n
-    float2 p = ffma2(make_float2(c3, c3), r, make_float2(c2, c2));
-    p = ffma2(p, r, make_float2(c1, c1));
-    p = ffma2(p, r, make_float2(c0, c0));
-    return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
-                       __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
-}
-
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&h);

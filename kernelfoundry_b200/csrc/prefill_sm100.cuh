@@ -61,14 +61,6 @@ struct PrefillCfg {
     static_assert(!TMA_STORE || BM * D * 4 <= (NQ == 2 ? NQ * Q_BYTES : NSLOT * KV_BYTES), "O staging area");
     // Registers after rebalancing (NQ == 2: 384 threads launch with 168 each):
     // control warpgroup 128 x 112 + softmax warpgroups 256 x 192 = 63488 <= 64512.
-    // Scores per 16 whose exp2 runs on the FMA pipe (exp2_poly2) instead of MUFU;
-    // a multiple of 4.  MUFU ex2 issues at a quarter of the FMA rate, so moving a
-    // few exps to the FMA pipe shortens the softmax when MUFU bounds it.
-#ifndef KF_PREFILL_EMU16
-#define KF_PREFILL_EMU16 0
-#endif
-    static constexpr int EMU16 = KF_PREFILL_EMU16;
-    static_assert(EMU16 % 4 == 0 && EMU16 <= 16, "EMU16 must be a multiple of 4");
 #ifndef KF_PREFILL_L2AHEAD
 #define KF_PREFILL_L2AHEAD 4
 #endif
@@ -611,9 +603,8 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     for (int i = hf * HALF; i < (hf + 1) * HALF; i += 4) {
                         const float2 x0 = ffma2(make_float2(KF_S(i), KF_S(i + 1)), c2, neg2);
                         const float2 x1 = ffma2(make_float2(KF_S(i + 2), KF_S(i + 3)), c2, neg2);
-                        const bool emu = (i % 16) >= 16 - C::EMU16;    // compile-time per i
-                        const float2 e0 = emu ? exp2_poly2(x0) : make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
-                        const float2 e1 = emu ? exp2_poly2(x1) : make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
+                        const float2 e0 = make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
+                        const float2 e1 = make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
                         acc0 = fadd2(acc0, e0);
                         acc1 = fadd2(acc1, e1);
                         sr[i / 2] = pack_half2(e0.x, e0.y);
