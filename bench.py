@@ -15,7 +15,8 @@ API (flash_attn_fwd) with the step's Q/K/V copied from pinned host memory and
 O copied back inside the timed region.  `extra` holds the decode configs
 (HBM GB/s with bytes = 2*B*H_kv*S_kv*D*2 + 2*B*H_q*D + 4*B*H_q*D; device time
 from CUDA-graph replay, the host-call time beside it), MQA D=64,
-prefill S=512 and, for N > 1, the KV-split long decode across the N GPUs.
+prefill S=512, RMSNorm / RoPE / SwiGLU (HBM GB/s of their algorithmic bytes)
+and, for N > 1, the KV-split long decode across the N GPUs.
 
 --impl reference times the reference's CPU path for the same workload: the
 NumPy reference_attn of kernel_models/flash_attn.py (restated in oracle/, the
@@ -393,6 +394,7 @@ def run_extras(args, rank, world, dev, peaks):
                                       "frac_tensor": round(tf / peaks["bf16_tflops"], 3),
                                       "flops": "4*D per visible (query, key) pair"}
     torch.cuda.empty_cache()
+    out.update(bench_pointwise(stream, gen, dev, peaks, iters))
     return out
 
 
@@ -430,6 +432,59 @@ def bench_paged(stream, gen, dev, peaks, l2, iters):
     return {"paged_decode_kv4096_B16_bs16": {"us": round(ms * 1e3, 2), "GB/s": round(gbs, 1),
                                              "frac_hbm": round(gbs / peaks["hbm_gbs"], 3),
                                              "host_call_us": round(host_ms * 1e3, 2), "rotated_sets": rot}}
+
+
+# RMSNorm / RoPE / SwiGLU on decoder-layer shapes of the same model family
+# (hidden = H_q * D = 4096; MLP width 14336; RoPE on the C2 batch-8 Q/K).
+# Every working set is above 2x L2, so each call streams from HBM.
+POINTWISE = {
+    # name: (description, algorithmic bytes per call)
+    "rmsnorm_add_T16384_H4096": ("fused residual add + RMSNorm, fp16 [16384, 4096]: read x and residual, "
+                                 "write residual and out", 4 * 16384 * 4096 * 2),
+    "rmsnorm_T16384_H4096": ("RMSNorm, fp16 [16384, 4096]: read x, write out", 2 * 16384 * 4096 * 2),
+    "rope_B8_S4096": ("NeoX RoPE in place on Q [8, 32, 4096, 128] and K [8, 8, 4096, 128] fp16, theta 5e5: "
+                      "read + write both", 2 * 8 * (H_Q + H_KV) * S * D * 2),
+    "swiglu_T8192_I14336": ("SwiGLU, fp16 gate_up [8192, 28672] -> out [8192, 14336]",
+                            8192 * 14336 * 3 * 2),
+}
+
+
+def pointwise_setup(name, gen, dev):
+    """Inputs for one POINTWISE entry; returns the call f(i)."""
+    import torch
+
+    from kernelfoundry_b200 import fused_add_rms_norm, rms_norm, rope_, swiglu
+
+    if name.startswith("rmsnorm"):
+        x = rand_f16((16384, 4096), gen, dev)
+        w = rand_f16((4096,), gen, dev)
+        o = torch.empty_like(x)
+        if name.startswith("rmsnorm_add"):
+            res = rand_f16((16384, 4096), gen, dev)
+            return lambda i: fused_add_rms_norm(x, res, w, 1e-5, out=o)
+        return lambda i: rms_norm(x, w, 1e-5, out=o)
+    if name.startswith("rope"):
+        q = rand_f16((8, H_Q, S, D), gen, dev)
+        k = rand_f16((8, H_KV, S, D), gen, dev)
+        return lambda i: rope_(q, k, theta=500000.0)
+    gu = rand_f16((8192, 2 * 14336), gen, dev)
+    o = torch.empty((8192, 14336), dtype=torch.float16, device=dev)
+    return lambda i: swiglu(gu, out=o)
+
+
+def bench_pointwise(stream, gen, dev, peaks, iters):
+    import torch
+
+    out = {}
+    for name, (desc, nbytes) in POINTWISE.items():
+        f = pointwise_setup(name, gen, dev)
+        ms = time_loop(f, iters, 3, stream)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"us": round(ms * 1e3, 2), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / peaks["hbm_gbs"], 3),
+                     "bytes": nbytes, "what": desc}
+        del f
+        torch.cuda.empty_cache()
+    return out
 
 
 def run_long_decode_split(args, rank, world, dev, peaks):
@@ -651,11 +706,17 @@ def run_case(args):
 
     from kernelfoundry_b200 import flash_attn_fwd, plan
 
-    B, Hq, Hkv, Sq, Skv, Dh = CASES[args.case]
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     gen = torch.Generator(device=dev)
     gen.manual_seed(77)
+    if args.case in POINTWISE:
+        desc, nbytes = POINTWISE[args.case]
+        ms = time_loop(pointwise_setup(args.case, gen, dev), args.steps, args.warmup, torch.cuda.current_stream(dev))
+        print(json.dumps({"case": args.case, "ms": round(ms, 5), "GB/s": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                          "bytes": nbytes, "what": desc}), flush=True)
+        return
+    B, Hq, Hkv, Sq, Skv, Dh = CASES[args.case]
     q = rand_f16((B, Hq, Sq, Dh), gen, dev)
     k = rand_f16((B, Hkv, Skv, Dh), gen, dev)
     v = rand_f16((B, Hkv, Skv, Dh), gen, dev)
@@ -680,7 +741,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true", help="headline only (skip decode/MQA/long-decode lines)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", choices=sorted(CASES), help="time one configuration only (for profiler captures)")
+    ap.add_argument("--case", choices=sorted(CASES) + sorted(POINTWISE),
+                    help="time one configuration only (for profiler captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)

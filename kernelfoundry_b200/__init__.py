@@ -8,6 +8,8 @@ include/kf_attn.h); this package is the Python host side.
   attention  torch-tensor API + the reference-compatible launcher
   multi_gpu  one-process-per-GPU sharding (batch / KV heads) and the
              cross-GPU split-KV decode (partials + NCCL all-gather + merge)
+  pointwise  RMSNorm (plain / fused residual), RoPE, SwiGLU
+             (C ABI: include/kf_pointwise.h)
   build      nvcc build of the library (sm_100a only)
 """
 from ._lib import KFError, lib  # noqa: F401
@@ -22,5 +24,7 @@ from .attention import (  # noqa: F401
     plan,
     workspace_bytes,
 )
+
+from .pointwise import fused_add_rms_norm, rms_norm, rope_, swiglu  # noqa: F401
 
 __version__ = "0.1.0"

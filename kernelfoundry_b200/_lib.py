@@ -1,4 +1,5 @@
-"""ctypes binding of libkf_attn.so (the C ABI declared in include/kf_attn.h).
+"""ctypes binding of libkf_attn.so (the C ABI declared in include/kf_attn.h and
+include/kf_pointwise.h).
 
 There is no fallback: if the library is missing this module raises, and every
 compute entry point goes through the CUDA kernels in the library.
@@ -23,13 +24,17 @@ KF_FLAG_CAUSAL = 1
 KF_FLAG_OUT_F16 = 2
 KF_FLAG_OUT_BF16 = 4
 
-# Every symbol include/kf_attn.h declares.
+KF_PW_BF16 = 1
+KF_ROPE_GPTJ = 2
+
+# Every symbol include/kf_attn.h and include/kf_pointwise.h declare.
 EXPORTED = [
     "kf_strerror", "kf_last_cuda_error", "kf_version",
     "kf_attn_fwd", "kf_attn_fwd_lse", "kf_attn_fwd_ex", "kf_attn_fwd_paged", "kf_attn_paged_workspace_bytes", "kf_attn_fwd_partial", "kf_attn_combine", "kf_attn_combine_packed",
     "kf_attn_workspace_bytes", "kf_attn_workspace_init", "kf_attn_plan",
     "kf_launch_flash_attn", "kf_attn_fwd_noalloc", "kf_device_error", "kf_set_wait_timeout_ns",
     "kf_selftest_wait_timeout",
+    "kf_rmsnorm", "kf_rope", "kf_swiglu",
 ]
 
 
@@ -94,6 +99,13 @@ def lib():
     L.kf_set_wait_timeout_ns.restype = None
     L.kf_selftest_wait_timeout.argtypes = [ctypes.c_ulonglong, P]
     L.kf_selftest_wait_timeout.restype = I
+    LL, U, F = ctypes.c_longlong, ctypes.c_uint, ctypes.c_float
+    L.kf_rmsnorm.argtypes = [P, P, P, P, LL, I, F, U, P]
+    L.kf_rmsnorm.restype = I
+    L.kf_rope.argtypes = [P, P, P, P, I, I, I, I, I, I, F, LL, LL, LL, LL, LL, LL, U, P]
+    L.kf_rope.restype = I
+    L.kf_swiglu.argtypes = [P, P, LL, I, U, P]
+    L.kf_swiglu.restype = I
     del FP
     _lib = L
     return _lib

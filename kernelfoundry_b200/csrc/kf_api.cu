@@ -16,8 +16,10 @@
 #include <mutex>
 
 #include "../../include/kf_attn.h"
+#include "../../include/kf_pointwise.h"
 #include "decode_sm100.cuh"
 #include "kf_ptx.cuh"
+#include "pointwise_sm100.cuh"
 #include "prefill_sm100.cuh"
 
 namespace kf {
@@ -759,6 +761,179 @@ int kf_attn_fwd_noalloc(const void* Q, const void* K, const void* V, float* O, i
     }
     return launch_decode(pl, D, Q, K, V, O, nullptr, nullptr, 0, B, H_q, H_kv, S_q, S_kv, scratch,
                          static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"
+
+// ---- RMSNorm / RoPE / SwiGLU -------------------------------------------------
+namespace {
+
+// Grid for a grid-stride pointwise kernel: as many blocks as are resident on
+// all SMs at once (occupancy cached per device and block size), at most
+// `needed`.  Block sizes are 256, 512 or 1024 threads.
+template <auto Kern>
+int pw_grid(int threads, long long needed, int* grid) {
+    static std::atomic<int> bps[kMaxDevices][3];
+    DeviceInfo* di = nullptr;
+    int rc = device_info(&di);
+    if (rc != KF_OK) return rc;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e);
+    const int slot = threads >= 1024 ? 2 : threads >= 512 ? 1 : 0;
+    int v = bps[dev][slot].load(std::memory_order_acquire);
+    if (v == 0) {
+        int n = 0;
+        if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, Kern, threads, 0)) != cudaSuccess)
+            return cuda_fail(e);
+        v = n > 0 ? n : 1;
+        bps[dev][slot].store(v, std::memory_order_release);
+    }
+    const long long cap = static_cast<long long>(di->sm_count) * v;
+    *grid = static_cast<int>(needed < cap ? needed : cap);
+    return KF_OK;
+}
+
+int launch_status() {
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? KF_OK : cuda_fail(e);
+}
+
+template <bool BF16, int VPT>
+int rmsnorm_t(const kf::RmsNormParams& p, int threads, cudaStream_t s) {
+    const int rpb = threads / p.G;
+    int grid = 0;
+    int rc = pw_grid<kf::rmsnorm_kernel<BF16, VPT>>(threads, (p.rows + rpb - 1) / rpb, &grid);
+    if (rc != KF_OK) return rc;
+    kf::rmsnorm_kernel<BF16, VPT><<<grid, threads, 0, s>>>(p);
+    return launch_status();
+}
+
+template <bool BF16>
+int rmsnorm_vpt(const kf::RmsNormParams& p, int vpt, int threads, cudaStream_t s) {
+    switch (vpt) {
+        case 1: return rmsnorm_t<BF16, 1>(p, threads, s);
+        case 2: return rmsnorm_t<BF16, 2>(p, threads, s);
+        case 4: return rmsnorm_t<BF16, 4>(p, threads, s);
+        default: return rmsnorm_t<BF16, 8>(p, threads, s);
+    }
+}
+
+template <bool BF16, bool NEOX>
+int rope_t(const kf::RopeParams& p, cudaStream_t s) {
+    int grid = 0;
+    int rc = pw_grid<kf::rope_kernel<BF16, NEOX>>(256, (p.n_tokens + p.TPB - 1) / p.TPB, &grid);
+    if (rc != KF_OK) return rc;
+    kf::rope_kernel<BF16, NEOX><<<grid, 256, 0, s>>>(p);
+    return launch_status();
+}
+
+template <bool BF16>
+int swiglu_t(const kf::SwigluParams& p, cudaStream_t s) {
+    int grid = 0;
+    int rc = pw_grid<kf::swiglu_kernel<BF16>>(256, p.rows, &grid);
+    if (rc != KF_OK) return rc;
+    kf::swiglu_kernel<BF16><<<grid, 256, 0, s>>>(p);
+    return launch_status();
+}
+
+bool stride_ok(long long st) { return st >= 0 && st % 8 == 0; }
+
+}  // namespace
+
+extern "C" {
+
+int kf_rmsnorm(const void* x, const void* weight, void* out, void* residual, long long rows, int hidden,
+               float eps, unsigned flags, void* stream) {
+    if (flags & ~static_cast<unsigned>(KF_PW_BF16)) return KF_ERR_INVALID_ARG;
+    if (rows < 0 || hidden < 8 || hidden > 32768 || hidden % 8 != 0) return KF_ERR_INVALID_ARG;
+    if (!(eps >= 0.f) || !std::isfinite(eps)) return KF_ERR_INVALID_ARG;
+    if (!x || !weight || !out) return KF_ERR_INVALID_ARG;
+    if (!aligned16(x) || !aligned16(weight) || !aligned16(out) || (residual && !aligned16(residual)))
+        return KF_ERR_MISALIGNED;
+    if (rows == 0) return KF_OK;
+    kf::RmsNormParams p;
+    p.x = static_cast<const uint4*>(x);
+    p.w = static_cast<const uint4*>(weight);
+    p.out = static_cast<uint4*>(out);
+    p.res = static_cast<uint4*>(residual);
+    p.rows = rows;
+    p.nvec = hidden / 8;
+    // Threads per row: enough for at most 8 vectors each up to 256 threads,
+    // at most 4 each beyond (1024 x 4 x 8 = 32768 elements).
+    int G = 1;
+    while (G * 8 < p.nvec) G <<= 1;
+    if (G > 256) {
+        G = 1;
+        while (G * 4 < p.nvec) G <<= 1;
+    }
+    const int per = (p.nvec + G - 1) / G;
+    int vpt = 1;
+    while (vpt < per) vpt <<= 1;                            // <= 8
+    p.G = G;
+    p.inv_hidden = 1.f / static_cast<float>(hidden);
+    p.eps = eps;
+    const int threads = G > 256 ? G : 256;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return (flags & KF_PW_BF16) ? rmsnorm_vpt<true>(p, vpt, threads, s) : rmsnorm_vpt<false>(p, vpt, threads, s);
+}
+
+int kf_rope(void* q, void* k, const int* positions, const float* inv_freq, int B, int S, int H_q, int H_kv,
+            int D, int rot_dim, float theta, long long q_stride_b, long long q_stride_h, long long q_stride_s,
+            long long k_stride_b, long long k_stride_h, long long k_stride_s, unsigned flags, void* stream) {
+    if (flags & ~static_cast<unsigned>(KF_PW_BF16 | KF_ROPE_GPTJ)) return KF_ERR_INVALID_ARG;
+    const bool neox = !(flags & KF_ROPE_GPTJ);
+    if (B < 0 || S < 0 || H_q < 0 || H_kv < 0 || H_q + H_kv < 1) return KF_ERR_INVALID_ARG;
+    if (D < 8 || D > 1024 || D % 8 != 0) return KF_ERR_INVALID_ARG;
+    if (rot_dim <= 0 || rot_dim > D || rot_dim % (neox ? 16 : 8) != 0) return KF_ERR_INVALID_ARG;
+    if (!inv_freq && !(theta > 0.f && std::isfinite(theta))) return KF_ERR_INVALID_ARG;
+    if (H_q > 0 && (!q || !stride_ok(q_stride_b) || !stride_ok(q_stride_h) || !stride_ok(q_stride_s)))
+        return KF_ERR_INVALID_ARG;
+    if (H_kv > 0 && (!k || !stride_ok(k_stride_b) || !stride_ok(k_stride_h) || !stride_ok(k_stride_s)))
+        return KF_ERR_INVALID_ARG;
+    if ((H_q > 0 && !aligned16(q)) || (H_kv > 0 && !aligned16(k))) return KF_ERR_MISALIGNED;
+    const long long n_tokens = static_cast<long long>(B) * S;
+    if (n_tokens == 0) return KF_OK;
+    kf::RopeParams p;
+    p.q = H_q > 0 ? static_cast<uint4*>(q) : nullptr;
+    p.k = H_kv > 0 ? static_cast<uint4*>(k) : nullptr;
+    p.pos = positions;
+    p.inv_freq = inv_freq;
+    p.q_sb = q_stride_b / 8; p.q_sh = q_stride_h / 8; p.q_ss = q_stride_s / 8;
+    p.k_sb = k_stride_b / 8; p.k_sh = k_stride_h / 8; p.k_ss = k_stride_s / 8;
+    p.n_tokens = n_tokens;
+    p.S = S;
+    p.H_q = H_q;
+    p.H_kv = H_kv;
+    p.rot_dim = rot_dim;
+    p.U = neox ? rot_dim / 16 : rot_dim / 8;                // 1..128
+    const int H = H_q + H_kv;
+    int hg = 64 / p.U;
+    if (hg < 1) hg = 1;
+    if (hg > H) hg = H;
+    p.HG = hg;
+    p.TPB = 256 / (p.U * hg);
+    if (p.TPB < 1) p.TPB = 1;
+    p.log2_theta = inv_freq ? 0.0 : std::log2(static_cast<double>(theta));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const bool bf16 = flags & KF_PW_BF16;
+    if (neox) return bf16 ? rope_t<true, true>(p, s) : rope_t<false, true>(p, s);
+    return bf16 ? rope_t<true, false>(p, s) : rope_t<false, false>(p, s);
+}
+
+int kf_swiglu(const void* gate_up, void* out, long long rows, int inter, unsigned flags, void* stream) {
+    if (flags & ~static_cast<unsigned>(KF_PW_BF16)) return KF_ERR_INVALID_ARG;
+    if (rows < 0 || inter < 8 || inter % 8 != 0) return KF_ERR_INVALID_ARG;
+    if (!gate_up || !out) return KF_ERR_INVALID_ARG;
+    if (!aligned16(gate_up) || !aligned16(out)) return KF_ERR_MISALIGNED;
+    if (rows == 0) return KF_OK;
+    kf::SwigluParams p;
+    p.gu = static_cast<const uint4*>(gate_up);
+    p.out = static_cast<uint4*>(out);
+    p.rows = rows;
+    p.ivec = inter / 8;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return (flags & KF_PW_BF16) ? swiglu_t<true>(p, s) : swiglu_t<false>(p, s);
 }
 
 int kf_selftest_wait_timeout(unsigned long long timeout_ns, void* stream) {

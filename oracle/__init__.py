@@ -13,6 +13,11 @@ Contents:
   ref_wrap.cu     Wrapper that compiles the unmodified reference sources into
                   oracle/_ref/libkfref.so (reference CPU code and CUDA kernel).
   Makefile        Builds lib/libkforacle.so and _ref/libkfref.so.
+  pointwise_oracle.py  RMSNorm / RoPE / SwiGLU in fp64 with explicit fp16 /
+                  bf16 rounding.  The reference has no code for these
+                  (README.md:16-18): parity against it is unpinned; the
+                  functions are pinned to transformers' Llama modules
+                  instead (tests/golden/make_pointwise_golden.py).
 
 Parity is pinned: tests/test_oracle.py checks these against golden vectors
 produced by the reference itself (tests/golden/make_golden.py).

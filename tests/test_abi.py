@@ -1,5 +1,6 @@
-"""The C-ABI library loads, exports what include/kf_attn.h declares, and
-validates arguments before touching a GPU (no compute calls here)."""
+"""The C-ABI library loads, exports what include/kf_attn.h and
+include/kf_pointwise.h declare, and validates arguments before touching a GPU
+(no compute calls here)."""
 from __future__ import annotations
 
 import ctypes
@@ -11,13 +12,15 @@ import pytest
 
 from conftest import REPO
 
-HEADER = os.path.join(REPO, "include", "kf_attn.h")
+HEADERS = [os.path.join(REPO, "include", h) for h in ("kf_attn.h", "kf_pointwise.h")]
 
 
 def _declared():
-    text = open(HEADER).read()
-    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(kf_[a-z_0-9]+)\s*\(", text)))
+    names = set()
+    for h in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", open(h).read(), flags=re.S)
+        names.update(re.findall(r"\b(kf_[a-z_0-9]+)\s*\(", text))
+    return sorted(names)
 
 
 def test_header_symbols_exported(kf_lib):
@@ -25,7 +28,8 @@ def test_header_symbols_exported(kf_lib):
     from kernelfoundry_b200.build import LIB_PATH
 
     declared = _declared()
-    assert len(declared) >= 14
+    assert len(declared) >= 17
+    assert {"kf_rmsnorm", "kf_rope", "kf_swiglu"} <= set(declared)
     assert sorted(declared) == sorted(_lib.EXPORTED)
     out = subprocess.run(["nm", "-D", "--defined-only", LIB_PATH], capture_output=True, text=True, check=True).stdout
     exported = set(re.findall(r"\bT (kf_\w+)", out))
@@ -127,6 +131,79 @@ def test_argument_validation_without_gpu(kf_lib):
     assert kf_lib.kf_attn_workspace_bytes(1, 6, 4, 1, 100, 128) == 0
     assert kf_lib.kf_launch_flash_attn(FAKE, FAKE, FAKE, FAKE, 1, 16, 1, 1, 48, None) \
         == L.KF_ERR_UNSUPPORTED_HEAD_DIM
+
+
+def test_pointwise_argument_validation_without_gpu(kf_lib):
+    from kernelfoundry_b200 import _lib as L
+
+    def rms(x=FAKE, w=FAKE, o=FAKE, r=None, rows=4, hidden=256, eps=1e-6, flags=0):
+        return kf_lib.kf_rmsnorm(x, w, o, r, rows, hidden, eps, flags, None)
+
+    assert rms(hidden=12) == L.KF_ERR_INVALID_ARG              # not a multiple of 8
+    assert rms(hidden=0) == L.KF_ERR_INVALID_ARG
+    assert rms(hidden=32776) == L.KF_ERR_INVALID_ARG           # above 32768
+    assert rms(rows=-1) == L.KF_ERR_INVALID_ARG
+    assert rms(eps=-1.0) == L.KF_ERR_INVALID_ARG
+    assert rms(eps=float("nan")) == L.KF_ERR_INVALID_ARG
+    assert rms(flags=4) == L.KF_ERR_INVALID_ARG
+    assert rms(w=ctypes.c_void_p(0)) == L.KF_ERR_INVALID_ARG
+    assert rms(x=MISALIGNED) == L.KF_ERR_MISALIGNED
+    assert rms(r=MISALIGNED) == L.KF_ERR_MISALIGNED
+    assert rms(rows=0) == L.KF_OK
+
+    def rope(q=FAKE, k=FAKE, B=1, S=8, Hq=4, Hkv=2, D=128, rot=128, theta=1e4, qs=(4096, 1024, 128),
+             ks=(2048, 1024, 128), flags=0, inv=None):
+        return kf_lib.kf_rope(q, k, None, inv, B, S, Hq, Hkv, D, rot, theta, *qs, *ks, flags, None)
+
+    assert rope(rot=136) == L.KF_ERR_INVALID_ARG               # rot_dim > D
+    assert rope(rot=40) == L.KF_ERR_INVALID_ARG                # NeoX needs a multiple of 16
+    assert rope(rot=40, flags=L.KF_ROPE_GPTJ) != L.KF_ERR_INVALID_ARG
+    assert rope(rot=36, flags=L.KF_ROPE_GPTJ) == L.KF_ERR_INVALID_ARG
+    assert rope(D=1032, rot=64) == L.KF_ERR_INVALID_ARG
+    assert rope(theta=0.0) == L.KF_ERR_INVALID_ARG
+    assert rope(theta=0.0, inv=FAKE) != L.KF_ERR_INVALID_ARG   # a frequency table replaces theta
+    assert rope(qs=(4096, 1024, 130)) == L.KF_ERR_INVALID_ARG  # stride not a multiple of 8
+    assert rope(ks=(-2048, 1024, 128)) == L.KF_ERR_INVALID_ARG
+    assert rope(k=ctypes.c_void_p(0)) == L.KF_ERR_INVALID_ARG
+    assert rope(k=ctypes.c_void_p(0), Hkv=0) != L.KF_ERR_INVALID_ARG
+    assert rope(Hq=0, Hkv=0) == L.KF_ERR_INVALID_ARG
+    assert rope(flags=8) == L.KF_ERR_INVALID_ARG
+    assert rope(q=MISALIGNED) == L.KF_ERR_MISALIGNED
+    assert rope(B=0) == L.KF_OK
+    assert rope(S=0) == L.KF_OK
+
+    def swiglu(g=FAKE, o=FAKE, rows=4, inter=256, flags=0):
+        return kf_lib.kf_swiglu(g, o, rows, inter, flags, None)
+
+    assert swiglu(inter=12) == L.KF_ERR_INVALID_ARG
+    assert swiglu(rows=-3) == L.KF_ERR_INVALID_ARG
+    assert swiglu(flags=2) == L.KF_ERR_INVALID_ARG
+    assert swiglu(o=ctypes.c_void_p(0)) == L.KF_ERR_INVALID_ARG
+    assert swiglu(o=MISALIGNED) == L.KF_ERR_MISALIGNED
+    assert swiglu(rows=0) == L.KF_OK
+
+
+@pytest.mark.skipif(os.path.exists("/dev/nvidia0"), reason="checks the no-driver path")
+def test_pointwise_compute_call_without_driver_reports_cuda_error(kf_lib):
+    from kernelfoundry_b200 import _lib as L
+
+    assert kf_lib.kf_rmsnorm(FAKE, FAKE, FAKE, None, 4, 256, 1e-6, 0, None) in (L.KF_ERR_CUDA,
+                                                                              L.KF_ERR_UNSUPPORTED_DEVICE)
+    assert kf_lib.kf_swiglu(FAKE, FAKE, 4, 256, 0, None) in (L.KF_ERR_CUDA, L.KF_ERR_UNSUPPORTED_DEVICE)
+
+
+def test_pointwise_python_api_refuses_cpu_tensors(kf_lib):
+    import torch
+
+    from kernelfoundry_b200 import rms_norm, rope_, swiglu
+
+    x = torch.zeros(4, 64, dtype=torch.float16)
+    with pytest.raises(ValueError, match="CUDA"):
+        rms_norm(x, torch.ones(64, dtype=torch.float16))
+    with pytest.raises(ValueError, match="CUDA"):
+        swiglu(x)
+    with pytest.raises(ValueError, match="CUDA"):
+        rope_(x.view(1, 1, 4, 64), None)
 
 
 @pytest.mark.skipif(os.path.exists("/dev/nvidia0"), reason="checks the no-driver path")
