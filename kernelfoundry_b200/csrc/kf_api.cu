@@ -799,33 +799,46 @@ int launch_status() {
     return e == cudaSuccess ? KF_OK : cuda_fail(e);
 }
 
-template <bool BF16, int VPT>
+template <bool BF16, int VPT, bool RES>
 int rmsnorm_t(const kf::RmsNormParams& p, int threads, cudaStream_t s) {
     const int rpb = threads / p.G;
     int grid = 0;
-    int rc = pw_grid<kf::rmsnorm_kernel<BF16, VPT>>(threads, (p.rows + rpb - 1) / rpb, &grid);
+    int rc = pw_grid<kf::rmsnorm_kernel<BF16, VPT, RES>>(threads, (p.rows + rpb - 1) / rpb, &grid);
     if (rc != KF_OK) return rc;
-    kf::rmsnorm_kernel<BF16, VPT><<<grid, threads, 0, s>>>(p);
+    kf::rmsnorm_kernel<BF16, VPT, RES><<<grid, threads, 0, s>>>(p);
     return launch_status();
 }
 
-template <bool BF16>
+template <bool BF16, bool RES>
 int rmsnorm_vpt(const kf::RmsNormParams& p, int vpt, int threads, cudaStream_t s) {
     switch (vpt) {
-        case 1: return rmsnorm_t<BF16, 1>(p, threads, s);
-        case 2: return rmsnorm_t<BF16, 2>(p, threads, s);
-        case 4: return rmsnorm_t<BF16, 4>(p, threads, s);
-        default: return rmsnorm_t<BF16, 8>(p, threads, s);
+        case 1: return rmsnorm_t<BF16, 1, RES>(p, threads, s);
+        case 2: return rmsnorm_t<BF16, 2, RES>(p, threads, s);
+        default: return rmsnorm_t<BF16, 4, RES>(p, threads, s);
     }
 }
 
-template <bool BF16, bool NEOX>
-int rope_t(const kf::RopeParams& p, cudaStream_t s) {
+template <bool BF16>
+int rmsnorm_dispatch(const kf::RmsNormParams& p, int vpt, int threads, cudaStream_t s) {
+    return p.res ? rmsnorm_vpt<BF16, true>(p, vpt, threads, s) : rmsnorm_vpt<BF16, false>(p, vpt, threads, s);
+}
+
+template <bool BF16, bool NEOX, int HB>
+int rope_hb(const kf::RopeParams& p, cudaStream_t s) {
     int grid = 0;
-    int rc = pw_grid<kf::rope_kernel<BF16, NEOX>>(256, (p.n_tokens + p.TPB - 1) / p.TPB, &grid);
+    int rc = pw_grid<kf::rope_kernel<BF16, NEOX, HB>>(256, (p.n_tokens + p.TPB - 1) / p.TPB, &grid);
     if (rc != KF_OK) return rc;
-    kf::rope_kernel<BF16, NEOX><<<grid, 256, 0, s>>>(p);
+    kf::rope_kernel<BF16, NEOX, HB><<<grid, 256, 0, s>>>(p);
     return launch_status();
+}
+
+template <bool BF16, bool NEOX>
+int rope_t(const kf::RopeParams& p, int hb, cudaStream_t s) {
+    switch (hb) {
+        case 1: return rope_hb<BF16, NEOX, 1>(p, s);
+        case 4: return rope_hb<BF16, NEOX, 4>(p, s);
+        default: return rope_hb<BF16, NEOX, 8>(p, s);
+    }
 }
 
 template <bool BF16>
@@ -861,21 +874,21 @@ int kf_rmsnorm(const void* x, const void* weight, void* out, void* residual, lon
     p.nvec = hidden / 8;
     // Threads per row: enough for at most 8 vectors each up to 256 threads,
     // at most 4 each beyond (1024 x 4 x 8 = 32768 elements).
+    // Threads per row: enough for at most 4 vectors each (1024 x 4 x 8 = 32768
+    // elements), which keeps a thread's row data at 16 registers (32 with
+    // the residual) and the SM's warps high enough to cover HBM latency.
     int G = 1;
-    while (G * 8 < p.nvec) G <<= 1;
-    if (G > 256) {
-        G = 1;
-        while (G * 4 < p.nvec) G <<= 1;
-    }
+    while (G * 4 < p.nvec) G <<= 1;
     const int per = (p.nvec + G - 1) / G;
     int vpt = 1;
-    while (vpt < per) vpt <<= 1;                            // <= 8
+    while (vpt < per) vpt <<= 1;                            // <= 4
     p.G = G;
     p.inv_hidden = 1.f / static_cast<float>(hidden);
     p.eps = eps;
     const int threads = G > 256 ? G : 256;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    return (flags & KF_PW_BF16) ? rmsnorm_vpt<true>(p, vpt, threads, s) : rmsnorm_vpt<false>(p, vpt, threads, s);
+    return (flags & KF_PW_BF16) ? rmsnorm_dispatch<true>(p, vpt, threads, s)
+                                : rmsnorm_dispatch<false>(p, vpt, threads, s);
 }
 
 int kf_rope(void* q, void* k, const int* positions, const float* inv_freq, int B, int S, int H_q, int H_kv,
@@ -907,18 +920,22 @@ int kf_rope(void* q, void* k, const int* positions, const float* inv_freq, int B
     p.H_kv = H_kv;
     p.rot_dim = rot_dim;
     p.U = neox ? rot_dim / 16 : rot_dim / 8;                // 1..128
+    // About 64 threads per token; each thread loads all of its HB head rows
+    // (HB in {1, 4, 8}) before it computes the token's angles, so one round
+    // trip to HBM covers the token whenever H <= 8 * (64 / U).
     const int H = H_q + H_kv;
-    int hg = 64 / p.U;
-    if (hg < 1) hg = 1;
-    if (hg > H) hg = H;
-    p.HG = hg;
-    p.TPB = 256 / (p.U * hg);
+    int hg_target = 64 / p.U;
+    if (hg_target < 1) hg_target = 1;
+    const int need = (H + hg_target - 1) / hg_target;
+    const int hb = need <= 1 ? 1 : need <= 4 ? 4 : 8;
+    p.HG = (H + hb - 1) / hb;
+    p.TPB = 256 / (p.U * p.HG);
     if (p.TPB < 1) p.TPB = 1;
     p.log2_theta = inv_freq ? 0.0 : std::log2(static_cast<double>(theta));
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const bool bf16 = flags & KF_PW_BF16;
-    if (neox) return bf16 ? rope_t<true, true>(p, s) : rope_t<false, true>(p, s);
-    return bf16 ? rope_t<true, false>(p, s) : rope_t<false, false>(p, s);
+    if (neox) return bf16 ? rope_t<true, true>(p, hb, s) : rope_t<false, true>(p, hb, s);
+    return bf16 ? rope_t<true, false>(p, hb, s) : rope_t<false, false>(p, hb, s);
 }
 
 int kf_swiglu(const void* gate_up, void* out, long long rows, int inter, unsigned flags, void* stream) {

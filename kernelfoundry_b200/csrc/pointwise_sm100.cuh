@@ -77,16 +77,15 @@ __device__ __forceinline__ void st_stream(uint4* p, uint4 v) { __stcs(p, v); }
 // ---- RMSNorm -------------------------------------------------------------------
 // One row of `hidden` = 8 * nvec elements is owned by a group of G threads
 // (G a power of two, 1..1024); thread r of the group holds vectors
-// r, r + G, ..., r + (VPT-1) G in registers between the sum of squares and the
-// scaling pass, so every input byte is read from HBM once.  Blocks hold
-// max(G, 256) / G row groups and stride over the rows.  VPT = 8 keeps 32
-// registers of row data, so its blocks stop at 256 threads (G <= 256); wider
-// rows use VPT <= 4 and up to 1024 threads.
+// r, r + G, ..., r + (VPT-1) G (VPT <= 4) in registers between the sum of
+// squares and the scaling pass, so every input byte is read from HBM once.
+// All of a row's loads (x, and the residual) are issued before its first
+// store.  Blocks hold max(G, 256) / G row groups and stride over the rows.
 struct RmsNormParams {
     const uint4* x;        // [rows, nvec] input
     const uint4* w;        // [nvec] weight
     uint4* out;            // [rows, nvec] output (may equal x)
-    uint4* res;            // [rows, nvec] residual, updated in place (nullptr: plain RMSNorm)
+    uint4* res;            // [rows, nvec] residual, updated in place (RES only)
     long long rows;
     int nvec;
     int G;                 // threads per row
@@ -94,8 +93,8 @@ struct RmsNormParams {
     float eps;
 };
 
-template <bool BF16, int VPT>
-__global__ void __launch_bounds__(VPT == 8 ? 256 : 1024) rmsnorm_kernel(const RmsNormParams p) {
+template <bool BF16, int VPT, bool RES>
+__global__ void __launch_bounds__(1024) rmsnorm_kernel(const RmsNormParams p) {
     __shared__ float red[32];
     const int G = p.G;
     const int r = threadIdx.x & (G - 1);
@@ -108,29 +107,28 @@ __global__ void __launch_bounds__(VPT == 8 ? 256 : 1024) rmsnorm_kernel(const Rm
         const long long row = base + gi;
         const bool valid = row < p.rows;
         const long long off = row * p.nvec;
-        uint4 v[VPT];
-        float ss = 0.f;
+        uint4 v[VPT], rv[VPT];
 #pragma unroll
         for (int k = 0; k < VPT; ++k) {
             const int c = r + k * G;
-            v[k] = make_uint4(0u, 0u, 0u, 0u);
-            if (valid && c < p.nvec) v[k] = ld_stream(p.x + off + c);
+            const bool in = valid && c < p.nvec;
+            v[k] = in ? ld_stream(p.x + off + c) : make_uint4(0u, 0u, 0u, 0u);
+            if constexpr (RES) rv[k] = in ? ld_stream(p.res + off + c) : make_uint4(0u, 0u, 0u, 0u);
         }
-        if (p.res) {
+        if constexpr (RES) {
 #pragma unroll
             for (int k = 0; k < VPT; ++k) {
                 const int c = r + k * G;
-                if (valid && c < p.nvec) {
-                    float a[8], b[8];
-                    unpack8<BF16>(v[k], a);
-                    unpack8<BF16>(ld_stream(p.res + off + c), b);
+                float a[8], b[8];
+                unpack8<BF16>(v[k], a);
+                unpack8<BF16>(rv[k], b);
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) a[e] += b[e];
-                    v[k] = pack8<BF16>(a);
-                    st_stream(p.res + off + c, v[k]);
-                }
+                for (int e = 0; e < 8; ++e) a[e] += b[e];
+                v[k] = pack8<BF16>(a);                   // rnd(x + res): exact sum, one rounding
+                if (valid && c < p.nvec) st_stream(p.res + off + c, v[k]);
             }
         }
+        float ss = 0.f;
 #pragma unroll
         for (int k = 0; k < VPT; ++k) {
             float a[8];
@@ -177,10 +175,11 @@ __global__ void __launch_bounds__(VPT == 8 ? 256 : 1024) rmsnorm_kernel(const Rm
 // [B, H, S, D] (the attention layout) and [B, S, H, D] work.  A "unit" is what
 // one thread rotates per head row: NeoX, 8 pairs = the 16-byte vector at
 // dims 8u.. and its partner at rot_dim/2 + 8u..; GPT-J, 4 pairs in one 16-byte
-// vector at dims 8u...  Thread (u, hg, tk) of a block owns unit u of the heads
-// hg, hg + HG, ... of one token per pass: the 4 or 8 angles are computed once
-// per token and reused across those heads, and the unit's frequencies once per
-// thread.
+// vector at dims 8u...  Thread (u, hg, tk) of a block owns unit u of the HB
+// heads hg, hg + HG, ... (HG * HB >= H_q + H_kv) of one token per pass: it
+// issues all of that token's loads first, then computes the 4 or 8 angles
+// once for all those heads, then rotates and stores.  The inverse
+// frequencies sit in shared memory (fp64, computed once per block).
 struct RopeParams {
     uint4* q;
     uint4* k;                     // nullptr when H_kv == 0
@@ -205,32 +204,26 @@ __device__ __forceinline__ float reduce_2pi(double a) {
     return static_cast<float>(r);
 }
 
-template <bool BF16, bool NEOX>
+template <bool BF16, bool NEOX, int HB>
 __global__ void __launch_bounds__(256) rope_kernel(const RopeParams p) {
     constexpr int NP = NEOX ? 8 : 4;                       // pairs per unit
-    constexpr int HB = 4;                                  // head rows in flight per thread
+    __shared__ double s_f[512];                            // inverse frequencies, rot_dim / 2 <= 512
+    for (int i = threadIdx.x; i < p.rot_dim / 2; i += blockDim.x)
+        s_f[i] = p.inv_freq ? static_cast<double>(p.inv_freq[i]) : exp2(-(2.0 * i / p.rot_dim) * p.log2_theta);
+    __syncthreads();
     const int u = threadIdx.x % p.U;
     const int rest = threadIdx.x / p.U;
     const int hg = rest % p.HG;
     const int tk = rest / p.HG;
     if (tk >= p.TPB) return;
-    double f[NP];
-#pragma unroll
-    for (int j = 0; j < NP; ++j) {
-        const int i = NP * u + j;                          // frequency index
-        f[j] = p.inv_freq ? static_cast<double>(p.inv_freq[i])
-                          : exp2(-(2.0 * i / p.rot_dim) * p.log2_theta);
-    }
+    const double* f = s_f + NP * u;
     const int H = p.H_q + p.H_kv;
     const long long half_vec = p.rot_dim / 16;             // NeoX partner offset, in vectors
     for (long long t = static_cast<long long>(blockIdx.x) * p.TPB + tk; t < p.n_tokens;
          t += static_cast<long long>(gridDim.x) * p.TPB) {
         const long long b = t / p.S;
         const long long s = t - b * p.S;
-        const double pos = p.pos ? static_cast<double>(__ldg(p.pos + t)) : static_cast<double>(s);
-        float cs[NP], sn[NP];
-#pragma unroll
-        for (int j = 0; j < NP; ++j) sincosf(reduce_2pi(pos * f[j]), &sn[j], &cs[j]);
+        const int pos_i = p.pos ? __ldg(p.pos + t) : static_cast<int>(s);
         for (int h0 = hg; h0 < H; h0 += HB * p.HG) {
             uint4* rowp[HB];
             uint4 a[HB], c[HB];
@@ -245,6 +238,9 @@ __global__ void __launch_bounds__(256) rope_kernel(const RopeParams p) {
                     if constexpr (NEOX) c[m] = rowp[m][half_vec + u];
                 }
             }
+            float cs[NP], sn[NP];
+#pragma unroll
+            for (int j = 0; j < NP; ++j) sincosf(reduce_2pi(static_cast<double>(pos_i) * f[j]), &sn[j], &cs[j]);
 #pragma unroll
             for (int m = 0; m < HB; ++m) {
                 if (!rowp[m]) continue;
@@ -276,7 +272,13 @@ __global__ void __launch_bounds__(256) rope_kernel(const RopeParams p) {
 
 // ---- SwiGLU --------------------------------------------------------------------
 // gate_up [rows, 2 * inter] (gate columns first, then up) -> out [rows, inter].
-// Blocks stride over rows; a block's threads stride over the row's vectors.
+// Blocks stride over rows; a block's threads stride over the row's vectors,
+// UNR vectors per thread per pass with all 2 * UNR loads issued first.
+// silu(g) = g / (1 + 2^(-g log2 e)) with the MUFU exponential and the fast
+// (reciprocal-multiply) division, ~2^-21 relative error in fp32, far below
+// the 16-bit rounding that follows.  The IEEE division made the kernel
+// issue-bound (5.1 TB/s against 6.0).  For g < -87.3 the denominator leaves the
+// fast division's range and the result is -0 (the true |silu| < 1e-36).
 struct SwigluParams {
     const uint4* gu;
     uint4* out;
@@ -286,20 +288,35 @@ struct SwigluParams {
 
 template <bool BF16>
 __global__ void __launch_bounds__(256) swiglu_kernel(const SwigluParams p) {
+    constexpr int UNR = 4;
     for (long long row = blockIdx.x; row < p.rows; row += gridDim.x) {
         const uint4* g = p.gu + row * 2 * p.ivec;
         const uint4* up = g + p.ivec;
         uint4* o = p.out + row * p.ivec;
-        for (int c = threadIdx.x; c < p.ivec; c += blockDim.x) {
-            float x[8], y[8];
-            unpack8<BF16>(ld_stream(g + c), x);
-            unpack8<BF16>(ld_stream(up + c), y);
+        for (int c0 = threadIdx.x; c0 < p.ivec; c0 += UNR * blockDim.x) {
+            uint4 gv[UNR], uv[UNR];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) x[e] = x[e] / (1.f + __expf(-x[e]));
-            round8<BF16>(x);                               // rnd(silu(g))
+            for (int j = 0; j < UNR; ++j) {
+                const int c = c0 + j * blockDim.x;
+                if (c < p.ivec) {
+                    gv[j] = ld_stream(g + c);
+                    uv[j] = ld_stream(up + c);
+                }
+            }
 #pragma unroll
-            for (int e = 0; e < 8; ++e) x[e] *= y[e];      // exact in fp32; rounded once by pack8
-            st_stream(o + c, pack8<BF16>(x));
+            for (int j = 0; j < UNR; ++j) {
+                const int c = c0 + j * blockDim.x;
+                if (c >= p.ivec) break;
+                float x[8], y[8];
+                unpack8<BF16>(gv[j], x);
+                unpack8<BF16>(uv[j], y);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) x[e] = __fdividef(x[e], 1.f + __expf(-x[e]));
+                round8<BF16>(x);                           // rnd(silu(g))
+#pragma unroll
+                for (int e = 0; e < 8; ++e) x[e] *= y[e];  // exact in fp32; rounded once by pack8
+                st_stream(o + c, pack8<BF16>(x));
+            }
         }
     }
 }

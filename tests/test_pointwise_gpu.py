@@ -232,3 +232,17 @@ def test_swiglu_special_values(cuda):
     gu = po.round_to(np.concatenate([g, u])[None, :], "f16")
     ref = po.swiglu(gu, "f16")
     _assert_ulps(_host(swiglu(_dev(gu, "f16", cuda))), ref, "f16", 2, 0.8, "special values")
+
+
+def test_swiglu_full_size_rows(cuda):
+    """The benchmark shape [8192, 2 x 14336]: a sample of rows matches the oracle."""
+    import torch
+
+    from kernelfoundry_b200 import swiglu
+
+    g = torch.Generator(device=cuda).manual_seed(8)
+    gu = (3 * torch.randn(8192, 2 * 14336, generator=g, device=cuda)).half()
+    y = swiglu(gu)
+    rows = np.random.default_rng(1).choice(8192, 64, replace=False)
+    ref = po.swiglu(_host(gu[torch.from_numpy(rows).to(cuda)]), "f16")
+    _assert_ulps(_host(y)[rows], ref, "f16", 2, 0.98, "full-size sample")
