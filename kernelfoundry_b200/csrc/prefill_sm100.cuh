@@ -29,6 +29,8 @@
 // and every role unwinds, drains its in-flight copies/MMAs, frees TMEM.
 #pragma once
 
+#include <type_traits>
+
 #include <math_constants.h>
 
 #include "kf_ptx.cuh"
@@ -542,11 +544,14 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 // the causal mask, past the row's diagonal read as -inf.
                 int kv_valid = p.S_kv - (kt0 + j) * BC;
                 if constexpr (CAUSAL) kv_valid = min(kv_valid, diag - j * BC);
-                if (kv_valid < BC) {
+                auto mask_s = [&]() {
+                    if (kv_valid < BC) {
 #pragma unroll
-                    for (int cc = 0; cc < BC; ++cc)
-                        if (cc >= kv_valid) sr[cc] = __float_as_uint(-CUDART_INF_F);
-                }
+                        for (int cc = 0; cc < BC; ++cc)
+                            if (cc >= kv_valid) sr[cc] = __float_as_uint(-CUDART_INF_F);
+                    }
+                };
+                mask_s();
 #define KF_S(i) __uint_as_float(sr[i])
                 // Row max: three-input max, four independent chains.
                 float mx0 = KF_S(0), mx1 = KF_S(1), mx2 = KF_S(2), mx3 = KF_S(3);
@@ -561,46 +566,19 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 mx1 = fmax3f(mx1, KF_S(BC - 2), KF_S(BC - 1));
                 const float m_new = fmax3f(m_true, fmaxf(mx0, mx1), fmaxf(mx2, mx3));
                 m_true = m_new;
-                // Lazy rescale: keep the reference max unless the row max grew by
-                // more than 2^8 (P <= 256 stays exact enough in fp16, l and O in fp32).
-                bool rescale = false;
-                float f = 1.0f;
-                if (j == 0) {
-                    m_ref = m_new;
-                } else {
-                    const bool need = (m_new - m_ref) * c > 8.0f;
-                    rescale = __any_sync(0xffffffffu, need);
-                    if (need) {
-                        f = ex2_approx((m_ref - m_new) * c);
-                        m_ref = m_new;
-                        l *= f;
-                    }
-                }
-                if (rescale) {
-                    // O_t is stable here: PV_t(j-1) completed before S_t(j) was committed.
-#pragma unroll
-                    for (int dc = 0; dc < D / RCH; ++dc) {
-                        uint32_t o[RCH];
-                        tmem_ld_chunk<RCH>(tO + dc * RCH, o);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int k = 0; k < RCH; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * f);
-                        tmem_st_chunk<RCH>(tO + dc * RCH, o);
-                    }
-                }
                 // P = 2^(s*c - m_ref*c): paired FMA, MUFU ex2, paired row-sum adds;
                 // packed to fp16 pairs in place (pair i/2 overwrites scores already
                 // read) and written over the first BC/2 TMEM columns of S_t (this
                 // thread's row), the A operand of the PV MMA.  Each half of the keys
                 // is published on its own barrier (p_half, then p_full).
-                const float2 c2 = make_float2(c, c);
-                const float2 neg2 = make_float2(-m_ref * c, -m_ref * c);
-                float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
                 constexpr int HALF = BC / 2;
+                float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+                auto exps = [&](auto lo_c, auto hi_c) {
+                    constexpr int LO = decltype(lo_c)::value, HI = decltype(hi_c)::value;
+                    const float2 c2 = make_float2(c, c);
+                    const float2 neg2 = make_float2(-m_ref * c, -m_ref * c);
 #pragma unroll
-                for (int hf = 0; hf < 2; ++hf) {
-#pragma unroll
-                    for (int i = hf * HALF; i < (hf + 1) * HALF; i += 4) {
+                    for (int i = LO; i < HI; i += 4) {
                         const float2 x0 = ffma2(make_float2(KF_S(i), KF_S(i + 1)), c2, neg2);
                         const float2 x1 = ffma2(make_float2(KF_S(i + 2), KF_S(i + 3)), c2, neg2);
                         const float2 e0 = make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
@@ -610,12 +588,59 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                         sr[i / 2] = pack_half2(e0.x, e0.y);
                         sr[i / 2 + 1] = pack_half2(e1.x, e1.y);
                     }
-                    tmem_st_chunk<HALF / 2>(tS + hf * (HALF / 2),
-                                            *reinterpret_cast<const uint32_t(*)[HALF / 2]>(&sr[hf * (HALF / 2)]));
-                    tmem_wait_st();      // this half of P (and any rescaled O) written before the MMA reads it
-                    tc_fence_before();
-                    mbar_arrive(hf == 0 ? &p_half[t] : &p_full[t]);
+                };
+                using Int0 = std::integral_constant<int, 0>;
+                using IntH = std::integral_constant<int, HALF>;
+                using IntB = std::integral_constant<int, BC>;
+                // Lazy rescale: keep the reference max unless the row max grew by
+                // more than 2^8 (P <= 256 stays exact enough in fp16, l and O in fp32).
+                // After the first step the first half's exps start from the current
+                // reference max while the row max is formed (no data dependence
+                // between them); if the check then asks for a rescale (rare), the
+                // scores are reloaded from TMEM and that half is redone.
+                if (j == 0) {
+                    m_ref = m_new;
+                    exps(Int0{}, IntH{});
+                } else {
+                    exps(Int0{}, IntH{});
+                    const bool need = (m_new - m_ref) * c > 8.0f;
+                    if (__any_sync(0xffffffffu, need)) {
+                        float f = 1.0f;
+                        if (need) {
+                            f = ex2_approx((m_ref - m_new) * c);
+                            m_ref = m_new;
+                            l *= f;
+                        }
+                        // O_t is stable here: PV_t(j-1) completed before S_t(j) was committed.
+#pragma unroll
+                        for (int dc = 0; dc < D / RCH; ++dc) {
+                            uint32_t o[RCH];
+                            tmem_ld_chunk<RCH>(tO + dc * RCH, o);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int k = 0; k < RCH; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * f);
+                            tmem_st_chunk<RCH>(tO + dc * RCH, o);
+                        }
+#pragma unroll
+                        for (int cc = 0; cc < HALF / 32; ++cc)
+                            tmem_ld32(tS + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[cc * 32]));
+                        tmem_wait_ld();
+                        mask_s();
+                        acc0 = make_float2(0.f, 0.f);
+                        acc1 = make_float2(0.f, 0.f);
+                        exps(Int0{}, IntH{});
+                    }
                 }
+                tmem_st_chunk<HALF / 2>(tS, *reinterpret_cast<const uint32_t(*)[HALF / 2]>(&sr[0]));
+                tmem_wait_st();          // first half of P (and any rescaled O) written before the MMA reads it
+                tc_fence_before();
+                mbar_arrive(&p_half[t]);
+                exps(IntH{}, IntB{});
+                tmem_st_chunk<HALF / 2>(tS + HALF / 2,
+                                        *reinterpret_cast<const uint32_t(*)[HALF / 2]>(&sr[HALF / 2]));
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(&p_full[t]);
 #undef KF_S
                 l += (acc0.x + acc0.y) + (acc1.x + acc1.y);
             }
