@@ -241,3 +241,34 @@ def test_half_precision_output(cuda, shape, dtype):
     g = got.float().cpu().numpy()
     assert np.abs(g - ref).max() <= 2e-3 + ulp * np.abs(ref).max()
     assert np.linalg.norm(g - ref) / np.linalg.norm(ref) <= 1e-3 + ulp
+
+
+@pytest.mark.parametrize("D,causal", [(128, False), (128, True), (64, False), (256, False)])
+def test_lazy_rescale_paths(cuda, D, causal):
+    """Scores that jump by more than 2^8 between KV tiles and between the two
+    halves of a tile, on some rows only: drives the O rescale, the reload of
+    the first half of S, and the warp-uniform decision with rows that do not
+    need it.  Random N(0,1) data almost never reaches these paths."""
+    import torch
+
+    from kernelfoundry_b200 import flash_attn_fwd
+
+    B, Hq, Hkv, S = 1, 4, 2, 1024
+    bc = 128 if D <= 128 else 64
+    rng = np.random.default_rng(D + causal)
+    Q = rng.standard_normal((B, Hq, S, D)).astype(np.float16)
+    K = rng.standard_normal((B, Hkv, S, D)).astype(np.float16)
+    V = rng.standard_normal((B, Hkv, S, D)).astype(np.float16)
+    s = np.arange(S)
+    # Feature 0 carries a bias: +8 per KV tile and +4 in the second half of each
+    # tile; query rows alternate between feeling it (q0 = 16) and not (q0 = 0).
+    K[..., 0] = (8 * (s // bc) + 4 * ((s % bc) >= bc // 2)).astype(np.float16)
+    Q[..., 0] = np.where((np.arange(S) // 3) % 2 == 0, 16.0, 0.0).astype(np.float16)
+    q, k, v = (torch.from_numpy(x).to(cuda) for x in (Q, K, V))
+    got = flash_attn_fwd(q, k, v, causal=causal).cpu().numpy()
+    if causal:
+        from oracle.attn_oracle import causal_attn_lse
+        ref = causal_attn_lse(Q.astype(np.float64), K.astype(np.float64), V.astype(np.float64))[0]
+    else:
+        ref = oracle64(Q, K, V)[0]
+    assert_close(got, ref, f"rescale D={D} causal={causal}")
