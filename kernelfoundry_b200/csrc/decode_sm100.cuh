@@ -443,17 +443,21 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         *reinterpret_cast<float2*>(p.part_ml + (unit_off + static_cast<size_t>(split) * nrows + tid) * 2) =
             make_float2(Mrow[tid], Lrow[tid]);
     }
-    __threadfence();
+    // Publication: the CTA barrier orders every thread's partial stores before
+    // thread 0's ticket, a release-acquire atomic at GPU scope (one round trip,
+    // no separate fence); the merging CTA's acquire and barrier order its reads
+    // after all of them, and the proxy fences cover its bulk (async-proxy) copies
+    // (into shared memory this CTA's threads wrote during the reduction, too).
     fence_proxy_async_global();
+    fence_proxy_async_smem();
     __syncthreads();
     const size_t cidx = (static_cast<size_t>(b) * p.H_kv + hk) * p.n_rg + rg;
     if (tid == 0) {
-        const unsigned ticket = atomicAdd(&p.counters[cidx], 1u);
+        const unsigned ticket = atom_add_acq_rel_gpu(&p.counters[cidx], 1u);
         *is_last = (ticket == static_cast<unsigned>(ns - 1)) ? 1 : 0;
     }
     __syncthreads();
     if (!*is_last) return;
-    __threadfence();
     fence_proxy_async_global();
 
     // ---- last CTA of this unit: merge all splits.
@@ -466,6 +470,25 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
     float* sM = swt + C::MAX_SPLIT * QROWS;
     float* sL = sM + QROWS;
     const float* ml = p.part_ml + unit_off * 2;
+    constexpr int KMAX = (QROWS * (D / 4) + C::THREADS - 1) / C::THREADS;
+    const int items = nrows * (D / 4);
+    const uint32_t split_bytes = static_cast<uint32_t>(nrows) * D * 4;
+    const int buf_bytes = ((C::BIG - WT_BYTES) / 2) / 16 * 16;
+    int per_chunk = buf_bytes / static_cast<int>(split_bytes);
+    per_chunk = per_chunk < 1 ? 1 : (per_chunk > ns ? ns : per_chunk);
+    const int n_chunks = (ns + per_chunk - 1) / per_chunk;
+    const float* src = p.part_O + unit_off * D;
+    auto issue = [&](int ch) {
+        const int s0 = ch * per_chunk;
+        const int cnt = min(per_chunk, ns - s0);
+        uint64_t* bar = &merge_bar[ch & 1];
+        mbar_arrive_expect_tx(bar, cnt * split_bytes);
+        bulk_g2s(sBig + (ch & 1) * buf_bytes, src + static_cast<size_t>(s0) * nrows * D, cnt * split_bytes, bar);
+    };
+    if (tid == 0) {           // the partials' copies fly while the weights are formed
+        issue(0);
+        if (n_chunks > 1) issue(1);
+    }
     for (int r = warp; r < nrows; r += NW + 1) {
         float M = -CUDART_INF_F;
         for (int s2 = lane; s2 < ns; s2 += 32) M = fmaxf(M, __ldcg(ml + (s2 * nrows + r) * 2));
@@ -488,25 +511,6 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
     }
     __syncthreads();
 
-    constexpr int KMAX = (QROWS * (D / 4) + C::THREADS - 1) / C::THREADS;
-    const int items = nrows * (D / 4);
-    const uint32_t split_bytes = static_cast<uint32_t>(nrows) * D * 4;
-    const int buf_bytes = ((C::BIG - WT_BYTES) / 2) / 16 * 16;
-    int per_chunk = buf_bytes / static_cast<int>(split_bytes);
-    per_chunk = per_chunk < 1 ? 1 : (per_chunk > ns ? ns : per_chunk);
-    const int n_chunks = (ns + per_chunk - 1) / per_chunk;
-    const float* src = p.part_O + unit_off * D;
-    auto issue = [&](int ch) {
-        const int s0 = ch * per_chunk;
-        const int cnt = min(per_chunk, ns - s0);
-        uint64_t* bar = &merge_bar[ch & 1];
-        mbar_arrive_expect_tx(bar, cnt * split_bytes);
-        bulk_g2s(sBig + (ch & 1) * buf_bytes, src + static_cast<size_t>(s0) * nrows * D, cnt * split_bytes, bar);
-    };
-    if (tid == 0) {
-        issue(0);
-        if (n_chunks > 1) issue(1);
-    }
     float4 acc[KMAX];
 #pragma unroll
     for (int k = 0; k < KMAX; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);

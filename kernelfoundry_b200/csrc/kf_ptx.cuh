@@ -164,6 +164,14 @@ __device__ __forceinline__ void fence_proxy_async_global() {
     asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
+// atomicAdd with acquire-release semantics at GPU scope (orders this thread's
+// earlier accesses, and what a CTA barrier ordered before them, with the add).
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* ptr, unsigned v) {
+    unsigned old;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(ptr), "r"(v) : "memory");
+    return old;
+}
+
 // Untiled bulk copy global -> shared (no multicast), completing on `bar`.
 // Both addresses 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
