@@ -540,11 +540,50 @@ def run_long_decode_split(args, rank, world, dev, peaks):
     graph_ms = e0.elapsed_time(e1) / iters
     del g                                   # graphs holding NCCL work go before the process group
     torch.cuda.synchronize()
-    host_ms, graph_ms = max_over_ranks([host_ms, graph_ms], world, dev)
+    # The same step with the NVLink peer exchange (no NCCL): partial kernel + one
+    # exchange-and-merge kernel, host-driven and as a CUDA graph.
+    from kernelfoundry_b200.multi_gpu import PeerExchange
+
+    ex = PeerExchange(tuple(q.shape), device=dev)
+
+    def step_p2p(_):
+        long_decode_forward(q, k, v, exchange=ex, out=out)
+
+    dist.barrier(device_ids=[dev.index])
+    p2p_host_ms = time_loop(step_p2p, iters, 3, stream)
+    with torch.cuda.stream(side):
+        for i in range(3):
+            step_p2p(i)
+    stream.wait_stream(side)
+    torch.cuda.synchronize()
+    dist.barrier(device_ids=[dev.index])
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step_p2p(0)
+    g.replay()
+    torch.cuda.synchronize()
+    dist.barrier(device_ids=[dev.index])
+    e0.record(stream)
+    for _ in range(iters):
+        g.replay()
+    e1.record(stream)
+    e1.synchronize()
+    p2p_graph_ms = e0.elapsed_time(e1) / iters
+    del g
+    torch.cuda.synchronize()
+    ex.close()
+    host_ms, graph_ms, p2p_host_ms, p2p_graph_ms = max_over_ranks([host_ms, graph_ms, p2p_host_ms, p2p_graph_ms],
+                                                                  world, dev)
     gbs = decode_bytes(1, H_Q, H_KV, S_kv, D) / (graph_ms * 1e-3) / 1e9
+    gbs_p2p = decode_bytes(1, H_Q, H_KV, S_kv, D) / (p2p_graph_ms * 1e-3) / 1e9
     return {"us": round(graph_ms * 1e3, 2), "host_call_us": round(host_ms * 1e3, 2), "GB/s_total": round(gbs, 1),
             "GB/s_per_gpu": round(gbs / world, 1), "frac_hbm_per_gpu": round(gbs / world / peaks["hbm_gbs"], 3),
-            "collective": "1x all_gather (NCCL), in place; us = CUDA-graph replay"}
+            "collective": "1x all_gather (NCCL), in place; us = CUDA-graph replay",
+            "p2p": {"us": round(p2p_graph_ms * 1e3, 2), "host_call_us": round(p2p_host_ms * 1e3, 2),
+                    "GB/s_total": round(gbs_p2p, 1),
+                    "frac_hbm_per_gpu": round(gbs_p2p / world / peaks["hbm_gbs"], 3),
+                    "exchange": "kf_attn_exchange_combine: partials written into peer windows over NVLink "
+                                "(CUDA IPC), flags, merge; no NCCL"}}
 
 
 def cpu_baseline_sample(budget_s=12.0):

@@ -145,6 +145,44 @@ int kf_attn_combine_packed(const float* parts, long long part_stride, int n_part
                            float* O, float* Mi, float* Li,
                            int B, int H_q, int S_q, int D, void* stream);
 
+/* ---- cross-GPU exchange over NVLink peer memory --------------------------
+ * No reference counterpart (the reference is single-GPU).  For long-context
+ * decode with the KV cache split by ranges over `world` GPUs (one process per
+ * GPU), one kernel replaces the all-gather + kf_attn_combine_packed pair: it
+ * writes this rank's partials into every peer's window over NVLink as 8-byte
+ * {value, sequence number} words, polls the peers' words in its own window
+ * and merges.
+ *
+ * Setup (once, outside the decode loop; these calls allocate):
+ *   kf_peer_window_bytes     size of a window for world ranks, parts of
+ *                            part_stride floats (>= B*H_q*S_q*(D+2), multiple
+ *                            of 4) and n_chunks CTAs (1 <= n_chunks <= SMs):
+ *                            staging part + 2 x world slots of 8-byte words +
+ *                            n_chunks call counters
+ *   kf_peer_window_alloc     cudaMalloc + zero fill + CUDA IPC export; writes
+ *                            KF_PEER_HANDLE_BYTES opaque bytes to handle_out
+ *   kf_peer_window_open      maps another process's window (from its handle)
+ *   kf_peer_window_close / kf_peer_window_free
+ * Per decode step:
+ *   kf_attn_fwd_partial(..., O = window, Mi = window + rows*D,
+ *                       Li = window + rows*D + rows, ...)   staging part at the base
+ *   kf_attn_exchange_combine(windows, world, rank, part_stride, n_chunks, O, ...)
+ * windows[r] is rank r's window as mapped in this process (windows[rank] is
+ * the own one).  Every rank makes the same sequence of calls with the same
+ * shapes; each call's sequence number is kept in device memory, so both calls
+ * can be captured in a CUDA graph and replayed.  Waits are bounded: a peer
+ * that never arrives leaves this rank's O rows unwritten and
+ * kf_device_error() reporting KF_ERR_DEVICE_TIMEOUT. */
+#define KF_PEER_HANDLE_BYTES 64
+#define KF_MAX_PEERS 8
+size_t kf_peer_window_bytes(int world, long long part_stride, int n_chunks);
+int kf_peer_window_alloc(size_t bytes, void** window, void* handle_out);
+int kf_peer_window_open(const void* handle, void** peer_window);
+int kf_peer_window_close(void* peer_window);
+int kf_peer_window_free(void* window);
+int kf_attn_exchange_combine(void* const* windows, int world, int rank, long long part_stride, int n_chunks,
+                             float* O, float* Mi, float* Li, int B, int H_q, int S_q, int D, void* stream);
+
 /* Bytes of workspace the call with these arguments would use (0 if none). */
 size_t kf_attn_workspace_bytes(int B, int H_q, int H_kv, int S_q, int S_kv, int D);
 

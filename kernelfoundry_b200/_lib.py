@@ -35,7 +35,12 @@ EXPORTED = [
     "kf_launch_flash_attn", "kf_attn_fwd_noalloc", "kf_device_error", "kf_set_wait_timeout_ns",
     "kf_selftest_wait_timeout",
     "kf_rmsnorm", "kf_rope", "kf_swiglu",
+    "kf_peer_window_bytes", "kf_peer_window_alloc", "kf_peer_window_open", "kf_peer_window_close",
+    "kf_peer_window_free", "kf_attn_exchange_combine",
 ]
+
+KF_PEER_HANDLE_BYTES = 64
+KF_MAX_PEERS = 8
 
 
 class KFError(RuntimeError):
@@ -100,6 +105,18 @@ def lib():
     L.kf_selftest_wait_timeout.argtypes = [ctypes.c_ulonglong, P]
     L.kf_selftest_wait_timeout.restype = I
     LL, U, F = ctypes.c_longlong, ctypes.c_uint, ctypes.c_float
+    L.kf_peer_window_bytes.argtypes = [I, LL, I]
+    L.kf_peer_window_bytes.restype = Z
+    L.kf_peer_window_alloc.argtypes = [Z, ctypes.POINTER(P), P]
+    L.kf_peer_window_alloc.restype = I
+    L.kf_peer_window_open.argtypes = [P, ctypes.POINTER(P)]
+    L.kf_peer_window_open.restype = I
+    L.kf_peer_window_close.argtypes = [P]
+    L.kf_peer_window_close.restype = I
+    L.kf_peer_window_free.argtypes = [P]
+    L.kf_peer_window_free.restype = I
+    L.kf_attn_exchange_combine.argtypes = [ctypes.POINTER(P), I, I, LL, I, P, P, P, I, I, I, I, P]
+    L.kf_attn_exchange_combine.restype = I
     L.kf_rmsnorm.argtypes = [P, P, P, P, LL, I, F, U, P]
     L.kf_rmsnorm.restype = I
     L.kf_rope.argtypes = [P, P, P, P, I, I, I, I, I, I, F, LL, LL, LL, LL, LL, LL, U, P]

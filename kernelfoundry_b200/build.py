@@ -18,7 +18,7 @@ CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_DIR = os.path.join(PKG_DIR, "lib")
 LIB_PATH = os.environ.get("KF_LIB_PATH") or os.path.join(LIB_DIR, "libkf_attn.so")
 SOURCES = ["kf_api.cu"]
-HEADERS = ["kf_ptx.cuh", "prefill_sm100.cuh", "decode_sm100.cuh", "pointwise_sm100.cuh"]
+HEADERS = ["kf_ptx.cuh", "prefill_sm100.cuh", "decode_sm100.cuh", "pointwise_sm100.cuh", "peer_sm100.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

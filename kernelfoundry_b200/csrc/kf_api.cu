@@ -18,6 +18,7 @@
 #include "../../include/kf_attn.h"
 #include "../../include/kf_pointwise.h"
 #include "decode_sm100.cuh"
+#include "peer_sm100.cuh"
 #include "kf_ptx.cuh"
 #include "pointwise_sm100.cuh"
 #include "prefill_sm100.cuh"
@@ -681,6 +682,98 @@ int kf_attn_combine_packed(const float* parts, long long part_stride, int n_part
     if (!aligned16(parts) || !aligned16(O)) return KF_ERR_MISALIGNED;
     return combine_launch(parts, parts + rows * D, parts + rows * D + rows, n_parts, part_stride, part_stride, O, Mi,
                           Li, rows, D, stream);
+}
+
+size_t kf_peer_window_bytes(int world, long long part_stride, int n_chunks) {
+    if (world < 1 || world > KF_MAX_PEERS || part_stride <= 0 || part_stride % 4 != 0 || n_chunks < 1) return 0;
+    return static_cast<size_t>(kf::peer_window_words(part_stride, world, n_chunks)) * 4;
+}
+
+int kf_peer_window_alloc(size_t bytes, void** window, void* handle_out) {
+    if (bytes == 0 || !window || !handle_out) return KF_ERR_INVALID_ARG;
+    static_assert(sizeof(cudaIpcMemHandle_t) == KF_PEER_HANDLE_BYTES, "IPC handle size");
+    DeviceInfo* di = nullptr;
+    int rc = device_info(&di);
+    if (rc != KF_OK) return rc;
+    void* ptr = nullptr;
+    cudaError_t e = cudaMalloc(&ptr, bytes);
+    if (e != cudaSuccess) return cuda_fail(e);
+    if ((e = cudaMemset(ptr, 0, bytes)) != cudaSuccess) { cudaFree(ptr); return cuda_fail(e); }
+    cudaIpcMemHandle_t h;
+    if ((e = cudaIpcGetMemHandle(&h, ptr)) != cudaSuccess) { cudaFree(ptr); return cuda_fail(e); }
+    std::memcpy(handle_out, &h, sizeof(h));
+    *window = ptr;
+    return KF_OK;
+}
+
+int kf_peer_window_open(const void* handle, void** peer_window) {
+    if (!handle || !peer_window) return KF_ERR_INVALID_ARG;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    void* ptr = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(e);
+    *peer_window = ptr;
+    return KF_OK;
+}
+
+int kf_peer_window_close(void* peer_window) {
+    if (!peer_window) return KF_ERR_INVALID_ARG;
+    cudaError_t e = cudaIpcCloseMemHandle(peer_window);
+    return e == cudaSuccess ? KF_OK : cuda_fail(e);
+}
+
+int kf_peer_window_free(void* window) {
+    if (!window) return KF_ERR_INVALID_ARG;
+    cudaError_t e = cudaFree(window);
+    return e == cudaSuccess ? KF_OK : cuda_fail(e);
+}
+
+int kf_attn_exchange_combine(void* const* windows, int world, int rank, long long part_stride, int n_chunks,
+                             float* O, float* Mi, float* Li, int B, int H_q, int S_q, int D, void* stream) {
+    if (!windows || world < 1 || world > KF_MAX_PEERS || rank < 0 || rank >= world) return KF_ERR_INVALID_ARG;
+    if (B < 0 || H_q <= 0 || S_q < 0 || n_chunks < 1) return KF_ERR_INVALID_ARG;
+    if (!(D == 16 || D == 64 || D == 128 || D == 256)) return KF_ERR_UNSUPPORTED_HEAD_DIM;
+    const long long rows = static_cast<long long>(B) * H_q * S_q;
+    if (part_stride < rows * (D + 2) || part_stride % 4 != 0) return KF_ERR_INVALID_ARG;
+    if (!O) return KF_ERR_INVALID_ARG;
+    for (int r = 0; r < world; ++r) {
+        if (!windows[r]) return KF_ERR_INVALID_ARG;
+        if (!aligned16(windows[r])) return KF_ERR_MISALIGNED;
+    }
+    if (!aligned16(O)) return KF_ERR_MISALIGNED;
+    if (rows == 0) return KF_OK;
+    DeviceInfo* di = nullptr;
+    int rc = device_info(&di);
+    if (rc != KF_OK) return rc;
+    // One CTA per SM at most: every chunk a peer waits for is resident.
+    if (n_chunks > di->sm_count) return KF_ERR_INVALID_ARG;
+    kf::ExchangeParams p;
+    for (int r = 0; r < kf::kMaxPeers; ++r) p.win[r] = r < world ? static_cast<float*>(windows[r]) : nullptr;
+    p.own = static_cast<float*>(windows[rank]);
+    p.world = world;
+    p.rank = rank;
+    p.part_stride = part_stride;
+    p.rows = rows;
+    p.D = D;
+    p.n_chunks = n_chunks;
+    p.O = O;
+    p.Mi = Mi;
+    p.Li = Li;
+    p.timeout_ns = g_timeout_ns.load();
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    switch (world) {
+        case 1: kf::exchange_combine_kernel<1><<<n_chunks, 256, 0, st>>>(p); break;
+        case 2: kf::exchange_combine_kernel<2><<<n_chunks, 256, 0, st>>>(p); break;
+        case 3: kf::exchange_combine_kernel<3><<<n_chunks, 256, 0, st>>>(p); break;
+        case 4: kf::exchange_combine_kernel<4><<<n_chunks, 256, 0, st>>>(p); break;
+        case 5: kf::exchange_combine_kernel<5><<<n_chunks, 256, 0, st>>>(p); break;
+        case 6: kf::exchange_combine_kernel<6><<<n_chunks, 256, 0, st>>>(p); break;
+        case 7: kf::exchange_combine_kernel<7><<<n_chunks, 256, 0, st>>>(p); break;
+        default: kf::exchange_combine_kernel<8><<<n_chunks, 256, 0, st>>>(p); break;
+    }
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? KF_OK : cuda_fail(e);
 }
 
 size_t kf_attn_workspace_bytes(int B, int H_q, int H_kv, int S_q, int S_kv, int D) {

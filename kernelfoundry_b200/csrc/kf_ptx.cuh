@@ -22,6 +22,7 @@ enum : unsigned {
     KF_DEVERR_TIMEOUT_MMA = 1u << 1,   // an MMA completion never arrived
     KF_DEVERR_TIMEOUT_SOFTMAX = 1u << 2,  // softmax handshake never arrived
     KF_DEVERR_TIMEOUT_SELFTEST = 1u << 3, // the self-test wait expired (expected)
+    KF_DEVERR_TIMEOUT_PEER = 1u << 4,     // a peer GPU's exchange flag never arrived
 };
 
 // Per-device error word: kernels OR KF_DEVERR_* bits into it; the host reads
@@ -162,6 +163,18 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 // Orders this thread's generic-proxy global accesses with its async-proxy (TMA) ones.
 __device__ __forceinline__ void fence_proxy_async_global() {
     asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Flag accesses between GPUs (system scope): a release store publishes this
+// thread's earlier writes (and what a CTA barrier ordered before them); an
+// acquire load orders later reads after the store it observes.
+__device__ __forceinline__ void st_release_sys(unsigned* ptr, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* ptr) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+    return v;
 }
 
 // atomicAdd with acquire-release semantics at GPU scope (orders this thread's

@@ -8,9 +8,11 @@ The reference is single-GPU; the path shards naturally:
   No communication: every rank runs :func:`flash_attn_fwd` on its own shard.
 * **KV-sequence sharding** (single-sequence long-context decode): the KV
   cache is cut into ``world`` contiguous ranges, each rank computes the
-  softmax partials (m, l, O_u) of its range, one NCCL all-gather exchanges
-  them ([rows*(D+2)] fp32 per rank; 16.6 KB at H_q=32, D=128), and every rank
-  merges them by log-sum-exp with the library's combine kernel.
+  softmax partials (m, l, O_u) of its range ([rows*(D+2)] fp32; 16.6 KB at
+  H_q=32, D=128) and they are merged by log-sum-exp on every rank.  Two
+  exchanges: one NCCL all-gather followed by the library's combine kernel,
+  or (:class:`PeerExchange`) one kernel that writes the partials into every
+  peer's window over NVLink, waits for the peers' flags and merges.
 
 The compute callables default to the CUDA kernels; tests on CPU ranks (gloo)
 inject stand-ins to check the partitioning and the exchange.
@@ -23,7 +25,7 @@ import torch
 import torch.distributed as dist
 
 __all__ = ["shard_range", "batch_shard", "head_shard", "kv_shard", "long_decode_forward", "pack_partials",
-           "unpack_partials"]
+           "unpack_partials", "PeerExchange"]
 
 
 def shard_range(n: int, world: int, rank: int) -> tuple[int, int]:
@@ -88,11 +90,123 @@ def _cuda_combine(O_p, m_p, l_p):
     return combine_partials(O_p, m_p, l_p)
 
 
+class _DevArray:
+    """A raw device range as a torch tensor (``__cuda_array_interface__``)."""
+
+    def __init__(self, ptr: int, shape, device: torch.device):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": "<f4", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+        self.device = device
+
+
+class PeerExchange:
+    """NVLink peer windows for the long-context decode exchange (one per rank).
+
+    Collective constructor: every rank of ``group`` allocates a window
+    (``kf_peer_window_alloc``), the CUDA IPC handles are all-gathered over
+    ``group`` (any backend; only host objects travel) and every peer window is
+    mapped into this process.  ``staging(shape)`` returns (O_u, m, l) tensors
+    over the own window's staging part, where :func:`flash_attn_partial`
+    writes; ``combine(out)`` launches the exchange-and-merge kernel.  Both are
+    stream-ordered and allocation-free (CUDA-graph capturable).  Every rank
+    must make the same sequence of calls.  ``close()`` (collective) unmaps.
+    """
+
+    def __init__(self, shape, group: Optional[dist.ProcessGroup] = None, n_chunks: Optional[int] = None,
+                 device: Optional[torch.device] = None):
+        import ctypes
+
+        from ._lib import KF_PEER_HANDLE_BYTES, check, lib
+
+        B, H_q, S_q, D = shape
+        self.shape = (B, H_q, S_q, D)
+        self.rows = B * H_q * S_q
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.part_stride = (self.rows * (D + 2) + 3) // 4 * 4
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        self.n_chunks = int(n_chunks or max(1, min(sms, self.rows)))   # up to one row per CTA
+        L = lib()
+        nbytes = L.kf_peer_window_bytes(self.world, self.part_stride, self.n_chunks)
+        if nbytes == 0:
+            raise ValueError("unsupported exchange shape or world size")
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * KF_PEER_HANDLE_BYTES)()
+        with torch.cuda.device(self.device):
+            check(L.kf_peer_window_alloc(nbytes, ctypes.byref(own), handle), "kf_peer_window_alloc")
+        self._own = own.value
+        handles = [bytes(handle)]
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+        ptrs = []
+        self._opened = []
+        with torch.cuda.device(self.device):
+            for r in range(self.world):
+                if r == self.rank:
+                    ptrs.append(self._own)
+                    continue
+                buf = (ctypes.c_ubyte * KF_PEER_HANDLE_BYTES).from_buffer_copy(handles[r])
+                peer = ctypes.c_void_p()
+                check(L.kf_peer_window_open(buf, ctypes.byref(peer)), "kf_peer_window_open")
+                ptrs.append(peer.value)
+                self._opened.append(peer.value)
+        self._windows = (ctypes.c_void_p * self.world)(*ptrs)
+        rows, dev = self.rows, self.device
+        self._stage = (torch.as_tensor(_DevArray(self._own, (B, H_q, S_q, D), dev), device=dev),
+                       torch.as_tensor(_DevArray(self._own + rows * D * 4, (B, H_q, S_q), dev), device=dev),
+                       torch.as_tensor(_DevArray(self._own + rows * (D + 1) * 4, (B, H_q, S_q), dev), device=dev))
+
+    def staging(self):
+        """(O_u [B,H_q,S_q,D], m [B,H_q,S_q], l [B,H_q,S_q]) over the own staging part."""
+        return self._stage
+
+    def combine(self, out: Optional[torch.Tensor] = None, Mi: Optional[torch.Tensor] = None,
+                Li: Optional[torch.Tensor] = None) -> torch.Tensor:
+        import ctypes
+
+        from ._lib import check, lib
+
+        B, H_q, S_q, D = self.shape
+        if out is None:
+            out = torch.empty(self.shape, dtype=torch.float32, device=self.device)
+        if out.shape != self.shape or out.dtype != torch.float32 or not out.is_contiguous():
+            raise ValueError("out must be a contiguous float32 tensor of the exchange shape")
+        p = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None  # noqa: E731
+        stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+        check(lib().kf_attn_exchange_combine(self._windows, self.world, self.rank, self.part_stride, self.n_chunks,
+                                             p(out), p(Mi), p(Li), B, H_q, S_q, D, stream),
+              "kf_attn_exchange_combine")
+        return out
+
+    def close(self) -> None:
+        """Collective: unmap the peers' windows, then free the own one."""
+        from ._lib import check, lib
+
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)       # no peer still writes into the own window
+        with torch.cuda.device(self.device):
+            for ptr in self._opened:
+                check(lib().kf_peer_window_close(ptr), "kf_peer_window_close")
+            if self.world > 1:
+                dist.barrier(group=self.group)   # every mapping of the own window is gone
+            check(lib().kf_peer_window_free(self._own), "kf_peer_window_free")
+        self._own = None
+        self._opened = []
+        self._stage = None
+
+
 def long_decode_forward(q: torch.Tensor, k_shard: torch.Tensor, v_shard: torch.Tensor,
                         group: Optional[dist.ProcessGroup] = None,
                         partial_fn: Optional[Callable] = None, combine_fn: Optional[Callable] = None,
                         gather_buf: Optional[torch.Tensor] = None,
-                        out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                        out: Optional[torch.Tensor] = None,
+                        exchange: Optional[PeerExchange] = None) -> torch.Tensor:
     """Attention of q over a KV cache split across the ranks of `group`.
 
     q [B,H_q,S_q,D] is replicated; k_shard/v_shard [B,H_kv,S_r,D] hold this
@@ -105,8 +219,19 @@ def long_decode_forward(q: torch.Tensor, k_shard: torch.Tensor, v_shard: torch.T
     partial launch, one all-gather, one combine launch and no host-side copies,
     so a decode step can be captured in a CUDA graph.  `partial_fn` /
     `combine_fn` substitute the compute (tests on CPU ranks).
+
+    With ``exchange`` (a :class:`PeerExchange` of q's shape) the partials go to
+    the exchange's staging part and one kernel exchanges them over NVLink and
+    merges: no NCCL call.
     """
     world = dist.get_world_size(group) if dist.is_initialized() else 1
+    if exchange is not None:
+        from .attention import flash_attn_partial
+
+        if tuple(q.shape) != exchange.shape:
+            raise ValueError("exchange was built for another shape")
+        flash_attn_partial(q, k_shard, v_shard, out=exchange.staging())
+        return exchange.combine(out=out)
     if partial_fn is None and combine_fn is None:
         from .attention import combine_packed, flash_attn_partial
 

@@ -133,6 +133,34 @@ def test_argument_validation_without_gpu(kf_lib):
         == L.KF_ERR_UNSUPPORTED_HEAD_DIM
 
 
+def test_peer_exchange_argument_validation_without_gpu(kf_lib):
+    from kernelfoundry_b200 import _lib as L
+
+    # window size: staging part + 2 parities x world slots of 8-byte words + n_chunks counters
+    assert kf_lib.kf_peer_window_bytes(2, 4160, 4) == (4160 * (1 + 4 * 2) + 4) * 4
+    assert kf_lib.kf_peer_window_bytes(0, 4160, 4) == 0
+    assert kf_lib.kf_peer_window_bytes(9, 4160, 4) == 0          # more than KF_MAX_PEERS
+    assert kf_lib.kf_peer_window_bytes(2, 4162, 4) == 0          # part stride not a multiple of 4
+    assert kf_lib.kf_peer_window_bytes(2, 4160, 0) == 0
+    wins = (ctypes.c_void_p * 2)(FAKE, FAKE)
+
+    def ex(world=2, rank=0, ps=32 * 130, nch=4, B=1, Hq=32, Sq=1, D=128, w=wins, o=FAKE):
+        return kf_lib.kf_attn_exchange_combine(w, world, rank, ps, nch, o, None, None, B, Hq, Sq, D, None)
+
+    assert ex(rank=2) == L.KF_ERR_INVALID_ARG
+    assert ex(world=0) == L.KF_ERR_INVALID_ARG
+    assert ex(ps=32 * 130 - 4) == L.KF_ERR_INVALID_ARG           # part smaller than rows*(D+2)
+    assert ex(ps=32 * 130 + 2) == L.KF_ERR_INVALID_ARG
+    assert ex(nch=0) == L.KF_ERR_INVALID_ARG
+    assert ex(D=96) == L.KF_ERR_UNSUPPORTED_HEAD_DIM
+    assert ex(o=ctypes.c_void_p(0)) == L.KF_ERR_INVALID_ARG
+    assert ex(w=(ctypes.c_void_p * 2)(FAKE, ctypes.c_void_p(0))) == L.KF_ERR_INVALID_ARG
+    assert ex(w=(ctypes.c_void_p * 2)(FAKE, MISALIGNED)) == L.KF_ERR_MISALIGNED
+    assert ex(B=0) == L.KF_OK
+    assert kf_lib.kf_peer_window_alloc(0, ctypes.byref(ctypes.c_void_p()), FAKE) == L.KF_ERR_INVALID_ARG
+    assert kf_lib.kf_peer_window_open(None, ctypes.byref(ctypes.c_void_p())) == L.KF_ERR_INVALID_ARG
+
+
 def test_pointwise_argument_validation_without_gpu(kf_lib):
     from kernelfoundry_b200 import _lib as L
 
