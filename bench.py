@@ -542,9 +542,27 @@ def run_long_decode_split(args, rank, world, dev, peaks):
     torch.cuda.synchronize()
     # The same step with the NVLink peer exchange (no NCCL): partial kernel + one
     # exchange-and-merge kernel, host-driven and as a CUDA graph.
+    from kernelfoundry_b200 import device_error
     from kernelfoundry_b200.multi_gpu import PeerExchange
 
-    ex = PeerExchange(tuple(q.shape), device=dev)
+    # Every rank agrees that the windows were set up before any rank times them.
+    ex, why = None, ""
+    try:
+        ex = PeerExchange(tuple(q.shape), device=dev)
+    except Exception as e:  # noqa: BLE001 -- reported in the JSON line, the NCCL numbers stand
+        why = f"{type(e).__name__}: {e}"[:200]
+    agree = torch.tensor([1 if ex is not None else 0], device=dev)
+    dist.all_reduce(agree, op=dist.ReduceOp.MIN)
+    host_ms, graph_ms = max_over_ranks([host_ms, graph_ms], world, dev)
+    gbs = decode_bytes(1, H_Q, H_KV, S_kv, D) / (graph_ms * 1e-3) / 1e9
+    res = {"us": round(graph_ms * 1e3, 2), "host_call_us": round(host_ms * 1e3, 2), "GB/s_total": round(gbs, 1),
+           "GB/s_per_gpu": round(gbs / world, 1), "frac_hbm_per_gpu": round(gbs / world / peaks["hbm_gbs"], 3),
+           "collective": "1x all_gather (NCCL), in place; us = CUDA-graph replay"}
+    if int(agree.item()) == 0:
+        if ex is not None:
+            ex.close()
+        res["p2p"] = {"unavailable": why or "peer window setup failed on another rank"}
+        return res
 
     def step_p2p(_):
         long_decode_forward(q, k, v, exchange=ex, out=out)
@@ -571,19 +589,19 @@ def run_long_decode_split(args, rank, world, dev, peaks):
     p2p_graph_ms = e0.elapsed_time(e1) / iters
     del g
     torch.cuda.synchronize()
+    rc, raw = device_error()                # an expired peer wait would void the timing
     ex.close()
-    host_ms, graph_ms, p2p_host_ms, p2p_graph_ms = max_over_ranks([host_ms, graph_ms, p2p_host_ms, p2p_graph_ms],
-                                                                  world, dev)
-    gbs = decode_bytes(1, H_Q, H_KV, S_kv, D) / (graph_ms * 1e-3) / 1e9
+    p2p_host_ms, p2p_graph_ms, bad = max_over_ranks([p2p_host_ms, p2p_graph_ms, float(rc != 0)], world, dev)
+    if bad:
+        res["p2p"] = {"unavailable": f"a peer wait expired during timing (device error word {raw:#x})"}
+        return res
     gbs_p2p = decode_bytes(1, H_Q, H_KV, S_kv, D) / (p2p_graph_ms * 1e-3) / 1e9
-    return {"us": round(graph_ms * 1e3, 2), "host_call_us": round(host_ms * 1e3, 2), "GB/s_total": round(gbs, 1),
-            "GB/s_per_gpu": round(gbs / world, 1), "frac_hbm_per_gpu": round(gbs / world / peaks["hbm_gbs"], 3),
-            "collective": "1x all_gather (NCCL), in place; us = CUDA-graph replay",
-            "p2p": {"us": round(p2p_graph_ms * 1e3, 2), "host_call_us": round(p2p_host_ms * 1e3, 2),
-                    "GB/s_total": round(gbs_p2p, 1),
-                    "frac_hbm_per_gpu": round(gbs_p2p / world / peaks["hbm_gbs"], 3),
-                    "exchange": "kf_attn_exchange_combine: partials written into peer windows over NVLink "
-                                "(CUDA IPC), flags, merge; no NCCL"}}
+    res["p2p"] = {"us": round(p2p_graph_ms * 1e3, 2), "host_call_us": round(p2p_host_ms * 1e3, 2),
+                  "GB/s_total": round(gbs_p2p, 1), "frac_hbm_per_gpu": round(gbs_p2p / world / peaks["hbm_gbs"], 3),
+                  "exchange": "kf_attn_exchange_combine: {value, sequence} words written into the peers' windows "
+                              "over NVLink (CUDA IPC), polled and merged in one kernel; no NCCL; us = CUDA-graph "
+                              "replay of partial + exchange"}
+    return res
 
 
 def cpu_baseline_sample(budget_s=12.0):
