@@ -81,7 +81,9 @@ struct DecodeParams {
 
 // PAGED: K/V come from block pools through a per-sequence block table (the maps
 // are 3-D over (D, block_size, n_blocks * H_kv)); sequences have their own lengths.
-template <int D, int MT, bool PAGED = false>
+// SPLIT = false: a launch with n_split == 1 (no partials, no merge), compiled
+// without the split-merge code so that code does not shape the streaming loop.
+template <int D, int MT, bool PAGED = false, bool SPLIT = true>
 __global__ void __launch_bounds__(DecodeCfg<D, MT>::THREADS)
 decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                   const DecodeParams p) {
@@ -401,7 +403,7 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
     }
     __syncthreads();
 
-    if (p.n_split == 1) {
+    if (!SPLIT || p.n_split == 1) {
         for (int idx = tid; idx < nrows * (D / 4); idx += C::THREADS) {
             const int row = idx / (D / 4), d = (idx % (D / 4)) * 4;
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);

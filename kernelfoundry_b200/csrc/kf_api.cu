@@ -417,8 +417,11 @@ int launch_decode_t(const Plan& pl, const void* Q, const void* K, const void* V,
                     const Paged* pg, int out_type) {
     using C = kf::DecodeCfg<D, MT>;
     int bps = 0;
-    int rc = pg ? kernel_setup<kf::decode_fwd_kernel<D, MT, true>>(C::SMEM_BYTES, C::THREADS, &bps)
-                : kernel_setup<kf::decode_fwd_kernel<D, MT, false>>(C::SMEM_BYTES, C::THREADS, &bps);
+    const bool split = pl.n_split > 1;
+    int rc = pg ? (split ? kernel_setup<kf::decode_fwd_kernel<D, MT, true, true>>(C::SMEM_BYTES, C::THREADS, &bps)
+                         : kernel_setup<kf::decode_fwd_kernel<D, MT, true, false>>(C::SMEM_BYTES, C::THREADS, &bps))
+                : (split ? kernel_setup<kf::decode_fwd_kernel<D, MT, false, true>>(C::SMEM_BYTES, C::THREADS, &bps)
+                         : kernel_setup<kf::decode_fwd_kernel<D, MT, false, false>>(C::SMEM_BYTES, C::THREADS, &bps));
     if (rc != KF_OK) return rc;
     const int kv_box = S_kv < C::TK ? S_kv : C::TK;
     CUtensorMap mk, mv;
@@ -461,10 +464,14 @@ int launch_decode_t(const Plan& pl, const void* Q, const void* K, const void* V,
     p.timeout_ns = g_timeout_ns.load();
     p.kv_box = pg ? C::TK : kv_box;
     dim3 grid(pl.n_split, H_kv * pl.n_rg, B);
-    if (pg)
-        kf::decode_fwd_kernel<D, MT, true><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
+    if (pg && split)
+        kf::decode_fwd_kernel<D, MT, true, true><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
+    else if (pg)
+        kf::decode_fwd_kernel<D, MT, true, false><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
+    else if (split)
+        kf::decode_fwd_kernel<D, MT, false, true><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
     else
-        kf::decode_fwd_kernel<D, MT, false><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
+        kf::decode_fwd_kernel<D, MT, false, false><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KF_OK : cuda_fail(e);
 }
