@@ -1,9 +1,9 @@
 """Generate the golden vectors that pin the CPU oracle to the reference.
 
-Run in a container that has the reference tree (default /root/reference):
+Run in a container that has the reference tree (its root given by --ref-root):
 
     make -C oracle ref            # builds oracle/_ref/libkfref.so from the reference sources
-    python tests/golden/make_golden.py [--ref-root /root/reference]
+    python tests/golden/make_golden.py [--ref-root REFERENCE_TREE]
 
 Writes (small, committed):
   tests/golden/sdpa_golden.npz      outputs of the reference's own
