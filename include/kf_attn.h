@@ -191,7 +191,9 @@ int kf_attn_workspace_init(void* workspace, size_t workspace_bytes, void* stream
 
 /* Execution plan the call would use, for tests and benchmarks:
  *   *path = 0 prefill (tcgen05 kernel) or 1 decode (split-KV kernel);
- *   *n_split = KV splits per (b, h_kv) (decode), *grid_ctas = CTAs launched. */
+ *   *n_split = KV splits per (b, h_kv) (decode), *grid_ctas = work items: one CTA
+ *   each, except that a prefill whose Q and K/V tiles are all full size launches
+ *   min(items, SM count) persistent CTAs that stride over the items. */
 int kf_attn_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t workspace_bytes,
                  int* path, int* n_split, int* grid_ctas);
 

@@ -94,7 +94,11 @@ def new_workspace(nbytes: int, device=None) -> torch.Tensor:
 
 
 def plan(B, H_q, H_kv, S_q, S_kv, D, workspace_bytes=2**62):
-    """Kernel selection for a call: {'path': 'prefill'|'decode', 'n_split', 'ctas'}."""
+    """Kernel selection for a call: {'path': 'prefill'|'decode', 'n_split', 'ctas'}.
+
+    'ctas' counts work items (kf_attn_plan's grid_ctas): a prefill with full-size
+    tiles runs them on min(items, SM count) persistent CTAs.
+    """
     path, ns, ctas = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
     check(lib().kf_attn_plan(B, H_q, H_kv, S_q, S_kv, D, workspace_bytes,
                              ctypes.byref(path), ctypes.byref(ns), ctypes.byref(ctas)), "kf_attn_plan")
