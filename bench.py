@@ -156,9 +156,30 @@ class ClockSampler:
 
 # ---------------------------------------------------------------- helpers
 def rand_f16(shape, gen, device):
-    import torch
+    """The next prod(shape) N(0,1) fp16 values of the seeded stream ``gen`` (a
+    kernelfoundry_b200.NormalStream), generated on the device by kf_fill_normal_f16.
+    oracle/synth_oracle.normal_f16 rebuilds any slice of them on the host."""
+    return gen.f16(shape, device)
 
-    return torch.randn(shape, generator=gen, device=device, dtype=torch.float32).to(torch.float16)
+
+# Seed of the headline's inputs on rank r: Q sets, then K sets, then V sets, drawn in that order.
+def headline_seed(rank):
+    return 1002 + 7919 * rank
+
+
+def headline_host_qkv(heads):
+    """Rank 0's first headline input set rebuilt on the host (float32 of the fp16 values):
+    query heads [0, heads) and the KV head they share (GQA group 0)."""
+    import numpy as np
+
+    from oracle.synth_oracle import normal_f16
+
+    nq, nkv, hd = H_Q * S * D, H_KV * S * D, S * D
+    seed = headline_seed(0)
+    Q = normal_f16(heads * hd, seed, 0).astype(np.float32).reshape(1, heads, S, D)
+    K = normal_f16(hd, seed, ROTATE * nq).astype(np.float32).reshape(1, 1, S, D)
+    V = normal_f16(hd, seed, ROTATE * nq + ROTATE * nkv).astype(np.float32).reshape(1, 1, S, D)
+    return Q, K, V
 
 
 def time_loop(fn, iters, warmup, stream):
@@ -217,11 +238,10 @@ def run_prefill_headline(args, rank, world, dev):
     import torch
     import torch.distributed as dist
 
-    from kernelfoundry_b200 import flash_attn_fwd, plan
+    from kernelfoundry_b200 import NormalStream, flash_attn_fwd, plan
 
     stream = torch.cuda.current_stream(dev)
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(1002 + 7919 * rank)
+    gen = NormalStream(headline_seed(rank))
     qs = [rand_f16((1, H_Q, S, D), gen, dev) for _ in range(ROTATE)]
     ks = [rand_f16((1, H_KV, S, D), gen, dev) for _ in range(ROTATE)]
     vs = [rand_f16((1, H_KV, S, D), gen, dev) for _ in range(ROTATE)]
@@ -279,12 +299,12 @@ def run_prefill_e2e(args, rank, world, dev):
     import torch
     import torch.distributed as dist
 
-    from kernelfoundry_b200 import flash_attn_fwd
+    from kernelfoundry_b200 import NormalStream, flash_attn_fwd
 
-    g = torch.Generator().manual_seed(2002 + rank)
-    hq = [torch.randn((1, H_Q, S, D), generator=g).to(torch.float16).pin_memory() for _ in range(2)]
-    hk = [torch.randn((1, H_KV, S, D), generator=g).to(torch.float16).pin_memory() for _ in range(2)]
-    hv = [torch.randn((1, H_KV, S, D), generator=g).to(torch.float16).pin_memory() for _ in range(2)]
+    g = NormalStream(2002 + rank)
+    hq = [rand_f16((1, H_Q, S, D), g, dev).cpu().pin_memory() for _ in range(2)]
+    hk = [rand_f16((1, H_KV, S, D), g, dev).cpu().pin_memory() for _ in range(2)]
+    hv = [rand_f16((1, H_KV, S, D), g, dev).cpu().pin_memory() for _ in range(2)]
     ho = [torch.empty((1, H_Q, S, D), dtype=torch.float32).pin_memory() for _ in range(2)]
     dq = [torch.empty_like(x, device=dev) for x in hq]
     dk = [torch.empty_like(x, device=dev) for x in hk]
@@ -339,11 +359,10 @@ def run_extras(args, rank, world, dev, peaks):
     """Decode (C3), long decode (C5), MQA (C4), short prefill (C1) on this rank's GPU."""
     import torch
 
-    from kernelfoundry_b200 import flash_attn_fwd, plan
+    from kernelfoundry_b200 import NormalStream, flash_attn_fwd, plan
 
     stream = torch.cuda.current_stream(dev)
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(4242)
+    gen = NormalStream(4242)
     l2 = torch.cuda.get_device_properties(dev).L2_cache_size
     iters = max(10, min(args.steps, 50))
     out = {}
@@ -495,16 +514,19 @@ def run_long_decode_split(args, rank, world, dev, peaks):
     import torch
     import torch.distributed as dist
 
+    from kernelfoundry_b200 import NormalStream, fill_normal_f16
     from kernelfoundry_b200.multi_gpu import kv_shard, long_decode_forward
 
     S_kv = 131072
     lo, hi = kv_shard(S_kv, world, rank)
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(5005)
-    q = rand_f16((1, H_Q, 1, D), gen, dev)
-    gen.manual_seed(6006 + rank)
-    k = rand_f16((1, H_KV, hi - lo, D), gen, dev)
-    v = rand_f16((1, H_KV, hi - lo, D), gen, dev)
+    q = rand_f16((1, H_Q, 1, D), NormalStream(5005), dev)
+    # This rank's KV range [lo, hi) of the one full-length K and V of seed 6006 (K first,
+    # then V), so every world size sees the same cache as one GPU does.
+    k = torch.empty((1, H_KV, hi - lo, D), dtype=torch.float16, device=dev)
+    v = torch.empty_like(k)
+    for h in range(H_KV):
+        fill_normal_f16(k[0, h], 6006, (h * S_kv + lo) * D)
+        fill_normal_f16(v[0, h], 6006, (H_KV * S_kv + h * S_kv + lo) * D)
     n = (H_Q * (D + 2) + 3) // 4 * 4
     buf = torch.empty(world * n, dtype=torch.float32, device=dev)
     out = torch.empty((1, H_Q, 1, D), dtype=torch.float32, device=dev)
@@ -605,10 +627,13 @@ def run_long_decode_split(args, rank, world, dev, peaks):
 
 
 def cpu_baseline_sample(budget_s=12.0):
-    """The reference's NumPy path (reference_attn restated), fp32, on a bounded sample of heads."""
+    """The reference's NumPy path (reference_attn restated), fp32, on a bounded sample of the
+    query heads of rank 0's first headline input set (rebuilt on the host from its seed: the
+    same fp16 values the GPU arm reads).  Only the attention calls are timed."""
     import numpy as np
 
     from oracle.attn_oracle import reference_attn
+    from oracle.synth_oracle import normal_f16
 
     try:
         from threadpoolctl import threadpool_info
@@ -616,20 +641,27 @@ def cpu_baseline_sample(budget_s=12.0):
         threads = max((i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"), default=1)
     except Exception:
         threads = os.cpu_count() or 1
-    rng = np.random.default_rng(7)
-    K = rng.standard_normal((1, 1, S, D), dtype=np.float32).astype(np.float16).astype(np.float32)
-    V = rng.standard_normal((1, 1, S, D), dtype=np.float32).astype(np.float16).astype(np.float32)
-    done = 0
-    t0 = time.perf_counter()
-    while done < H_Q and time.perf_counter() - t0 < budget_s:
-        Qh = rng.standard_normal((1, 1, S, D), dtype=np.float32).astype(np.float16).astype(np.float32)
-        reference_attn(Qh, K, V)
+    seed, nq, nkv, hd = headline_seed(0), H_Q * S * D, H_KV * S * D, S * D
+
+    def head(off):
+        return normal_f16(hd, seed, off).astype(np.float32).reshape(1, 1, S, D)
+
+    kv = {}
+    done, dt = 0, 0.0
+    while done < H_Q and dt < budget_s:
+        g = done // (H_Q // H_KV)                     # GQA: query head -> its KV head
+        if g not in kv:
+            kv = {g: (head(ROTATE * nq + g * hd), head(ROTATE * nq + ROTATE * nkv + g * hd))}
+        Qh = head(done * hd)
+        t0 = time.perf_counter()
+        reference_attn(Qh, *kv[g])
+        dt += time.perf_counter() - t0
         done += 1
-    dt = time.perf_counter() - t0
     tf = prefill_flops(1, done, S, S, D) / dt / 1e12
     return {"value": round(tf, 5), "unit": "TFLOP/s", "cores": int(threads), "kind": "port",
-            "sample": f"{done} of {H_Q} query heads of one S=4096 D=128 sequence, fp32 NumPy "
-                      f"reference_attn (oracle restatement), {dt:.1f} s"}
+            "sample": f"{done} of {H_Q} query heads of the first headline input set (S=4096, D=128, the GPU "
+                      f"arm's own fp16 values rebuilt from its seed), fp32 NumPy reference_attn (oracle "
+                      f"restatement), {dt:.1f} s of attention"}
 
 
 def run_ours(args):
@@ -673,7 +705,7 @@ def run_ours(args):
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded N(0,1) fp16)",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded N(0,1) fp16 from the counter-based generator of include/kf_synth.h, made on the device)",
         "config": workload_config(world),
         "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
@@ -713,10 +745,7 @@ def run_reference(args):
     except Exception:
         threads = os.cpu_count() or 1
     heads = 2     # bounded sample per step: 2 of the 32 query heads (1/16 of the per-GPU work)
-    rng = np.random.default_rng(11)
-    Q = rng.standard_normal((1, heads, S, D), dtype=np.float32).astype(np.float16).astype(np.float32)
-    K = rng.standard_normal((1, 1, S, D), dtype=np.float32).astype(np.float16).astype(np.float32)
-    V = rng.standard_normal((1, 1, S, D), dtype=np.float32).astype(np.float16).astype(np.float32)
+    Q, K, V = headline_host_qkv(heads)     # the GPU arm's first input set, rebuilt from its seed
     for _ in range(args.warmup):
         reference_attn(Q, K, V)
     t0 = time.perf_counter()
@@ -724,12 +753,13 @@ def run_reference(args):
         reference_attn(Q, K, V)
     dt = (time.perf_counter() - t0) / args.steps
     value = prefill_flops(1, heads, S, S, D) / dt / 1e12
-    sample = (f"{heads} of {H_Q} query heads (GQA group of one KV head) of one S=4096 D=128 sequence per step, "
+    sample = (f"{heads} of {H_Q} query heads (GQA group of one KV head) of the first headline input set "
+              f"(S=4096, D=128, the GPU arm's own fp16 values rebuilt from its seed) per step, "
               f"fp32 NumPy reference_attn (restated from kernel_models/flash_attn.py:250-265)")
     line = {
         "metric": METRIC, "value": round(value, 5), "unit": "TFLOP/s", "impl": "reference", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) fp16-rounded)",
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (the GPU arm's seeded N(0,1) fp16 inputs, rebuilt on the host by oracle/synth_oracle.py)",
         "config": workload_config(world),
         "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": int(threads), "kind": "port",
                          "sample": sample},
@@ -761,12 +791,11 @@ def run_case(args):
     prints one JSON line with the mean device time of the timed launches."""
     import torch
 
-    from kernelfoundry_b200 import flash_attn_fwd, plan
+    from kernelfoundry_b200 import NormalStream, flash_attn_fwd, plan
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(77)
+    gen = NormalStream(77)
     if args.case in POINTWISE:
         desc, nbytes = POINTWISE[args.case]
         ms = time_loop(pointwise_setup(args.case, gen, dev), args.steps, args.warmup, torch.cuda.current_stream(dev))

@@ -10,6 +10,8 @@ include/kf_attn.h); this package is the Python host side.
              cross-GPU split-KV decode (partials + NCCL all-gather + merge)
   pointwise  RMSNorm (plain / fused residual), RoPE, SwiGLU
              (C ABI: include/kf_pointwise.h)
+  synth      seeded counter-based N(0,1) fp16 inputs generated on the GPU
+             (C ABI: include/kf_synth.h)
   build      nvcc build of the library (sm_100a only)
 """
 from ._lib import KFError, lib  # noqa: F401
@@ -26,5 +28,6 @@ from .attention import (  # noqa: F401
 )
 
 from .pointwise import fused_add_rms_norm, rms_norm, rope_, swiglu  # noqa: F401
+from .synth import NormalStream, fill_normal_f16  # noqa: F401
 
 __version__ = "0.1.0"

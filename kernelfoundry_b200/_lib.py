@@ -1,5 +1,5 @@
-"""ctypes binding of libkf_attn.so (the C ABI declared in include/kf_attn.h and
-include/kf_pointwise.h).
+"""ctypes binding of libkf_attn.so (the C ABI declared in include/kf_attn.h,
+include/kf_pointwise.h and include/kf_synth.h).
 
 There is no fallback: if the library is missing this module raises, and every
 compute entry point goes through the CUDA kernels in the library.
@@ -27,7 +27,7 @@ KF_FLAG_OUT_BF16 = 4
 KF_PW_BF16 = 1
 KF_ROPE_GPTJ = 2
 
-# Every symbol include/kf_attn.h and include/kf_pointwise.h declare.
+# Every symbol include/kf_attn.h, include/kf_pointwise.h and include/kf_synth.h declare.
 EXPORTED = [
     "kf_strerror", "kf_last_cuda_error", "kf_version",
     "kf_attn_fwd", "kf_attn_fwd_lse", "kf_attn_fwd_ex", "kf_attn_fwd_paged", "kf_attn_paged_workspace_bytes", "kf_attn_fwd_partial", "kf_attn_combine", "kf_attn_combine_packed",
@@ -37,6 +37,7 @@ EXPORTED = [
     "kf_rmsnorm", "kf_rope", "kf_swiglu",
     "kf_peer_window_bytes", "kf_peer_window_alloc", "kf_peer_window_open", "kf_peer_window_close",
     "kf_peer_window_free", "kf_attn_exchange_combine",
+    "kf_fill_normal_f16",
 ]
 
 KF_PEER_HANDLE_BYTES = 64
@@ -123,6 +124,8 @@ def lib():
     L.kf_rope.restype = I
     L.kf_swiglu.argtypes = [P, P, LL, I, U, P]
     L.kf_swiglu.restype = I
+    L.kf_fill_normal_f16.argtypes = [P, LL, ctypes.c_ulonglong, LL, P]
+    L.kf_fill_normal_f16.restype = I
     del FP
     _lib = L
     return _lib

@@ -18,7 +18,8 @@ CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_DIR = os.path.join(PKG_DIR, "lib")
 LIB_PATH = os.environ.get("KF_LIB_PATH") or os.path.join(LIB_DIR, "libkf_attn.so")
 SOURCES = ["kf_api.cu"]
-HEADERS = ["kf_ptx.cuh", "prefill_sm100.cuh", "decode_sm100.cuh", "pointwise_sm100.cuh", "peer_sm100.cuh"]
+HEADERS = ["kf_ptx.cuh", "prefill_sm100.cuh", "decode_sm100.cuh", "pointwise_sm100.cuh", "peer_sm100.cuh",
+           "synth_sm100.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -38,7 +39,7 @@ def needs_rebuild() -> bool:
         return True
     t = os.path.getmtime(LIB_PATH)
     deps = [os.path.join(CSRC, f) for f in SOURCES + HEADERS]
-    deps += [os.path.join(REPO_DIR, "include", h) for h in ("kf_attn.h", "kf_pointwise.h")]
+    deps += [os.path.join(REPO_DIR, "include", h) for h in ("kf_attn.h", "kf_pointwise.h", "kf_synth.h")]
     return any(os.path.getmtime(d) > t for d in deps if os.path.exists(d))
 
 

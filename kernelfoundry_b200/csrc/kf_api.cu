@@ -17,11 +17,13 @@
 
 #include "../../include/kf_attn.h"
 #include "../../include/kf_pointwise.h"
+#include "../../include/kf_synth.h"
 #include "decode_sm100.cuh"
 #include "peer_sm100.cuh"
 #include "kf_ptx.cuh"
 #include "pointwise_sm100.cuh"
 #include "prefill_sm100.cuh"
+#include "synth_sm100.cuh"
 
 namespace kf {
 
@@ -1051,6 +1053,23 @@ int kf_swiglu(const void* gate_up, void* out, long long rows, int inter, unsigne
     p.ivec = inter / 8;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     return (flags & KF_PW_BF16) ? swiglu_t<true>(p, s) : swiglu_t<false>(p, s);
+}
+
+int kf_fill_normal_f16(uint16_t* dst, long long n, unsigned long long seed, long long offset, void* stream) {
+    if (n < 0 || offset < 0 || (n > 0 && !dst)) return KF_ERR_INVALID_ARG;
+    if (n > (1ll << 62) - offset) return KF_ERR_INVALID_ARG;     // element indices stay below 2^62
+    if (n == 0) return KF_OK;
+    if (reinterpret_cast<uintptr_t>(dst) & 1u) return KF_ERR_MISALIGNED;
+    DeviceInfo* di = nullptr;
+    int rc = device_info(&di);
+    if (rc != KF_OK) return rc;
+    const long long pairs = ((offset + n + 1) >> 1) - (offset >> 1);
+    const long long want = (pairs + 255) / 256, cap = 8ll * di->sm_count;
+    const unsigned grid = static_cast<unsigned>(want < cap ? want : cap);
+    kf::fill_normal_f16_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        reinterpret_cast<__half*>(dst), n, static_cast<uint64_t>(seed), offset);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? KF_OK : cuda_fail(e);
 }
 
 int kf_selftest_wait_timeout(unsigned long long timeout_ns, void* stream) {

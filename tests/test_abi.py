@@ -1,6 +1,6 @@
-"""The C-ABI library loads, exports what include/kf_attn.h and
-include/kf_pointwise.h declare, and validates arguments before touching a GPU
-(no compute calls here)."""
+"""The C-ABI library loads, exports what include/kf_attn.h,
+include/kf_pointwise.h and include/kf_synth.h declare, and validates arguments
+before touching a GPU (no compute calls here)."""
 from __future__ import annotations
 
 import ctypes
@@ -12,7 +12,7 @@ import pytest
 
 from conftest import REPO
 
-HEADERS = [os.path.join(REPO, "include", h) for h in ("kf_attn.h", "kf_pointwise.h")]
+HEADERS = [os.path.join(REPO, "include", h) for h in ("kf_attn.h", "kf_pointwise.h", "kf_synth.h")]
 
 
 def _declared():
@@ -29,7 +29,7 @@ def test_header_symbols_exported(kf_lib):
 
     declared = _declared()
     assert len(declared) >= 17
-    assert {"kf_rmsnorm", "kf_rope", "kf_swiglu"} <= set(declared)
+    assert {"kf_rmsnorm", "kf_rope", "kf_swiglu", "kf_fill_normal_f16"} <= set(declared)
     assert sorted(declared) == sorted(_lib.EXPORTED)
     out = subprocess.run(["nm", "-D", "--defined-only", LIB_PATH], capture_output=True, text=True, check=True).stdout
     exported = set(re.findall(r"\bT (kf_\w+)", out))
@@ -211,6 +211,19 @@ def test_pointwise_argument_validation_without_gpu(kf_lib):
     assert swiglu(rows=0) == L.KF_OK
 
 
+def test_fill_normal_argument_validation_without_gpu(kf_lib):
+    from kernelfoundry_b200 import _lib as L
+
+    fill = kf_lib.kf_fill_normal_f16
+    assert fill(None, 0, 1, 0, None) == L.KF_OK               # empty fill: no CUDA call
+    assert fill(FAKE, 0, 1, 7, None) == L.KF_OK
+    assert fill(FAKE, -1, 1, 0, None) == L.KF_ERR_INVALID_ARG
+    assert fill(FAKE, 8, 1, -2, None) == L.KF_ERR_INVALID_ARG
+    assert fill(None, 8, 1, 0, None) == L.KF_ERR_INVALID_ARG
+    assert fill(FAKE, 1 << 62, 1, 1, None) == L.KF_ERR_INVALID_ARG
+    assert fill(ctypes.c_void_p(FAKE.value + 1), 8, 1, 0, None) == L.KF_ERR_MISALIGNED
+
+
 @pytest.mark.skipif(os.path.exists("/dev/nvidia0"), reason="checks the no-driver path")
 def test_pointwise_compute_call_without_driver_reports_cuda_error(kf_lib):
     from kernelfoundry_b200 import _lib as L
@@ -218,6 +231,7 @@ def test_pointwise_compute_call_without_driver_reports_cuda_error(kf_lib):
     assert kf_lib.kf_rmsnorm(FAKE, FAKE, FAKE, None, 4, 256, 1e-6, 0, None) in (L.KF_ERR_CUDA,
                                                                               L.KF_ERR_UNSUPPORTED_DEVICE)
     assert kf_lib.kf_swiglu(FAKE, FAKE, 4, 256, 0, None) in (L.KF_ERR_CUDA, L.KF_ERR_UNSUPPORTED_DEVICE)
+    assert kf_lib.kf_fill_normal_f16(FAKE, 8, 1, 0, None) in (L.KF_ERR_CUDA, L.KF_ERR_UNSUPPORTED_DEVICE)
 
 
 def test_pointwise_python_api_refuses_cpu_tensors(kf_lib):
