@@ -162,6 +162,16 @@ def rand_f16(shape, gen, device):
     return gen.f16(shape, device)
 
 
+# Long-context decode: one full-length K then V [1, H_KV, S_kv, D] of this seed; each rank
+# generates only its KV range.
+LONG_KV_SEED = 6006
+
+
+def long_kv_offsets(h, lo, s_kv):
+    """Stream offsets of row `lo` of KV head `h` in the full-length K and in V."""
+    return (h * s_kv + lo) * D, (H_KV * s_kv + h * s_kv + lo) * D
+
+
 # Seed of the headline's inputs on rank r: Q sets, then K sets, then V sets, drawn in that order.
 def headline_seed(rank):
     return 1002 + 7919 * rank
@@ -520,13 +530,14 @@ def run_long_decode_split(args, rank, world, dev, peaks):
     S_kv = 131072
     lo, hi = kv_shard(S_kv, world, rank)
     q = rand_f16((1, H_Q, 1, D), NormalStream(5005), dev)
-    # This rank's KV range [lo, hi) of the one full-length K and V of seed 6006 (K first,
+    # This rank's KV range [lo, hi) of the one full-length K and V of LONG_KV_SEED (K first,
     # then V), so every world size sees the same cache as one GPU does.
     k = torch.empty((1, H_KV, hi - lo, D), dtype=torch.float16, device=dev)
     v = torch.empty_like(k)
     for h in range(H_KV):
-        fill_normal_f16(k[0, h], 6006, (h * S_kv + lo) * D)
-        fill_normal_f16(v[0, h], 6006, (H_KV * S_kv + h * S_kv + lo) * D)
+        k_off, v_off = long_kv_offsets(h, lo, S_kv)
+        fill_normal_f16(k[0, h], LONG_KV_SEED, k_off)
+        fill_normal_f16(v[0, h], LONG_KV_SEED, v_off)
     n = (H_Q * (D + 2) + 3) // 4 * 4
     buf = torch.empty(world * n, dtype=torch.float32, device=dev)
     out = torch.empty((1, H_Q, 1, D), dtype=torch.float32, device=dev)

@@ -61,3 +61,28 @@ def test_moments_and_seeds():
     assert np.abs(x).max() < 8.6                     # sqrt(-2 ln 2^-53)
     y = normal_f16(1 << 12, 2025).astype(np.float64)
     assert abs(np.corrcoef(x[:1 << 12], y)[0, 1]) < 0.06
+
+
+def test_long_decode_rank_slices_rebuild_one_cache():
+    """bench.py's per-rank KV ranges of the long-context decode are slices of one cache."""
+    import bench
+    from kernelfoundry_b200.multi_gpu import kv_shard
+
+    s_kv, H, D = 96, bench.H_KV, bench.D
+    n = H * s_kv * D
+    full_k = normal_f16(n, bench.LONG_KV_SEED, 0).reshape(H, s_kv, D)
+    full_v = normal_f16(n, bench.LONG_KV_SEED, n).reshape(H, s_kv, D)
+    for world in (1, 2, 4, 8):
+        ks, vs = [], []
+        for rank in range(world):
+            lo, hi = kv_shard(s_kv, world, rank)
+            k = np.empty((H, hi - lo, D), np.float16)
+            v = np.empty_like(k)
+            for h in range(H):
+                k_off, v_off = bench.long_kv_offsets(h, lo, s_kv)
+                k[h] = normal_f16((hi - lo) * D, bench.LONG_KV_SEED, k_off).reshape(hi - lo, D)
+                v[h] = normal_f16((hi - lo) * D, bench.LONG_KV_SEED, v_off).reshape(hi - lo, D)
+            ks.append(k)
+            vs.append(v)
+        assert np.array_equal(np.concatenate(ks, 1).view(np.uint16), full_k.view(np.uint16)), world
+        assert np.array_equal(np.concatenate(vs, 1).view(np.uint16), full_v.view(np.uint16)), world
