@@ -215,9 +215,12 @@ int kf_launch_flash_attn(const uint16_t* Q, const uint16_t* K, const uint16_t* V
  *     split-KV decode kernel (H_q/H_kv * S_q <= 64 for D <= 128, <= 32 for
  *     D = 256); other shapes return KF_ERR_INVALID_ARG.
  *   - The split partials and ticket counters live in a fixed 2 MiB array inside
- *     the library, held by every GPU that loads it until the process exits.  A
- *     call whose plan needs more than 2 MiB returns KF_ERR_WORKSPACE (use
- *     kf_attn_fwd with a workspace); nothing is allocated either way.
+ *     the library, held by every GPU that loads it until the process exits.  The
+ *     KV split count is planned to fit it: where kf_attn_fwd with a larger
+ *     workspace would split further (many rows at long KV), this call splits
+ *     less (same results, possibly slower); nothing is allocated either way.
+ *   - The ticket counters start at zero and every launch leaves them at zero
+ *     (also after an expired wait), so no call clears the array.
  *   - The first call on a device looks up that array's device address (once per
  *     device, with the device current); make that first call before any stream
  *     capture.

@@ -356,7 +356,19 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         }
     }
     __syncthreads();   // every stage consumed: the ring memory becomes reduction scratch
-    if (*abort_flag) return;
+    const bool aborted = *abort_flag != 0;
+    if (aborted && (!SPLIT || p.n_split == 1)) return;
+    if (aborted) {
+        // A wait expired (the device error word says so).  The split still takes its
+        // ticket, and the last one resets the unit's counter without merging, so the
+        // counters are zero again after the call and the next call's merge is right.
+        const size_t cidx = (static_cast<size_t>(b) * p.H_kv + hk) * p.n_rg + rg;
+        if (tid == 0) {
+            const unsigned ticket = atom_add_acq_rel_gpu(&p.counters[cidx], 1u);
+            if (ticket == static_cast<unsigned>(p.n_split - 1)) p.counters[cidx] = 0u;
+        }
+        return;
+    }
 
     float* red_m = reinterpret_cast<float*>(sBig);            // [NW][QROWS]
     float* red_l = red_m + NW * QROWS;                         // [NW][QROWS]

@@ -707,7 +707,14 @@ int kf_peer_window_alloc(size_t bytes, void** window, void* handle_out) {
     void* ptr = nullptr;
     cudaError_t e = cudaMalloc(&ptr, bytes);
     if (e != cudaSuccess) return cuda_fail(e);
-    if ((e = cudaMemset(ptr, 0, bytes)) != cudaSuccess) { cudaFree(ptr); return cuda_fail(e); }
+    // The window must be zero before its handle leaves this process: a peer that
+    // opens it may write its first {value, sequence} words at once, and a zero fill
+    // still queued behind them would erase them.  cudaMemset does not block the
+    // host for device memory, so wait for the fill explicitly.
+    if ((e = cudaMemsetAsync(ptr, 0, bytes, 0)) != cudaSuccess || (e = cudaStreamSynchronize(0)) != cudaSuccess) {
+        cudaFree(ptr);
+        return cuda_fail(e);
+    }
     cudaIpcMemHandle_t h;
     if ((e = cudaIpcGetMemHandle(&h, ptr)) != cudaSuccess) { cudaFree(ptr); return cuda_fail(e); }
     std::memcpy(handle_out, &h, sizeof(h));
@@ -848,18 +855,18 @@ int kf_attn_fwd_noalloc(const void* Q, const void* K, const void* V, float* O, i
     if (rc != KF_OK) return rc;
     if (B == 0 || S_q == 0) return KF_OK;
     if (!use_decode(H_q / H_kv, S_q, D)) return KF_ERR_INVALID_ARG;   // short-query (decode) shapes only
-    // Same plan kf_attn_fwd makes when its workspace is large enough.
+    // The plan kf_attn_fwd makes with a workspace of the fixed scratch's size: the
+    // planner keeps the split count whose partials fit (n_split = 1 needs none).
     Plan pl;
-    if ((rc = plan_for_call(B, H_q, H_kv, S_q, S_kv, D, static_cast<size_t>(-1), &pl)) != KF_OK) return rc;
-    if (pl.ws_bytes > kNoAllocScratchBytes) return KF_ERR_WORKSPACE;
+    if ((rc = plan_for_call(B, H_q, H_kv, S_q, S_kv, D, kNoAllocScratchBytes, &pl)) != KF_OK) return rc;
+    if (pl.ws_bytes > kNoAllocScratchBytes) return KF_ERR_WORKSPACE;   // not reached: the plan fits
     void* scratch = nullptr;
     if (pl.n_split > 1) {
+        // The ticket counters at the head of the array start at zero (a __device__
+        // array is zero-initialised when the module loads) and every launch leaves
+        // them at zero: the merging CTA of each unit resets its counter, also after
+        // an expired wait.  The partials are overwritten before they are read.
         if ((rc = noalloc_scratch(&scratch)) != KF_OK) return rc;
-        // The array keeps the last call's contents: the ticket counters this call
-        // uses must start at zero, so clear them (the partials are overwritten).
-        const size_t units = static_cast<size_t>(B) * H_kv * pl.n_rg;
-        cudaError_t e = cudaMemsetAsync(scratch, 0, units * sizeof(unsigned), static_cast<cudaStream_t>(stream));
-        if (e != cudaSuccess) return cuda_fail(e);
     }
     return launch_decode(pl, D, Q, K, V, O, nullptr, nullptr, 0, B, H_q, H_kv, S_q, S_kv, scratch,
                          static_cast<cudaStream_t>(stream));

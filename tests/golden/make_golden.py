@@ -112,7 +112,9 @@ def make_legacy(out_path):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref-root", default="/root/reference")
+    ap.add_argument("--ref-root", default=os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(HERE))),
+                                                         "reference"),
+                    help="reference checkout (default: the directory `reference` beside this repository)")
     args = ap.parse_args()
     ref_model = load_reference_model(args.ref_root)
     make_sdpa(ref_model, os.path.join(HERE, "sdpa_golden.npz"))

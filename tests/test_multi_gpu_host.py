@@ -3,8 +3,9 @@
 The per-rank attention math is replaced by the oracle (test-only stand-ins
 injected through long_decode_forward's partial_fn/combine_fn) so that the
 sharding, the packed all-gather and the merge order are checked without a
-GPU.  The CUDA version of the same path runs in bench.py and
-tests/test_multi_gpu_gpu.py.
+GPU.  The CUDA version of the same path runs on two GPUs in
+tests/test_multi_gpu_nccl.py (NCCL all-gather) and tests/test_multi_gpu_p2p.py
+(NVLink peer exchange), and in bench.py for N > 1.
 """
 from __future__ import annotations
 

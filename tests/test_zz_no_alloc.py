@@ -5,8 +5,9 @@ loop that handed all free memory to its KV-cache pool at start-up, or a
 latency-bound decode loop that must not call cudaMalloc because it can
 synchronize the device.  kf_attn_fwd_noalloc takes its split-KV scratch from a
 fixed array inside the library instead of a workspace.  These checks call it
-through the C ABI and compare it with kf_attn_fwd (given a workspace) on the
-same inputs, twice in a row, since every call reuses the same array.
+through the C ABI, twice in a row (every call reuses the same array), and
+compare each result with the fp64 oracle (reference_attn on the fp16 inputs)
+at the north-star tolerance and with kf_attn_fwd given a workspace.
 
 This file sorts last so that a run stopping at the first failure has already
 run every other test; it also passes when run alone in a fresh process.
@@ -20,7 +21,7 @@ import pytest
 
 from oracle.attn_oracle import error_stats, normal_qkv
 
-from gpu_util import MAX_ABS_TOL, REL_L2_TOL, to_dev
+from gpu_util import MAX_ABS_TOL, REL_L2_TOL, assert_close, oracle64, to_dev
 
 pytestmark = pytest.mark.gpu
 
@@ -36,8 +37,6 @@ def _call_noalloc(lib, q, k, v, out, stream):
 
 
 def _call_with_workspace(lib, q, k, v, out, ws, stream):
-    import torch
-
     B, H_q, S_q, D = q.shape
     H_kv, S_kv = k.shape[1], k.shape[2]
     return lib.kf_attn_fwd(P(q.data_ptr()), P(k.data_ptr()), P(v.data_ptr()), P(out.data_ptr()),
@@ -50,11 +49,19 @@ SHAPES = [
     (2, 32, 1, 1, 1000, 64),      # MQA, D=64
     (3, 8, 8, 1, 777, 256),       # D=256
     (2, 32, 8, 2, 2048, 128),     # two query positions
+    (8, 32, 1, 1, 32768, 128),    # full plan needs more than the scratch: fewer splits
 ]
 
 
+def _split_count(lib, shape, ws_bytes):
+    path, ns, ctas = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
+    assert lib.kf_attn_plan(*shape, ws_bytes, ctypes.byref(path), ctypes.byref(ns), ctypes.byref(ctas)) == 0
+    assert path.value == 1
+    return ns.value
+
+
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "B{}_Hq{}_Hkv{}_Sq{}_Skv{}_D{}".format(*s))
-def test_noalloc_matches_workspace_entry_point(cuda, shape):
+def test_noalloc_matches_oracle_and_workspace_entry_point(cuda, shape):
     import torch
 
     from kernelfoundry_b200._lib import KF_OK, lib
@@ -62,49 +69,38 @@ def test_noalloc_matches_workspace_entry_point(cuda, shape):
     L = lib()
     B, H_q, H_kv, S_q, S_kv, D = shape
     need = L.kf_attn_workspace_bytes(*shape)
-    assert need <= SCRATCH_BYTES
     Q, K, V = normal_qkv(*shape, seed=11 * sum(shape))
+    O64 = oracle64(Q, K, V)[0]
     q, k, v = (to_dev(x, cuda) for x in (Q, K, V))
     stream = torch.cuda.current_stream(cuda).cuda_stream
-    ws = torch.zeros(max(need, 16), dtype=torch.uint8, device=cuda)
+    # kf_attn_fwd with the workspace the same plan gets inside the fixed scratch.
+    ws_bytes = min(need, SCRATCH_BYTES)
+    ws = torch.zeros(max(ws_bytes, 16), dtype=torch.uint8, device=cuda)
     ref = torch.empty((B, H_q, S_q, D), dtype=torch.float32, device=cuda)
     assert _call_with_workspace(L, q, k, v, ref, ws, stream) == KF_OK
     torch.cuda.synchronize()
     ref_np = ref.cpu().numpy()
+    assert_close(ref_np, O64, f"kf_attn_fwd {shape}")
+    if need > SCRATCH_BYTES:
+        assert _split_count(L, shape, SCRATCH_BYTES) < _split_count(L, shape, need)
     for call in range(2):
         out = torch.full((B, H_q, S_q, D), float("nan"), dtype=torch.float32, device=cuda)
         assert _call_noalloc(L, q, k, v, out, stream) == KF_OK
         torch.cuda.synchronize()
         got = out.cpu().numpy()
-        assert np.isfinite(got).all(), f"call {call}"
+        assert_close(got, O64, f"noalloc call {call} {shape}")
         max_abs, rel_l2 = error_stats(got, ref_np)
         assert max_abs <= MAX_ABS_TOL and rel_l2 <= REL_L2_TOL, (call, max_abs, rel_l2)
 
 
-def test_noalloc_rejects_over_limit_and_prefill_shapes(cuda):
+def test_noalloc_rejects_prefill_shapes(cuda):
     import torch
 
-    from kernelfoundry_b200._lib import KF_ERR_INVALID_ARG, KF_ERR_WORKSPACE, KF_OK, lib
+    from kernelfoundry_b200._lib import KF_ERR_INVALID_ARG, KF_OK, lib
 
     L = lib()
     stream = torch.cuda.current_stream(cuda).cuda_stream
-    # A decode shape whose split plan needs more than the fixed scratch.
-    over = None
-    for B in (8, 16, 32):
-        for S_kv in (32768, 65536):
-            shape = (B, 32, 1, 1, S_kv, 128)
-            if L.kf_attn_workspace_bytes(*shape) > SCRATCH_BYTES:
-                over = shape
-                break
-        if over:
-            break
-    assert over is not None, "no candidate shape exceeds the scratch limit"
-    B, H_q, H_kv, S_q, S_kv, D = over
-    q = torch.zeros((B, H_q, S_q, D), dtype=torch.float16, device=cuda)
-    kv = torch.zeros((B, H_kv, S_kv, D), dtype=torch.float16, device=cuda)
-    out = torch.zeros((B, H_q, S_q, D), dtype=torch.float32, device=cuda)
-    assert _call_noalloc(L, q, kv, kv, out, stream) == KF_ERR_WORKSPACE
-    # Prefill shapes use no scratch and belong to kf_attn_fwd.
+    # Prefill shapes use no split scratch and belong to kf_attn_fwd.
     q = torch.zeros((1, 8, 512, 128), dtype=torch.float16, device=cuda)
     kv = torch.zeros((1, 2, 512, 128), dtype=torch.float16, device=cuda)
     out = torch.zeros((1, 8, 512, 128), dtype=torch.float32, device=cuda)
