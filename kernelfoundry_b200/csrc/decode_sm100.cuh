@@ -30,17 +30,26 @@
 
 namespace kf {
 
-template <int D, int MT>
+// DEEP: for launches whose CTAs all fit on the SMs at once (one CTA per SM): a ring
+// of twice the bytes (about 192 KB) and two groups of four consumer warps that take
+// alternate stages.  A CTA's stream is bound by its consumers' warp-MMA work per stage
+// (about 0.5 us per 32 KB stage with one group), so two groups double its rate.
+template <int D, int MT, bool DEEP = false>
 struct DecodeCfg {
     static constexpr int TK = 64;                        // KV rows per stage
-    static constexpr int NW = 4;                         // consumer warps, 16 rows each
+    static constexpr int NW = 4;                         // consumer warps per group, 16 rows each
     static constexpr int SWB = (D >= 64) ? 128 : 2 * D;
     static constexpr int SWE = SWB / 2;
     static constexpr int NSPAN = D / SWE;
     static constexpr int TILE_BYTES = TK * D * 2;        // one K or V tile
     static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
-    static constexpr int NSTAGE_RAW = 98304 / STAGE_BYTES;
+    static constexpr int NSTAGE_RAW = (DEEP ? 196608 : 98304) / STAGE_BYTES;
     static constexpr int NSTAGE = NSTAGE_RAW < 2 ? 2 : (NSTAGE_RAW > 8 ? 8 : NSTAGE_RAW);
+    // Consumer groups.  Group g takes stages g, g + NG, ...; the ring depth is a
+    // multiple of NG so that the stage a group waits for reuses a slot whose previous
+    // stage that same group consumed (its barrier is then at most one phase behind).
+    static constexpr int NG = (DEEP && NSTAGE % 2 == 0) ? 2 : 1;
+    static constexpr int NCW = NW * NG;                  // consumer warps
     static constexpr int QROWS = MT * 16;
     static constexpr int QPITCH = D + 8;                 // halfs; +16 B breaks bank conflicts
     static constexpr int Q_BYTES = (QROWS * QPITCH * 2 + 15) / 16 * 16;
@@ -49,11 +58,15 @@ struct DecodeCfg {
     // split merge: weights [MAX_SPLIT][QROWS] + M, L, and two bulk-copy buffers of >= 1 split each
     static constexpr int CMB_BYTES = (MAX_SPLIT * QROWS + 2 * QROWS) * 4 + 2 * QROWS * D * 4;
     static constexpr int STAGES_BYTES = NSTAGE * STAGE_BYTES;
-    static constexpr int BIG0 = STAGES_BYTES > RED_BYTES ? STAGES_BYTES : RED_BYTES;
+    // Group merge: group 1 hands its per-lane (m, l, O) fragments to group 0.
+    static constexpr int GX_BYTES = NG > 1 ? NW * 32 * (MT * D / 2 + 4 * MT) * 4 : 0;
+    static constexpr int RED0 = RED_BYTES > GX_BYTES ? RED_BYTES : GX_BYTES;
+    static constexpr int BIG0 = STAGES_BYTES > RED0 ? STAGES_BYTES : RED0;
     static constexpr int BIG = BIG0 > CMB_BYTES ? BIG0 : CMB_BYTES;
     static constexpr int SMEM_BYTES = 1024 + BIG + Q_BYTES + 256;   // + barriers/flags
-    static constexpr int THREADS = 32 * (NW + 1);
+    static constexpr int THREADS = 32 * (NCW + 1);
     static_assert(NW * 16 == TK, "each consumer warp owns 16 rows of a stage");
+    static_assert(NSTAGE % NG == 0, "ring depth a multiple of the consumer groups");
     static_assert(SMEM_BYTES <= 232448, "shared memory over budget");
 };
 
@@ -83,12 +96,12 @@ struct DecodeParams {
 // are 3-D over (D, block_size, n_blocks * H_kv)); sequences have their own lengths.
 // SPLIT = false: a launch with n_split == 1 (no partials, no merge), compiled
 // without the split-merge code so that code does not shape the streaming loop.
-template <int D, int MT, bool PAGED = false, bool SPLIT = true>
-__global__ void __launch_bounds__(DecodeCfg<D, MT>::THREADS)
+template <int D, int MT, bool PAGED = false, bool SPLIT = true, bool DEEP = false>
+__global__ void __launch_bounds__(DecodeCfg<D, MT, DEEP>::THREADS)
 decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                   const DecodeParams p) {
-    using C = DecodeCfg<D, MT>;
-    constexpr int TK = C::TK, NW = C::NW, SWB = C::SWB, SWE = C::SWE, NSPAN = C::NSPAN;
+    using C = DecodeCfg<D, MT, DEEP>;
+    constexpr int TK = C::TK, NW = C::NW, NG = C::NG, NCW = C::NCW, SWB = C::SWB, SWE = C::SWE, NSPAN = C::NSPAN;
     constexpr int NSTAGE = C::NSTAGE, QROWS = C::QROWS, QPITCH = C::QPITCH;
 
     extern __shared__ uint8_t smem_raw[];
@@ -136,16 +149,16 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         fence_proxy_async_smem();
     }
     __syncthreads();
-    if (warp < NW) {
+    if (warp < NCW) {
         // Consumers stage Q (padded, rows >= nrows zero) while the producer's first
         // K/V copies are already in flight.
-        for (int idx = tid; idx < QROWS * (D / 8); idx += NW * 32) {
+        for (int idx = tid; idx < QROWS * (D / 8); idx += NCW * 32) {
             const int row = idx / (D / 8), ch = idx % (D / 8);
             uint4 v = make_uint4(0, 0, 0, 0);
             if (row < nrows) v = *reinterpret_cast<const uint4*>(p.Q + (row_base + row) * D + ch * 8);
             *reinterpret_cast<uint4*>(sQ + row * QPITCH + ch * 8) = v;
         }
-        named_bar_sync(1, NW * 32);
+        named_bar_sync(1, NCW * 32);
     }
 
     float o[MT][D / 8][4];
@@ -158,7 +171,7 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         for (int n = 0; n < D / 8; ++n) o[mt][n][0] = o[mt][n][1] = o[mt][n][2] = o[mt][n][3] = 0.f;
     }
 
-    if (warp == NW && PAGED) {
+    if (warp == NCW && PAGED) {
         // ------------------------------------------------------------ TMA producer (paged)
         // The whole warp walks the stages; lanes hold the pool-block ids of 32
         // consecutive logical blocks (one coalesced load), lane 0 issues the copies.
@@ -218,7 +231,7 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
             for (int i = first; i < issued; ++i)
                 mbar_wait_bounded(&full[i % NSTAGE], (i / NSTAGE) & 1, &dummy, p.timeout_ns);
         }
-    } else if (warp == NW) {
+    } else if (warp == NCW) {
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
             tma_prefetch_desc(&tmK);
@@ -255,7 +268,8 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         const int cq = lane & 3;
         const int lm = lane >> 3, lr = lane & 7;
         const uint32_t sQa = smem_u32(sQ);
-        for (int i = 0; i < n_st; ++i) {
+        const int g = warp / NW, wg = warp % NW;      // consumer group, 16-row slice of a stage
+        for (int i = g; i < n_st; i += NG) {
             const int slot = i % NSTAGE;
             bool ok = mbar_wait_bounded(&full[slot], (i / NSTAGE) & 1, abort_flag, p.timeout_ns);
             ok = __all_sync(0xffffffffu, ok);
@@ -272,7 +286,7 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
 #pragma unroll
             for (int ks = 0; ks < D / 16; ++ks) {
                 uint32_t b00, b01, b10, b11;
-                const int krow = warp * 16 + lr + ((lm >> 1) << 3);
+                const int krow = wg * 16 + lr + ((lm >> 1) << 3);
                 const int kcol = ks * 16 + ((lm & 1) << 3);
                 ldmatrix_x4(sK + swz_offset<SWB>(TK, krow, kcol), b00, b01, b10, b11);
 #pragma unroll
@@ -287,7 +301,7 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
             }
             // Mask keys past the end of this split (only the last stage can hold them).
             if (i == n_st - 1) {
-                const int kv0 = kv_lo + i * TK + warp * 16 + 2 * cq;
+                const int kv0 = kv_lo + i * TK + wg * 16 + 2 * cq;
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -319,10 +333,12 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
                         ps += s[mt][nt][2 * hh] + s[mt][nt][2 * hh + 1];
                     }
                     lsum[mt][hh] = lsum[mt][hh] * f + ps;
+                    if (__any_sync(0xffffffffu, f != 1.0f)) {    // the row max moved (rare after the start)
 #pragma unroll
-                    for (int n = 0; n < D / 8; ++n) {
-                        o[mt][n][2 * hh] *= f;
-                        o[mt][n][2 * hh + 1] *= f;
+                        for (int n = 0; n < D / 8; ++n) {
+                            o[mt][n][2 * hh] *= f;
+                            o[mt][n][2 * hh + 1] *= f;
+                        }
                     }
                 }
                 pa[mt][0] = pack_half2(s[mt][0][0], s[mt][0][1]);
@@ -334,13 +350,13 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
 #pragma unroll
             for (int dp = 0; dp < D / 16; ++dp) {
                 uint32_t b0a, b1a, b0b, b1b;
-                const int vrow = warp * 16 + lr + ((lm & 1) << 3);
+                const int vrow = wg * 16 + lr + ((lm & 1) << 3);
                 const int vcol = dp * 16 + ((lm >> 1) << 3);
                 ldmatrix_x4_trans(sV + swz_offset<SWB>(TK, vrow, vcol), b0a, b1a, b0b, b1b);
                 if (PAGED && i == n_st - 1) {
                     // P is 0 for keys past the end, but 0 * (Inf or NaN) is not: clear the V
                     // halves of those keys (this lane's keys 2cq, 2cq+1, 2cq+8, 2cq+9).
-                    const int k0 = kv_lo + i * TK + warp * 16 + 2 * cq;
+                    const int k0 = kv_lo + i * TK + wg * 16 + 2 * cq;
                     const uint32_t m0 = (k0 < kv_hi ? 0x0000ffffu : 0u) | (k0 + 1 < kv_hi ? 0xffff0000u : 0u);
                     const uint32_t m1 = (k0 + 8 < kv_hi ? 0x0000ffffu : 0u) | (k0 + 9 < kv_hi ? 0xffff0000u : 0u);
                     b0a &= m0; b0b &= m0; b1a &= m1; b1b &= m1;
@@ -368,6 +384,51 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
             if (ticket == static_cast<unsigned>(p.n_split - 1)) p.counters[cidx] = 0u;
         }
         return;
+    }
+
+    if constexpr (NG > 1) {
+        // Group 1 hands its fragments (same rows and columns as group 0's warp of the
+        // same slice) to group 0, which merges them by log-sum-exp in registers.
+        constexpr int PER_LANE = MT * D / 2 + 4 * MT;
+        float* gx = reinterpret_cast<float*>(sBig) + ((warp % NW) * 32 + lane) * PER_LANE;
+        if (warp >= NW && warp < NCW) {
+            int k = 0;
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) { gx[k++] = mrow[mt][hh]; gx[k++] = lsum[mt][hh]; }
+#pragma unroll
+                for (int n = 0; n < D / 8; ++n)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) gx[k++] = o[mt][n][e];
+            }
+        }
+        __syncthreads();
+        if (warp < NW) {
+            int k = 0;
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                float fa[2], fb[2];
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    const float mb = gx[k++], lb = gx[k++];
+                    const float M = fmaxf(mrow[mt][hh], mb);
+                    const float Mu = (M == -CUDART_INF_F) ? 0.f : M;
+                    fa[hh] = ex2_approx((mrow[mt][hh] - Mu) * c);
+                    fb[hh] = ex2_approx((mb - Mu) * c);
+                    mrow[mt][hh] = M;
+                    lsum[mt][hh] = lsum[mt][hh] * fa[hh] + lb * fb[hh];
+                }
+#pragma unroll
+                for (int n = 0; n < D / 8; ++n)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int hh = e >> 1;
+                        o[mt][n][e] = o[mt][n][e] * fa[hh] + gx[k++] * fb[hh];
+                    }
+            }
+        }
+        __syncthreads();   // fragments read before the reduction below reuses the memory
     }
 
     float* red_m = reinterpret_cast<float*>(sBig);            // [NW][QROWS]
@@ -503,7 +564,7 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         issue(0);
         if (n_chunks > 1) issue(1);
     }
-    for (int r = warp; r < nrows; r += NW + 1) {
+    for (int r = warp; r < nrows; r += C::THREADS / 32) {
         float M = -CUDART_INF_F;
         for (int s2 = lane; s2 < ns; s2 += 32) M = fmaxf(M, __ldcg(ml + (s2 * nrows + r) * 2));
 #pragma unroll

@@ -182,6 +182,7 @@ struct Plan {
     int mt = 1;          // decode: 16-row MMA tiles per CTA
     int n_rg = 1;        // decode: row groups per (b, h_kv)
     int n_split = 1;     // decode: KV splits
+    bool deep = false;   // decode: the deep-ring kernel (one CTA per SM, all CTAs resident)
     int chunk = 0;       // decode: KV rows per split
     size_t ws_bytes = 0; // workspace the plan uses
     long long ctas = 0;
@@ -219,7 +220,7 @@ int decode_bps(int D, int mt, int* bps) {
 }
 
 int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_bytes, int sm_count,
-              int blocks_per_sm, Plan* pl, bool causal = false, double cta_rate = 1.0) {
+              int blocks_per_sm, Plan* pl, bool causal = false, double cta_rate = 1.0, bool allow_deep = true) {
     const int G = H_q / H_kv;
     // Causal with several query rows takes the prefill kernel (the decode kernel has
     // no per-row mask); with one row the mask keeps every key, so decode is exact.
@@ -239,7 +240,10 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
         const int n_kv = (S_kv + bc - 1) / bc;
         int k = (rem > 0 && !causal) ? cap / rem : 1;   // causal units differ in size: no split
         k = k > 4 ? 4 : k;
-        k = k > n_kv / 2 ? n_kv / 2 : k;
+        // Each chunk keeps >= 4 KV tiles: writing and merging the partials costs about
+        // as much as 3 KV steps (measured: S = 512, 4 tiles in 2 chunks, took 21 us
+        // against 16 us unsplit).
+        k = k > n_kv / 4 ? n_kv / 4 : k;
         if (k >= 2) {
             const int per = (n_kv + k - 1) / k;
             const int k_eff = (n_kv + per - 1) / per;
@@ -271,29 +275,51 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
     // n_split partials of nrows x D floats).
     // Constants fitted to a split-count sweep on B200 (KV=4096 at B=1/16/64, KV=131072 at B=1).
     // cta_rate < 1: a CTA streams slower (paged KV: one small TMA copy per page).
-    const double kBwTotal = 6.0e3, kBwCta = 50.0 * cta_rate, kBwMerge = 100.0;   // GB/s == bytes/ns -> x1e-3 per us
-    const double kT0 = 2.0, kMerge0 = 1.5;
+    // Split merge: ~3 us of round trips (partials out, ticket, partials back) measured on
+    // B200 (KV=512, B=1: 8 one-stage splits 6.4 us against 3.3 us for one stage alone);
+    // the 32-row kernel (MT = 2) merges far slower (MQA, KV=512: 1 split 10.5 us, 8 splits
+    // 19.8 us), so its splits must buy more streaming time.
+    const double kBwMerge = 200.0;   // GB/s == bytes/ns -> x1e-3 per us
+    const double kT0 = 2.0, kMerge0 = pl->mt == 1 ? 3.0 : 10.0;
     const double stage_bytes = 2.0 * TK * D * 2;
     const double total_bytes = static_cast<double>(units) * total_stages * stage_bytes;
     const int nrows = R < 16 * pl->mt ? R : 16 * pl->mt;
     int best_s = 1;
+    bool best_deep = false;
     double best_cost = 1e300;
     const int max_s = total_stages < kf::DecodeCfg<128, 1>::MAX_SPLIT ? total_stages : kf::DecodeCfg<128, 1>::MAX_SPLIT;
     const long long rows = static_cast<long long>(B) * H_q * S_q;
-    for (int s = 1; s <= max_s; ++s) {
-        const int nst = (total_stages + s - 1) / s;
-        const int s_eff = (total_stages + nst - 1) / nst;
-        if (s_eff != s) continue;
-        if (s > 1 && (units > kCounterSlots || split_ws_bytes(rows, s, D) > ws_bytes)) break;
-        const double ctas = static_cast<double>(units) * s;
-        const double bw = ctas * kBwCta < kBwTotal ? ctas * kBwCta : kBwTotal;
-        const double t_stream = total_bytes / (bw * 1e3) + kT0 * std::ceil(ctas / cap);
-        const double t_cta = kT0 + nst * stage_bytes / (kBwCta * 1e3);
-        const double t_merge = s > 1 ? kMerge0 + s * nrows * D * 4.0 / (kBwMerge * 1e3) : 0.0;
-        const double cost = (t_stream > t_cta ? t_stream : t_cta) + t_merge;
-        if (cost < best_cost * 0.999) {
-            best_cost = cost;
-            best_s = s;
+    // The deep-ring kernel (contiguous K/V, 16-row tiles only: one CTA per SM, two
+    // consumer groups) is a candidate when every CTA of the launch is resident.
+    // Measured against the one-group kernel on B200 (B=1, 16 splits): a whole launch
+    // reaches ~6.6 instead of ~6.0 TB/s, for ~0.6 us more fixed cost (the groups'
+    // merge, the larger ring's set-up): it wins from about 8K keys at B=1 and at B=16,
+    // KV=4096.
+    const int deep_opt = (allow_deep && pl->mt == 1)
+                             ? (std::getenv("KF_DECODE_DEEP") ? std::atoi(std::getenv("KF_DECODE_DEEP")) : -1) : 0;
+    for (int deep = 0; deep < 2; ++deep) {
+        if ((deep == 1 && deep_opt == 0) || (deep == 0 && deep_opt == 1)) continue;
+        const double kBwCta = (deep ? 55.0 : 50.0) * cta_rate;
+        const double kBwTotal = deep ? 6.6e3 : 6.0e3;
+        const double t_fixed = deep ? 0.6 : 0.0;
+        const double cap_d = deep ? static_cast<double>(sm_count) : cap;
+        for (int s = 1; s <= max_s; ++s) {
+            const int nst = (total_stages + s - 1) / s;
+            const int s_eff = (total_stages + nst - 1) / nst;
+            if (s_eff != s) continue;
+            if (s > 1 && (units > kCounterSlots || split_ws_bytes(rows, s, D) > ws_bytes)) break;
+            const double ctas = static_cast<double>(units) * s;
+            if (deep && ctas > cap_d) break;
+            const double bw = ctas * kBwCta < kBwTotal ? ctas * kBwCta : kBwTotal;
+            const double t_stream = total_bytes / (bw * 1e3) + kT0 * std::ceil(ctas / cap_d);
+            const double t_cta = kT0 + nst * stage_bytes / (kBwCta * 1e3);
+            const double t_merge = s > 1 ? kMerge0 + s * nrows * D * 4.0 / (kBwMerge * 1e3) : 0.0;
+            const double cost = (t_stream > t_cta ? t_stream : t_cta) + t_merge + t_fixed;
+            if (cost < best_cost * 0.999) {
+                best_cost = cost;
+                best_s = s;
+                best_deep = deep != 0;
+            }
         }
     }
     // Tuning override (benchmark sweeps): KF_DECODE_NSPLIT=<n> forces the split
@@ -305,6 +331,8 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
             best_s = (total_stages + ((total_stages + want - 1) / want) - 1) / ((total_stages + want - 1) / want);
     }
     const int nst = (total_stages + best_s - 1) / best_s;
+    if (best_deep && static_cast<long long>(units) * best_s > sm_count) best_deep = false;   // after an override
+    pl->deep = best_deep;
     pl->n_split = best_s;
     pl->chunk = nst * TK;
     pl->ws_bytes = best_s > 1 ? split_ws_bytes(rows, best_s, D) : 0;
@@ -325,7 +353,8 @@ int plan_for_call(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_
         rc = decode_bps(D, mt, &bps);
         if (rc != KF_OK) return rc;
     }
-    return make_plan(B, H_q, H_kv, S_q, S_kv, D, ws_bytes, di->sm_count, bps, pl, causal, cta_rate);
+    return make_plan(B, H_q, H_kv, S_q, S_kv, D, ws_bytes, di->sm_count, bps, pl, causal, cta_rate,
+                     cta_rate >= 1.0);   // paged K/V (cta_rate < 1) has no deep-ring kernel
 }
 
 // ------------------------------------------------------------------ launches
@@ -413,17 +442,24 @@ struct Paged {
     int n_blocks, block_size, max_blocks;
 };
 
-template <int D, int MT>
+template <int D, int MT, bool DEEP>
 int launch_decode_t(const Plan& pl, const void* Q, const void* K, const void* V, void* O, float* Mi, float* Li,
                     int unnorm, int B, int H_q, int H_kv, int S_q, int S_kv, void* ws, cudaStream_t s,
                     const Paged* pg, int out_type) {
-    using C = kf::DecodeCfg<D, MT>;
+    using C = kf::DecodeCfg<D, MT, DEEP>;
     int bps = 0;
     const bool split = pl.n_split > 1;
-    int rc = pg ? (split ? kernel_setup<kf::decode_fwd_kernel<D, MT, true, true>>(C::SMEM_BYTES, C::THREADS, &bps)
+    int rc;
+    if constexpr (DEEP) {
+        if (pg) return KF_ERR_INVALID_ARG;    // no deep-ring paged kernel (the planner never asks)
+        rc = split ? kernel_setup<kf::decode_fwd_kernel<D, MT, false, true, true>>(C::SMEM_BYTES, C::THREADS, &bps)
+                   : kernel_setup<kf::decode_fwd_kernel<D, MT, false, false, true>>(C::SMEM_BYTES, C::THREADS, &bps);
+    } else {
+        rc = pg ? (split ? kernel_setup<kf::decode_fwd_kernel<D, MT, true, true>>(C::SMEM_BYTES, C::THREADS, &bps)
                          : kernel_setup<kf::decode_fwd_kernel<D, MT, true, false>>(C::SMEM_BYTES, C::THREADS, &bps))
                 : (split ? kernel_setup<kf::decode_fwd_kernel<D, MT, false, true>>(C::SMEM_BYTES, C::THREADS, &bps)
                          : kernel_setup<kf::decode_fwd_kernel<D, MT, false, false>>(C::SMEM_BYTES, C::THREADS, &bps));
+    }
     if (rc != KF_OK) return rc;
     const int kv_box = S_kv < C::TK ? S_kv : C::TK;
     CUtensorMap mk, mv;
@@ -466,14 +502,20 @@ int launch_decode_t(const Plan& pl, const void* Q, const void* K, const void* V,
     p.timeout_ns = g_timeout_ns.load();
     p.kv_box = pg ? C::TK : kv_box;
     dim3 grid(pl.n_split, H_kv * pl.n_rg, B);
-    if (pg && split)
+    if constexpr (DEEP) {
+        if (split)
+            kf::decode_fwd_kernel<D, MT, false, true, true><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
+        else
+            kf::decode_fwd_kernel<D, MT, false, false, true><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
+    } else if (pg && split) {
         kf::decode_fwd_kernel<D, MT, true, true><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
-    else if (pg)
+    } else if (pg) {
         kf::decode_fwd_kernel<D, MT, true, false><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
-    else if (split)
+    } else if (split) {
         kf::decode_fwd_kernel<D, MT, false, true><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
-    else
+    } else {
         kf::decode_fwd_kernel<D, MT, false, false><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
+    }
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KF_OK : cuda_fail(e);
 }
@@ -481,8 +523,11 @@ int launch_decode_t(const Plan& pl, const void* Q, const void* K, const void* V,
 int launch_decode(const Plan& pl, int D, const void* Q, const void* K, const void* V, void* O, float* Mi,
                   float* Li, int unnorm, int B, int H_q, int H_kv, int S_q, int S_kv, void* ws, cudaStream_t s,
                   const Paged* pg = nullptr, int out_type = kf::KF_OUT_F32) {
-#define KF_DEC(DV, MTV) \
-    return launch_decode_t<DV, MTV>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s, pg, out_type)
+#define KF_DEC(DV, MTV)                                                                                        \
+    return pl.deep ? launch_decode_t<DV, MTV, true>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s, \
+                                                    pg, out_type)                                                  \
+                   : launch_decode_t<DV, MTV, false>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s,\
+                                                     pg, out_type)
     switch (D) {
         case 16: if (pl.mt == 2) KF_DEC(16, 2); KF_DEC(16, 1);
         case 64: if (pl.mt == 2) KF_DEC(64, 2); KF_DEC(64, 1);

@@ -173,3 +173,31 @@ def test_split_merge_paths(cuda, nsplit, monkeypatch):
     assert_close(got, O, f"nsplit {nsplit}")
     assert np.abs(Mi - rMi).max() < 1e-3
     assert np.abs(Li / rLi - 1).max() < 1e-3
+
+
+DEEP_SHAPES = [
+    (1, 32, 8, 1, 4096, 128),    # the C3 B=1 shape
+    (3, 32, 8, 1, 1000, 128),    # ragged last stage
+    (2, 8, 2, 1, 777, 64),       # D=64
+    (1, 40, 8, 1, 2049, 128),    # GQA ratio 5, one key past a stage
+    (2, 16, 8, 2, 513, 16),      # D=16, S_q=2
+]
+
+
+@pytest.mark.parametrize("deep", [0, 1])
+@pytest.mark.parametrize("n_split", [1, 3, 16])
+@pytest.mark.parametrize("shape", DEEP_SHAPES, ids=lambda s: "B{}_Hq{}_Hkv{}_Sq{}_Skv{}_D{}".format(*s))
+def test_decode_ring_variants(cuda, shape, n_split, deep, monkeypatch):
+    """Both decode kernels -- one consumer group with the 3-stage ring, and the deep ring
+    with two consumer groups taking alternate stages -- at forced split counts agree with
+    the fp64 oracle (the planner normally chooses between them; the overrides are its
+    benchmark sweep switches)."""
+    B, H_q, H_kv, S_q, S_kv, D = shape
+    monkeypatch.setenv("KF_DECODE_DEEP", str(deep))
+    monkeypatch.setenv("KF_DECODE_NSPLIT", str(n_split))
+    Q, K, V = normal_qkv(*shape, seed=sum(shape) + 31 * n_split + deep)
+    got, Mi, Li = run_fwd(Q, K, V, cuda, return_lse=True)
+    O, rMi, rLi = oracle64(Q, K, V)
+    assert_close(got, O, f"deep={deep} n_split={n_split} {shape}")
+    assert np.abs(Mi - rMi).max() < 1e-3
+    assert np.abs(Li / rLi - 1).max() < 1e-3
