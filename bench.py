@@ -700,43 +700,62 @@ def run_long_decode_split(args, rank, world, dev, peaks):
         res["p2p"] = {"unavailable": why or "peer window setup failed on another rank"}
         return res
 
-    def step_p2p(_):
-        long_decode_forward(q, k, v, exchange=ex, out=out)
+    fused_ok = torch.tensor([1 if ex.attend(q, k, v, out=out) is not None else 0], device=dev)
+    dist.all_reduce(fused_ok, op=dist.ReduceOp.MIN)
 
-    dist.barrier(device_ids=[dev.index])
-    p2p_host_ms = time_loop(step_p2p, iters, 3, stream)
-    with torch.cuda.stream(side):
-        for i in range(3):
-            step_p2p(i)
-    stream.wait_stream(side)
-    torch.cuda.synchronize()
-    dist.barrier(device_ids=[dev.index])
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        step_p2p(0)
-    g.replay()
-    torch.cuda.synchronize()
-    dist.barrier(device_ids=[dev.index])
-    e0.record(stream)
-    for _ in range(iters):
+    def time_p2p(fused):
+        def step_p2p(_):
+            long_decode_forward(q, k, v, exchange=ex, out=out, fused=fused)
+
+        dist.barrier(device_ids=[dev.index])
+        host = time_loop(step_p2p, iters, 3, stream)
+        with torch.cuda.stream(side):
+            for i in range(3):
+                step_p2p(i)
+        stream.wait_stream(side)
+        torch.cuda.synchronize()
+        dist.barrier(device_ids=[dev.index])
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step_p2p(0)
         g.replay()
-    e1.record(stream)
-    e1.synchronize()
-    p2p_graph_ms = e0.elapsed_time(e1) / iters
-    del g
-    torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        dist.barrier(device_ids=[dev.index])
+        e0.record(stream)
+        for _ in range(iters):
+            g.replay()
+        e1.record(stream)
+        e1.synchronize()
+        graph = e0.elapsed_time(e1) / iters
+        del g
+        torch.cuda.synchronize()
+        return host, graph
+
+    timings = {"two_launch": time_p2p(False)}
+    if int(fused_ok.item()):
+        timings["fused"] = time_p2p(True)
     rc, raw = device_error()                # an expired peer wait would void the timing
     ex.close()
-    p2p_host_ms, p2p_graph_ms, bad = max_over_ranks([p2p_host_ms, p2p_graph_ms, float(rc != 0)], world, dev)
-    if bad:
+    flat = [x for k in ("two_launch", "fused") if k in timings for x in timings[k]]
+    vals = max_over_ranks(flat + [float(rc != 0)], world, dev)
+    if vals[-1]:
         res["p2p"] = {"unavailable": f"a peer wait expired during timing (device error word {raw:#x})"}
         return res
-    gbs_p2p = decode_bytes(1, H_Q, H_KV, S_kv, D) / (p2p_graph_ms * 1e-3) / 1e9
-    res["p2p"] = {"us": round(p2p_graph_ms * 1e3, 2), "host_call_us": round(p2p_host_ms * 1e3, 2),
-                  "GB/s_total": round(gbs_p2p, 1), "frac_hbm_per_gpu": round(gbs_p2p / world / peaks["hbm_gbs"], 3),
-                  "exchange": "kf_attn_exchange_combine: {value, sequence} words written into the peers' windows "
-                              "over NVLink (CUDA IPC), polled and merged in one kernel; no NCCL; us = CUDA-graph "
-                              "replay of partial + exchange"}
+    what = {"two_launch": "kf_attn_fwd_partial, then kf_attn_exchange_combine: {value, sequence} words written into "
+                          "the peers' windows over NVLink (CUDA IPC), polled and merged in a second kernel",
+            "fused": "kf_attn_fwd_exchange: the decode kernel's merging CTA of each (b, h_kv) writes its partial into "
+                     "the peers' windows and merges theirs; one launch"}
+    i = 0
+    for key in ("two_launch", "fused"):
+        if key not in timings:
+            continue
+        host_ms, graph_ms = vals[i], vals[i + 1]
+        i += 2
+        gbs_p = decode_bytes(1, H_Q, H_KV, S_kv, D) / (graph_ms * 1e-3) / 1e9
+        res["p2p" if key == "fused" else "p2p_two_launch"] = {
+            "us": round(graph_ms * 1e3, 2), "host_call_us": round(host_ms * 1e3, 2), "GB/s_total": round(gbs_p, 1),
+            "frac_hbm_per_gpu": round(gbs_p / world / peaks["hbm_gbs"], 3),
+            "exchange": what[key] + "; no NCCL; us = CUDA-graph replay, max over ranks"}
     return res
 
 

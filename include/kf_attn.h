@@ -158,7 +158,7 @@ int kf_attn_combine_packed(const float* parts, long long part_stride, int n_part
  *                            part_stride floats (>= B*H_q*S_q*(D+2), multiple
  *                            of 4) and n_chunks CTAs (1 <= n_chunks <= SMs):
  *                            staging part + 2 x world slots of 8-byte words +
- *                            n_chunks call counters
+ *                            per-unit and n_chunks call counters
  *   kf_peer_window_alloc     cudaMalloc + zero fill + CUDA IPC export; writes
  *                            KF_PEER_HANDLE_BYTES opaque bytes to handle_out
  *   kf_peer_window_open      maps another process's window (from its handle)
@@ -182,6 +182,25 @@ int kf_peer_window_close(void* peer_window);
 int kf_peer_window_free(void* window);
 int kf_attn_exchange_combine(void* const* windows, int world, int rank, long long part_stride, int n_chunks,
                              float* O, float* Mi, float* Li, int B, int H_q, int S_q, int D, void* stream);
+
+/* The same exchange fused into the decode kernel: one launch per decode step.  Q is
+ * replicated, K/V [B, H_kv, S_kv, D] hold this rank's contiguous KV range; the kernel
+ * CTA that merges a (b, h_kv) unit's KV splits writes the unit's partial straight into
+ * every rank's window as {value, sequence} words, polls its own window for the other
+ * ranks' words of that unit and writes the merged O (and Mi/Li) of the whole KV cache.
+ * No staging part, no second launch.  Windows as above (kf_peer_window_bytes with any
+ * n_chunks); each (b, h_kv) unit keeps its own call counter in the window, so this call
+ * and kf_attn_exchange_combine may share windows.  Supported: D = 128, world 1, 2, 4
+ * or 8, H_q/H_kv * S_q <= 16, and shapes whose launch fits the SMs in one wave (every
+ * CTA a peer waits for is then resident); other shapes return KF_ERR_INVALID_ARG (use
+ * kf_attn_fwd_partial + kf_attn_exchange_combine).  Workspace for the KV splits, sized
+ * by kf_attn_exchange_workspace_bytes (NULL: fewer splits).  Waits are bounded as above.
+ * No reference counterpart (the reference is single-GPU). */
+int kf_attn_fwd_exchange(const void* Q, const void* K, const void* V, void* const* windows, int world, int rank,
+                         long long part_stride, float* O, float* Mi, float* Li,
+                         int B, int H_q, int H_kv, int S_q, int S_kv, int D,
+                         void* workspace, size_t workspace_bytes, void* stream);
+size_t kf_attn_exchange_workspace_bytes(int B, int H_q, int H_kv, int S_q, int S_kv, int D);
 
 /* Bytes of workspace the call with these arguments would use (0 if none). */
 size_t kf_attn_workspace_bytes(int B, int H_q, int H_kv, int S_q, int S_kv, int D);

@@ -36,7 +36,7 @@ EXPORTED = [
     "kf_selftest_wait_timeout",
     "kf_rmsnorm", "kf_rope", "kf_swiglu",
     "kf_peer_window_bytes", "kf_peer_window_alloc", "kf_peer_window_open", "kf_peer_window_close",
-    "kf_peer_window_free", "kf_attn_exchange_combine",
+    "kf_peer_window_free", "kf_attn_exchange_combine", "kf_attn_fwd_exchange", "kf_attn_exchange_workspace_bytes",
     "kf_fill_normal_f16",
 ]
 
@@ -118,6 +118,10 @@ def lib():
     L.kf_peer_window_free.restype = I
     L.kf_attn_exchange_combine.argtypes = [ctypes.POINTER(P), I, I, LL, I, P, P, P, I, I, I, I, P]
     L.kf_attn_exchange_combine.restype = I
+    L.kf_attn_fwd_exchange.argtypes = [P, P, P, ctypes.POINTER(P), I, I, LL, P, P, P, I, I, I, I, I, I, P, Z, P]
+    L.kf_attn_fwd_exchange.restype = I
+    L.kf_attn_exchange_workspace_bytes.argtypes = [I, I, I, I, I, I]
+    L.kf_attn_exchange_workspace_bytes.restype = Z
     L.kf_rmsnorm.argtypes = [P, P, P, P, LL, I, F, U, P]
     L.kf_rmsnorm.restype = I
     L.kf_rope.argtypes = [P, P, P, P, I, I, I, I, I, I, F, LL, LL, LL, LL, LL, LL, U, P]

@@ -27,6 +27,7 @@
 #include <math_constants.h>
 
 #include "kf_ptx.cuh"
+#include "peer_sm100.cuh"
 
 namespace kf {
 
@@ -90,13 +91,152 @@ struct DecodeParams {
     const int* block_table;
     const int* seq_lens;
     int max_blocks, block_size;
+    // Fused cross-GPU exchange (kernels with XW > 0, XW = world size; see xch_unit):
+    // windows of every rank as mapped here (xown = the own one), part stride, rows of
+    // a part (B * H_q * S_q), this rank, and the own window's per-unit call counters.
+    float* xwin[kMaxPeers];
+    float* xown;
+    unsigned* xcalls;
+    long long xps, xrows;
+    int xrank;
 };
+
+// Cross-GPU exchange of one unit's softmax state, fused into the decode kernel of
+// long-context decode with the KV cache split by ranges over XW GPUs.  The CTA that
+// holds the unit's merged partial over this rank's keys (rows [row_base, row_base +
+// nrows): O_u un-normalised per item of `acc`, raw-score max sM and sum sL per row)
+// writes it into slot (parity, rank) of every rank's window as 8-byte {value, sequence
+// number} words (one single-copy-atomic store each, the low-latency protocol of the
+// exchange-and-merge kernel), then polls the same rows of every rank's slot in its own
+// window (bounded) and merges the XW parts by log-sum-exp into O, Mi, Li.  The sequence
+// number is the unit's call counter in the own window, so the launch can be replayed
+// from a CUDA graph.  Called by every thread of the CTA.  The launch is a single wave
+// (the deep-ring plan), so every CTA a peer waits for is resident.
+template <int XW, int D, int KMAX, int THREADS>
+__device__ __forceinline__ void xch_unit(const DecodeParams& p, size_t cidx, int nrows, size_t row_base,
+                                         const float4 (&acc)[KMAX], const float* sM, const float* sL,
+                                         volatile unsigned* s_seq, float* scratch) {
+    const int tid = threadIdx.x;
+    if (tid == 0) *s_seq = p.xcalls[cidx] + 1u;
+    __syncthreads();
+    const unsigned seq = *s_seq;
+    const int par = static_cast<int>(seq & 1u);
+    const long long ps = p.xps, rows = p.xrows;
+    const int items = nrows * (D / 4);
+    // 1. send
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k) {
+        const int it = tid + k * THREADS;
+        if (it < items) {
+            const long long e = static_cast<long long>(row_base + it / (D / 4)) * D + (it % (D / 4)) * 4;
+#pragma unroll
+            for (int dst = 0; dst < XW; ++dst) {
+                unsigned long long* w =
+                    reinterpret_cast<unsigned long long*>(p.xwin[dst] + peer_slot_off(ps, XW, par, p.xrank)) + e;
+                st_ll(w, acc[k].x, seq);
+                st_ll(w + 1, acc[k].y, seq);
+                st_ll(w + 2, acc[k].z, seq);
+                st_ll(w + 3, acc[k].w, seq);
+            }
+        }
+    }
+    if (tid < nrows) {
+        const long long gr = static_cast<long long>(row_base) + tid;
+        const float m_nat = sM[tid] * p.scale;          // natural-log units of the scaled scores
+#pragma unroll
+        for (int dst = 0; dst < XW; ++dst) {
+            unsigned long long* w = reinterpret_cast<unsigned long long*>(p.xwin[dst] + peer_slot_off(ps, XW, par, p.xrank));
+            st_ll(w + rows * D + gr, m_nat, seq);
+            st_ll(w + rows * D + rows + gr, sL[tid], seq);
+        }
+    }
+    // 2. every rank's (m, l) of these rows from the own window (one poll round for a
+    // thread), the merge weights w_g = e^(m_g - M) and L = sum_g w_g l_g into scratch.
+    constexpr float LOG2E = 1.4426950408889634f;
+    const unsigned long long* slots =
+        reinterpret_cast<const unsigned long long*>(p.xown + peer_slot_off(ps, XW, par, 0));
+    float* x_w = scratch;                     // [XW][nrows] weights, then [nrows] L and M
+    float* x_L = scratch + XW * nrows;
+    float* x_M = x_L + nrows;
+    const uint64_t t0 = global_timer_ns();
+    bool ok = true;
+    auto poll = [&](unsigned long long& w, const unsigned long long* addr) {
+        uint32_t spins = 0;
+        while (static_cast<unsigned>(w >> 32) != seq) {
+            if ((++spins & 15u) == 0u && global_timer_ns() - t0 > p.timeout_ns) { ok = false; return; }
+            w = ld_word(addr);
+        }
+    };
+    __syncthreads();                          // sM / sL read by the send above
+    if (tid < nrows) {
+        const long long gr = static_cast<long long>(row_base) + tid;
+        unsigned long long wm[XW], wl[XW];
+#pragma unroll
+        for (int g = 0; g < XW; ++g) {
+            wm[g] = ld_word(slots + g * ps + rows * D + gr);
+            wl[g] = ld_word(slots + g * ps + rows * D + rows + gr);
+        }
+#pragma unroll
+        for (int g = 0; g < XW; ++g) {
+            poll(wm[g], slots + g * ps + rows * D + gr);
+            poll(wl[g], slots + g * ps + rows * D + rows + gr);
+        }
+        float M = -CUDART_INF_F;
+#pragma unroll
+        for (int g = 0; g < XW; ++g) M = fmaxf(M, __uint_as_float(static_cast<unsigned>(wm[g])));
+        const float Mu = (M == -CUDART_INF_F) ? 0.f : M;
+        float L = 0.f;
+#pragma unroll
+        for (int g = 0; g < XW; ++g) {
+            const float wt = ex2_approx((__uint_as_float(static_cast<unsigned>(wm[g])) - Mu) * LOG2E);
+            x_w[g * nrows + tid] = wt;
+            L += wt * __uint_as_float(static_cast<unsigned>(wl[g]));
+        }
+        x_L[tid] = L;
+        x_M[tid] = M;
+        if (p.Mi) p.Mi[gr] = M;
+        if (p.Li) p.Li[gr] = L;
+    }
+    ok = __syncthreads_and(ok) != 0;
+    // 3. O = sum_g w_g O_g / L: a thread issues the 4 * XW words of its item together.
+#pragma unroll 1
+    for (int k = 0; k < KMAX && ok; ++k) {
+        const int it = tid + k * THREADS;
+        if (it >= items) continue;
+        const int r = it / (D / 4);
+        const long long e = static_cast<long long>(row_base + r) * D + (it % (D / 4)) * 4;
+        unsigned long long w[XW][4];
+#pragma unroll
+        for (int g = 0; g < XW; ++g)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) w[g][j] = ld_word(slots + g * ps + e + j);
+#pragma unroll
+        for (int g = 0; g < XW; ++g)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) poll(w[g][j], slots + g * ps + e + j);
+        if (!ok) break;
+        float a[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int g = 0; g < XW; ++g) {
+            const float wt = x_w[g * nrows + r];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) a[j] += wt * __uint_as_float(static_cast<unsigned>(w[g][j]));
+        }
+        const float inv = x_L[r] > 0.f ? 1.0f / x_L[r] : 0.f;
+        store_out4(p.O, e, make_float4(a[0] * inv, a[1] * inv, a[2] * inv, a[3] * inv), p.out_type);
+    }
+    if (!ok) atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_PEER);
+    __syncthreads();
+    if (tid == 0) p.xcalls[cidx] = seq;
+}
 
 // PAGED: K/V come from block pools through a per-sequence block table (the maps
 // are 3-D over (D, block_size, n_blocks * H_kv)); sequences have their own lengths.
 // SPLIT = false: a launch with n_split == 1 (no partials, no merge), compiled
 // without the split-merge code so that code does not shape the streaming loop.
-template <int D, int MT, bool PAGED = false, bool SPLIT = true, bool DEEP = false>
+// XW > 0: the unit's result is exchanged with XW - 1 peer GPUs and merged (xch_unit)
+// instead of written.
+template <int D, int MT, bool PAGED = false, bool SPLIT = true, bool DEEP = false, int XW = 0>
 __global__ void __launch_bounds__(DecodeCfg<D, MT, DEEP>::THREADS)
 decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                   const DecodeParams p) {
@@ -113,6 +253,7 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
     uint64_t* merge_bar = empty + NSTAGE;      // [2] split-merge bulk copies
     volatile int* abort_flag = reinterpret_cast<volatile int*>(merge_bar + 2);
     volatile int* is_last = abort_flag + 1;
+    volatile unsigned* s_seq = reinterpret_cast<volatile unsigned*>(is_last + 1);
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
@@ -477,6 +618,28 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
     __syncthreads();
 
     if (!SPLIT || p.n_split == 1) {
+        if constexpr (XW > 0) {
+            constexpr int KX = (QROWS * (D / 4) + C::THREADS - 1) / C::THREADS;
+            float4 acc[KX];
+#pragma unroll
+            for (int k = 0; k < KX; ++k) {
+                const int it = tid + k * C::THREADS;
+                acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (it < nrows * (D / 4)) {
+                    const int row = it / (D / 4), d = (it % (D / 4)) * 4;
+#pragma unroll
+                    for (int w = 0; w < NW; ++w) {
+                        const float wt = wts[w * QROWS + row];
+                        const float4 v = *reinterpret_cast<const float4*>(red_o + (w * QROWS + row) * D + d);
+                        acc[k].x += wt * v.x; acc[k].y += wt * v.y; acc[k].z += wt * v.z; acc[k].w += wt * v.w;
+                    }
+                }
+            }
+            const size_t cidx = (static_cast<size_t>(b) * p.H_kv + hk) * p.n_rg + rg;
+            xch_unit<XW, D, KX, C::THREADS>(p, cidx, nrows, row_base, acc, Mrow, Lrow, s_seq,
+                                            reinterpret_cast<float*>(sQ));
+            return;
+        }
         for (int idx = tid; idx < nrows * (D / 4); idx += C::THREADS) {
             const int row = idx / (D / 4), d = (idx % (D / 4)) * 4;
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -614,6 +777,14 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         }
         __syncthreads();   // buffer (ch & 1) fully read
         if (tid == 0 && ch + 2 < n_chunks) issue(ch + 2);
+    }
+    if constexpr (XW > 0) {
+        // Every thread takes part (the exchange synchronizes the CTA); after a failed
+        // copy above the error word is already set and the peers' merge is void.
+        if (tid == 0) p.counters[cidx] = 0u;
+        xch_unit<XW, D, KMAX, C::THREADS>(p, cidx, nrows, row_base, acc, sM, sL, s_seq,
+                                          reinterpret_cast<float*>(sQ));
+        return;
     }
     if (ok) {
 #pragma unroll

@@ -220,7 +220,8 @@ int decode_bps(int D, int mt, int* bps) {
 }
 
 int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_bytes, int sm_count,
-              int blocks_per_sm, Plan* pl, bool causal = false, double cta_rate = 1.0, bool allow_deep = true) {
+              int blocks_per_sm, Plan* pl, bool causal = false, double cta_rate = 1.0, bool allow_deep = true,
+              bool deep_only = false) {
     const int G = H_q / H_kv;
     // Causal with several query rows takes the prefill kernel (the decode kernel has
     // no per-row mask); with one row the mask keeps every key, so decode is exact.
@@ -295,8 +296,9 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
     // reaches ~6.6 instead of ~6.0 TB/s, for ~0.6 us more fixed cost (the groups'
     // merge, the larger ring's set-up): it wins from about 8K keys at B=1 and at B=16,
     // KV=4096.
-    const int deep_opt = (allow_deep && pl->mt == 1)
-                             ? (std::getenv("KF_DECODE_DEEP") ? std::atoi(std::getenv("KF_DECODE_DEEP")) : -1) : 0;
+    int deep_opt = (allow_deep && pl->mt == 1)
+                       ? (std::getenv("KF_DECODE_DEEP") ? std::atoi(std::getenv("KF_DECODE_DEEP")) : -1) : 0;
+    if (deep_only) deep_opt = 1;                     // the caller rejects a plan that is not deep
     for (int deep = 0; deep < 2; ++deep) {
         if ((deep == 1 && deep_opt == 0) || (deep == 0 && deep_opt == 1)) continue;
         const double kBwCta = (deep ? 55.0 : 50.0) * cta_rate;
@@ -341,7 +343,7 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
 }
 
 int plan_for_call(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_bytes, Plan* pl,
-                  bool causal = false, double cta_rate = 1.0) {
+                  bool causal = false, double cta_rate = 1.0, bool deep_only = false) {
     DeviceInfo* di = nullptr;
     int rc = device_info(&di);
     if (rc != KF_OK) return rc;
@@ -354,7 +356,8 @@ int plan_for_call(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_
         if (rc != KF_OK) return rc;
     }
     return make_plan(B, H_q, H_kv, S_q, S_kv, D, ws_bytes, di->sm_count, bps, pl, causal, cta_rate,
-                     cta_rate >= 1.0);   // paged K/V (cta_rate < 1) has no deep-ring kernel
+                     cta_rate >= 1.0,    // paged K/V (cta_rate < 1) has no deep-ring kernel
+                     deep_only);
 }
 
 // ------------------------------------------------------------------ launches
@@ -442,15 +445,27 @@ struct Paged {
     int n_blocks, block_size, max_blocks;
 };
 
-template <int D, int MT, bool DEEP>
+// Fused cross-GPU exchange arguments (kf_attn_fwd_exchange); null otherwise.
+struct Xch {
+    void* const* windows;
+    int world, rank;
+    long long part_stride;
+};
+
+template <int D, int MT, bool DEEP, int XW = 0>
 int launch_decode_t(const Plan& pl, const void* Q, const void* K, const void* V, void* O, float* Mi, float* Li,
                     int unnorm, int B, int H_q, int H_kv, int S_q, int S_kv, void* ws, cudaStream_t s,
-                    const Paged* pg, int out_type) {
+                    const Paged* pg, int out_type, const Xch* xa = nullptr) {
     using C = kf::DecodeCfg<D, MT, DEEP>;
     int bps = 0;
     const bool split = pl.n_split > 1;
     int rc;
-    if constexpr (DEEP) {
+    if constexpr (XW > 0) {
+        static_assert(DEEP, "the fused exchange runs as a single wave (deep-ring plan)");
+        if (pg || !xa) return KF_ERR_INVALID_ARG;
+        rc = split ? kernel_setup<kf::decode_fwd_kernel<D, MT, false, true, true, XW>>(C::SMEM_BYTES, C::THREADS, &bps)
+                   : kernel_setup<kf::decode_fwd_kernel<D, MT, false, false, true, XW>>(C::SMEM_BYTES, C::THREADS, &bps);
+    } else if constexpr (DEEP) {
         if (pg) return KF_ERR_INVALID_ARG;    // no deep-ring paged kernel (the planner never asks)
         rc = split ? kernel_setup<kf::decode_fwd_kernel<D, MT, false, true, true>>(C::SMEM_BYTES, C::THREADS, &bps)
                    : kernel_setup<kf::decode_fwd_kernel<D, MT, false, false, true>>(C::SMEM_BYTES, C::THREADS, &bps);
@@ -501,8 +516,26 @@ int launch_decode_t(const Plan& pl, const void* Q, const void* K, const void* V,
     p.out_type = out_type;
     p.timeout_ns = g_timeout_ns.load();
     p.kv_box = pg ? C::TK : kv_box;
+    for (int r = 0; r < kf::kMaxPeers; ++r) p.xwin[r] = nullptr;
+    p.xown = nullptr;
+    p.xcalls = nullptr;
+    p.xps = 0;
+    p.xrows = rows;
+    p.xrank = 0;
+    if (xa) {
+        for (int r = 0; r < xa->world; ++r) p.xwin[r] = static_cast<float*>(xa->windows[r]);
+        p.xown = p.xwin[xa->rank];
+        p.xps = xa->part_stride;
+        p.xrank = xa->rank;
+        p.xcalls = reinterpret_cast<unsigned*>(p.xown + kf::peer_unit_calls_off(xa->part_stride, xa->world));
+    }
     dim3 grid(pl.n_split, H_kv * pl.n_rg, B);
-    if constexpr (DEEP) {
+    if constexpr (XW > 0) {
+        if (split)
+            kf::decode_fwd_kernel<D, MT, false, true, true, XW><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
+        else
+            kf::decode_fwd_kernel<D, MT, false, false, true, XW><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
+    } else if constexpr (DEEP) {
         if (split)
             kf::decode_fwd_kernel<D, MT, false, true, true><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
         else
@@ -632,6 +665,17 @@ int noalloc_scratch(void** out) {
     return KF_OK;
 }
 
+}  // namespace
+
+namespace {
+// Plan of a fused exchange call: the deep-ring decode kernel as one wave (D = 128, one
+// 16-row tile per (b, h_kv): H_q / H_kv * S_q <= 16).
+int exchange_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_bytes, Plan* pl) {
+    if (D != 128 || static_cast<long long>(H_q / H_kv) * S_q > 16) return KF_ERR_INVALID_ARG;
+    int rc = plan_for_call(B, H_q, H_kv, S_q, S_kv, D, ws_bytes, pl, false, 1.0, true);
+    if (rc != KF_OK) return rc;
+    return (pl->path == 1 && pl->deep && pl->mt == 1) ? KF_OK : KF_ERR_INVALID_ARG;
+}
 }  // namespace
 
 extern "C" {
@@ -835,6 +879,49 @@ int kf_attn_exchange_combine(void* const* windows, int world, int rank, long lon
     }
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KF_OK : cuda_fail(e);
+}
+
+size_t kf_attn_exchange_workspace_bytes(int B, int H_q, int H_kv, int S_q, int S_kv, int D) {
+    if (validate(reinterpret_cast<const void*>(16), reinterpret_cast<const void*>(16),
+                 reinterpret_cast<const void*>(16), reinterpret_cast<const float*>(16), B, H_q, H_kv, S_q, S_kv,
+                 D) != KF_OK || B == 0 || S_q == 0)
+        return 0;
+    Plan pl;
+    if (exchange_plan(B, H_q, H_kv, S_q, S_kv, D, static_cast<size_t>(-1), &pl) != KF_OK) return 0;
+    return pl.ws_bytes;
+}
+
+int kf_attn_fwd_exchange(const void* Q, const void* K, const void* V, void* const* windows, int world, int rank,
+                         long long part_stride, float* O, float* Mi, float* Li, int B, int H_q, int H_kv, int S_q,
+                         int S_kv, int D, void* workspace, size_t workspace_bytes, void* stream) {
+    int rc = validate(Q, K, V, O, B, H_q, H_kv, S_q, S_kv, D);
+    if (rc != KF_OK) return rc;
+    if (!windows || !(world == 1 || world == 2 || world == 4 || world == 8) || rank < 0 || rank >= world)
+        return KF_ERR_INVALID_ARG;
+    const long long rows = static_cast<long long>(B) * H_q * S_q;
+    if (part_stride < rows * (D + 2) || part_stride % 4 != 0) return KF_ERR_INVALID_ARG;
+    for (int r = 0; r < world; ++r) {
+        if (!windows[r]) return KF_ERR_INVALID_ARG;
+        if (!aligned16(windows[r])) return KF_ERR_MISALIGNED;
+    }
+    if (B == 0 || S_q == 0) return KF_OK;
+    if (!workspace) workspace_bytes = 0;
+    if (workspace && !aligned16(workspace)) return KF_ERR_MISALIGNED;
+    Plan pl;
+    if ((rc = exchange_plan(B, H_q, H_kv, S_q, S_kv, D, workspace_bytes, &pl)) != KF_OK) return rc;
+    const Xch xa{windows, world, rank, part_stride};
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    void* ws = pl.n_split > 1 ? workspace : nullptr;
+    switch (world) {
+        case 1: return launch_decode_t<128, 1, true, 1>(pl, Q, K, V, O, Mi, Li, 0, B, H_q, H_kv, S_q, S_kv, ws, s,
+                                                       nullptr, kf::KF_OUT_F32, &xa);
+        case 2: return launch_decode_t<128, 1, true, 2>(pl, Q, K, V, O, Mi, Li, 0, B, H_q, H_kv, S_q, S_kv, ws, s,
+                                                       nullptr, kf::KF_OUT_F32, &xa);
+        case 4: return launch_decode_t<128, 1, true, 4>(pl, Q, K, V, O, Mi, Li, 0, B, H_q, H_kv, S_q, S_kv, ws, s,
+                                                       nullptr, kf::KF_OUT_F32, &xa);
+        default: return launch_decode_t<128, 1, true, 8>(pl, Q, K, V, O, Mi, Li, 0, B, H_q, H_kv, S_q, S_kv, ws, s,
+                                                        nullptr, kf::KF_OUT_F32, &xa);
+    }
 }
 
 size_t kf_attn_workspace_bytes(int B, int H_q, int H_kv, int S_q, int S_kv, int D) {

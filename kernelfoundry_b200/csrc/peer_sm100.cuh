@@ -35,12 +35,19 @@ constexpr int kMaxPeers = 8;
 //   [0, ps)                                  staging: this rank's partials
 //                                            (O_u [rows][D], then m [rows], then l [rows])
 //   ps + 2 * ps * (parity * world + src)     slot[parity][src]: ps 8-byte words {value, seq}
-//   ps * (1 + 4 * world)                     calls[n_chunks]: this rank's call counters
+//   ps * (1 + 4 * world)                     unit_calls[ps / 16]: call counters of the fused
+//                                            decode exchange, one per (b, h_kv, row group)
+//                                            (units <= rows <= ps / 18)
+//   ps * (1 + 4 * world) + ps / 16           calls[n_chunks]: call counters of the
+//                                            exchange-and-merge kernel, one per CTA
 __host__ __device__ constexpr long long peer_slot_off(long long ps, int world, int parity, int src) {
     return ps + 2 * ps * (static_cast<long long>(parity) * world + src);
 }
-__host__ __device__ constexpr long long peer_calls_off(long long ps, int world) {
+__host__ __device__ constexpr long long peer_unit_calls_off(long long ps, int world) {
     return ps * (1 + 4ll * world);
+}
+__host__ __device__ constexpr long long peer_calls_off(long long ps, int world) {
+    return peer_unit_calls_off(ps, world) + ps / 16;
 }
 __host__ __device__ constexpr long long peer_window_words(long long ps, int world, int n_chunks) {
     return peer_calls_off(ps, world) + n_chunks;

@@ -154,6 +154,8 @@ class PeerExchange:
                 ptrs.append(peer.value)
                 self._opened.append(peer.value)
         self._windows = (ctypes.c_void_p * self.world)(*ptrs)
+        self._xws = None                       # split workspace of the fused path (attend)
+        self._xws_shape = None
         rows, dev = self.rows, self.device
         self._stage = (torch.as_tensor(_DevArray(self._own, (B, H_q, S_q, D), dev), device=dev),
                        torch.as_tensor(_DevArray(self._own + rows * D * 4, (B, H_q, S_q), dev), device=dev),
@@ -181,6 +183,46 @@ class PeerExchange:
               "kf_attn_exchange_combine")
         return out
 
+    def attend(self, q: torch.Tensor, k_shard: torch.Tensor, v_shard: torch.Tensor,
+               out: Optional[torch.Tensor] = None, Mi: Optional[torch.Tensor] = None,
+               Li: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
+        """One launch for the whole decode step (kf_attn_fwd_exchange): attention of q over
+        this rank's KV range, with each (b, h_kv) unit's partial sent to every rank's
+        window and merged with the other ranks' partials inside the same kernel.  Returns
+        the full O, or None when the shape is outside what the fused kernel supports
+        (D = 128, world 1/2/4/8, one wave): the caller then uses the two-launch path.
+        Every rank must make the same calls (the same choice follows from the same
+        shapes)."""
+        import ctypes
+
+        from ._lib import KF_ERR_INVALID_ARG, check, lib
+
+        if tuple(q.shape) != self.shape:
+            raise ValueError("exchange was built for another shape")
+        B, H_q, S_q, D = self.shape
+        H_kv, S_kv = k_shard.shape[1], k_shard.shape[2]
+        L = lib()
+        if self._xws is None or self._xws_shape != (H_kv, S_kv):
+            nbytes = int(L.kf_attn_exchange_workspace_bytes(B, H_q, H_kv, S_q, S_kv, D))
+            self._xws = torch.zeros(max(nbytes, 16), dtype=torch.uint8, device=self.device)
+            self._xws_shape = (H_kv, S_kv)
+        if out is None:
+            out = torch.empty(self.shape, dtype=torch.float32, device=self.device)
+        if out.shape != self.shape or out.dtype != torch.float32 or not out.is_contiguous():
+            raise ValueError("out must be a contiguous float32 tensor of the exchange shape")
+        for t, name in ((q, "q"), (k_shard, "k"), (v_shard, "v")):
+            if not t.is_cuda or t.dtype != torch.float16 or not t.is_contiguous() or t.device != self.device:
+                raise ValueError(f"{name} must be a contiguous fp16 tensor on {self.device}")
+        p = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None  # noqa: E731
+        stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+        rc = L.kf_attn_fwd_exchange(p(q), p(k_shard), p(v_shard), self._windows, self.world, self.rank,
+                                    self.part_stride, p(out), p(Mi), p(Li), B, H_q, H_kv, S_q, S_kv, D,
+                                    p(self._xws), self._xws.numel(), stream)
+        if rc == KF_ERR_INVALID_ARG:
+            return None
+        check(rc, "kf_attn_fwd_exchange")
+        return out
+
     def close(self) -> None:
         """Collective: unmap the peers' windows, then free the own one."""
         from ._lib import check, lib
@@ -206,7 +248,7 @@ def long_decode_forward(q: torch.Tensor, k_shard: torch.Tensor, v_shard: torch.T
                         partial_fn: Optional[Callable] = None, combine_fn: Optional[Callable] = None,
                         gather_buf: Optional[torch.Tensor] = None,
                         out: Optional[torch.Tensor] = None,
-                        exchange: Optional[PeerExchange] = None) -> torch.Tensor:
+                        exchange: Optional[PeerExchange] = None, fused: bool = True) -> torch.Tensor:
     """Attention of q over a KV cache split across the ranks of `group`.
 
     q [B,H_q,S_q,D] is replicated; k_shard/v_shard [B,H_kv,S_r,D] hold this
@@ -220,9 +262,11 @@ def long_decode_forward(q: torch.Tensor, k_shard: torch.Tensor, v_shard: torch.T
     so a decode step can be captured in a CUDA graph.  `partial_fn` /
     `combine_fn` substitute the compute (tests on CPU ranks).
 
-    With ``exchange`` (a :class:`PeerExchange` of q's shape) the partials go to
-    the exchange's staging part and one kernel exchanges them over NVLink and
-    merges: no NCCL call.
+    With ``exchange`` (a :class:`PeerExchange` of q's shape) and ``fused`` (the
+    default), one decode kernel computes this rank's partials, sends them over NVLink
+    and merges (:meth:`PeerExchange.attend`); shapes it does not support, or
+    ``fused=False``, take two launches: the partials go to the exchange's staging part
+    and one kernel exchanges them and merges.  Neither calls NCCL.
     """
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     if exchange is not None:
@@ -230,6 +274,10 @@ def long_decode_forward(q: torch.Tensor, k_shard: torch.Tensor, v_shard: torch.T
 
         if tuple(q.shape) != exchange.shape:
             raise ValueError("exchange was built for another shape")
+        if fused:
+            res = exchange.attend(q, k_shard, v_shard, out=out)
+            if res is not None:
+                return res
         flash_attn_partial(q, k_shard, v_shard, out=exchange.staging())
         return exchange.combine(out=out)
     if partial_fn is None and combine_fn is None:

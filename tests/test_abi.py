@@ -137,7 +137,8 @@ def test_peer_exchange_argument_validation_without_gpu(kf_lib):
     from kernelfoundry_b200 import _lib as L
 
     # window size: staging part + 2 parities x world slots of 8-byte words + n_chunks counters
-    assert kf_lib.kf_peer_window_bytes(2, 4160, 4) == (4160 * (1 + 4 * 2) + 4) * 4
+    # staging + 2 x 2 slots of 8-byte words + per-unit counters (part / 16) + 4 chunk counters
+    assert kf_lib.kf_peer_window_bytes(2, 4160, 4) == (4160 * (1 + 4 * 2) + 4160 // 16 + 4) * 4
     assert kf_lib.kf_peer_window_bytes(0, 4160, 4) == 0
     assert kf_lib.kf_peer_window_bytes(9, 4160, 4) == 0          # more than KF_MAX_PEERS
     assert kf_lib.kf_peer_window_bytes(2, 4162, 4) == 0          # part stride not a multiple of 4
@@ -266,3 +267,24 @@ def test_python_api_refuses_cpu_tensors(kf_lib):
     q = torch.zeros(1, 2, 4, 64, dtype=torch.float16)
     with pytest.raises(ValueError, match="CUDA"):
         flash_attn_fwd(q, q[:, :1], q[:, :1])
+
+
+def test_fused_exchange_argument_checks_without_gpu(kf_lib):
+    """kf_attn_fwd_exchange rejects bad world sizes, ranks, windows and part strides
+    before any CUDA call."""
+    from kernelfoundry_b200 import _lib as L
+
+    wins = (ctypes.c_void_p * 2)(FAKE, FAKE)
+
+    def _x(world=2, rank=0, ps=8 * 132, windows=wins, B=1, D=128):
+        return kf_lib.kf_attn_fwd_exchange(FAKE, FAKE, FAKE, windows, world, rank, ps, FAKE, None, None,
+                                           B, 8, 2, 1, 4096, D, None, 0, None)
+    assert _x(world=3) == L.KF_ERR_INVALID_ARG
+    assert _x(world=0) == L.KF_ERR_INVALID_ARG
+    assert _x(rank=2) == L.KF_ERR_INVALID_ARG
+    assert _x(windows=None) == L.KF_ERR_INVALID_ARG
+    assert _x(ps=8 * 129) == L.KF_ERR_INVALID_ARG                      # part smaller than rows * (D + 2)
+    assert _x(ps=8 * 130 + 2) == L.KF_ERR_INVALID_ARG                  # not a multiple of 4
+    assert _x(windows=(ctypes.c_void_p * 2)(FAKE, MISALIGNED)) == L.KF_ERR_MISALIGNED
+    assert _x(D=96) == L.KF_ERR_UNSUPPORTED_HEAD_DIM
+    assert _x(B=0) == L.KF_OK                                          # empty problem: no launch

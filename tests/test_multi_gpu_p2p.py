@@ -1,8 +1,10 @@
 """KV-split long decode over 2 GPUs with the NVLink peer exchange (no NCCL).
 
-Each rank holds a contiguous KV range; kf_attn_exchange_combine writes its
-partials into the peer's window as {value, sequence} words, polls the peer's
-words in its own window and merges.
+Each rank holds a contiguous KV range; its partials go into the peer's window as
+{value, sequence} words, it polls the peer's words in its own window and merges:
+either inside the decode kernel (kf_attn_fwd_exchange, one launch) or in a
+second kernel after the partial (kf_attn_exchange_combine).  Both paths share
+the windows: the fused calls alternate with two-launch calls.
 Checked against the fp64 oracle over the whole cache, over several calls
 (both parities of the double-buffered slots) and over CUDA-graph replays
 (sequence numbers kept on the device).  The failure path: one rank calls
@@ -54,7 +56,8 @@ def _worker(rank, world, port, result_dir, mode):
         ex = PeerExchange(tuple(q.shape), device=dev)
         result = {}
         if mode == "ok":
-            outs = [long_decode_forward(q, k, v, exchange=ex).cpu().numpy() for _ in range(5)]
+            assert ex.attend(q, k, v) is not None            # the fused kernel supports this shape
+            outs = [long_decode_forward(q, k, v, exchange=ex, fused=(i % 2 == 0)).cpu().numpy() for i in range(6)]
             out = torch.empty(tuple(q.shape), dtype=torch.float32, device=dev)
             stream = torch.cuda.current_stream(dev)
             side = torch.cuda.Stream(dev)
