@@ -752,10 +752,13 @@ def run_long_decode_split(args, rank, world, dev, peaks):
         host_ms, graph_ms = vals[i], vals[i + 1]
         i += 2
         gbs_p = decode_bytes(1, H_Q, H_KV, S_kv, D) / (graph_ms * 1e-3) / 1e9
-        res["p2p" if key == "fused" else "p2p_two_launch"] = {
+        res["p2p_fused" if key == "fused" else "p2p_two_launch"] = {
             "us": round(graph_ms * 1e3, 2), "host_call_us": round(host_ms * 1e3, 2), "GB/s_total": round(gbs_p, 1),
             "frac_hbm_per_gpu": round(gbs_p / world / peaks["hbm_gbs"], 3),
             "exchange": what[key] + "; no NCCL; us = CUDA-graph replay, max over ranks"}
+    # The path long_decode_forward takes by default (fused for two ranks, else two launches).
+    default = "p2p_fused" if (world <= 2 and "p2p_fused" in res) else "p2p_two_launch"
+    res["p2p"] = dict(res[default], path=default)
     return res
 
 
