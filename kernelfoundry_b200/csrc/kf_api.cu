@@ -189,6 +189,7 @@ struct Plan {
     // prefill work list: units = B * H_q * q-blocks; the last (units - plain)
     // units (a partial last wave) are split over split_k CTAs of `per` KV tiles
     int pf_qblk = 1, pf_units = 0, pf_plain = 0, pf_k = 1, pf_per = 0;
+    int pf_tiles = 2;    // prefill: 128-row query tiles per unit
 };
 
 int decode_max_mt(int D) { return D <= 128 ? 2 : 1; }
@@ -227,8 +228,16 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
     // no per-row mask); with one row the mask keeps every key, so decode is exact.
     if (!use_decode(G, S_q, D) || (causal && S_q > 1)) {
         pl->path = 0;
-        const int rows_per_cta = (D <= 128 ? 2 : 1) * 128;
+        const int nq = D <= 128 ? 2 : 1;
         const int bc = D <= 128 ? 128 : 64;
+        // Units of one 128-row tile instead of two when the two-tile units would leave
+        // over half the SMs idle, the one-tile units still fit one wave and the keys are
+        // too few for a KV split (S = 512 at B = 1: 64 two-tile units on 148 SMs).
+        const long long u2 = static_cast<long long>((S_q + 255) / 256) * H_q * B;
+        const long long u1 = static_cast<long long>((S_q + 127) / 128) * H_q * B;
+        const int n_kv_tiles = (S_kv + bc - 1) / bc;
+        pl->pf_tiles = (nq == 2 && !causal && u1 > u2 && u1 <= sm_count && n_kv_tiles < 8) ? 1 : nq;
+        const int rows_per_cta = pl->pf_tiles * 128;
         pl->pf_qblk = (S_q + rows_per_cta - 1) / rows_per_cta;
         const long long units = static_cast<long long>(pl->pf_qblk) * H_q * B;
         if (units > (1ll << 31) - 1) return KF_ERR_INVALID_ARG;
@@ -239,7 +248,7 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
         const int cap = sm_count;
         const int rem = static_cast<int>(units % cap);
         const int n_kv = (S_kv + bc - 1) / bc;
-        int k = (rem > 0 && !causal) ? cap / rem : 1;   // causal units differ in size: no split
+        int k = (rem > 0 && !causal && pl->pf_tiles == nq) ? cap / rem : 1;   // causal units differ in size: no split
         k = k > 4 ? 4 : k;
         // Each chunk keeps >= 4 KV tiles: writing and merging the partials costs about
         // as much as 3 KV steps (measured: S = 512, 4 tiles in 2 chunks, took 21 us
@@ -407,6 +416,7 @@ int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, 
     p.q_box = q_box;
     p.kv_box = kv_box;
     p.n_qblk = pl.pf_qblk;
+    p.unit_tiles = pl.pf_tiles;
     p.B_H = B * H_q;
     p.kv_off = S_kv - S_q;
     p.n_units = pl.pf_units;

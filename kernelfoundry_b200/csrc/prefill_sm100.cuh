@@ -94,7 +94,8 @@ struct PrefillParams {
     // [n_plain, n_units) -- the partial last wave -- is split over split_k CTAs,
     // each taking `per` KV tiles, which write softmax partials to `part` and the
     // last to finish (ticket in `counters`) merges them into O.
-    int n_qblk;         // 256-row blocks per (b, h_q)
+    int n_qblk;         // query blocks of unit_tiles * 128 rows per (b, h_q)
+    int unit_tiles;     // query tiles per unit: NQ, or 1 when two-tile units would leave most SMs idle
     int kv_off;         // S_kv - S_q (>= 0); causal kernels: query i sees keys j <= i + kv_off
     int n_units, n_plain, split_k, per;
     int n_items;        // n_plain + (n_units - n_plain) * split_k; CTAs stride over them
@@ -143,9 +144,9 @@ __device__ __forceinline__ PrefillItem prefill_item(const PrefillParams& p, int 
     it.h = CAUSAL ? (it.unit % p.B_H) % p.H_q : (it.unit / p.n_qblk) % p.H_q;
     it.b = CAUSAL ? (it.unit % p.B_H) / p.H_q : it.unit / (p.n_qblk * p.H_q);
     it.h_kv = it.h / p.G;
-    it.q_row0 = it.qblk * C::NQ * C::BM;
+    it.q_row0 = it.qblk * p.unit_tiles * C::BM;
     const int rows_left = p.S_q - it.q_row0;
-    it.nq_active = rows_left >= C::NQ * C::BM ? C::NQ : (rows_left + C::BM - 1) / C::BM;
+    it.nq_active = rows_left >= p.unit_tiles * C::BM ? p.unit_tiles : (rows_left + C::BM - 1) / C::BM;
     const int n_kv_all = (p.S_kv + C::BC - 1) / C::BC;
     it.kt0 = it.split ? it.chunk * p.per : 0;                                         // first KV tile
     it.n_kv = it.split ? min(p.per, n_kv_all - it.kt0) : n_kv_all;                   // KV tiles of the item

@@ -272,3 +272,21 @@ def test_lazy_rescale_paths(cuda, D, causal):
     else:
         ref = oracle64(Q, K, V)[0]
     assert_close(got, ref, f"rescale D={D} causal={causal}")
+
+
+@pytest.mark.parametrize("shape", [(1, 32, 8, 512, 512, 128), (1, 32, 8, 300, 300, 64), (1, 16, 4, 384, 500, 16),
+                                   (2, 8, 8, 129, 700, 128)],
+                         ids=lambda s: "B{}_Hq{}_Hkv{}_Sq{}_Skv{}_D{}".format(*s))
+def test_single_tile_units(cuda, shape):
+    """Short sequences run one 128-row query tile per CTA (twice the CTAs of two-tile units);
+    results and softmax state match the fp64 oracle."""
+    from kernelfoundry_b200 import plan
+
+    B, H_q, H_kv, S_q, S_kv, D = shape
+    assert plan(*shape)["ctas"] == B * H_q * ((S_q + 127) // 128)
+    Q, K, V = normal_qkv(*shape, seed=sum(shape) + 9)
+    got, Mi, Li = run_fwd(Q, K, V, cuda, return_lse=True)
+    O, rMi, rLi = oracle64(Q, K, V)
+    assert_close(got, O, str(shape))
+    assert np.abs(Mi - rMi).max() < 1e-3
+    assert np.abs(Li / rLi - 1).max() < 1e-3
