@@ -638,8 +638,7 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
             const size_t cidx = (static_cast<size_t>(b) * p.H_kv + hk) * p.n_rg + rg;
             xch_unit<XW, D, KX, C::THREADS>(p, cidx, nrows, row_base, acc, Mrow, Lrow, s_seq,
                                             reinterpret_cast<float*>(sQ));
-            return;
-        }
+        } else {
         for (int idx = tid; idx < nrows * (D / 4); idx += C::THREADS) {
             const int row = idx / (D / 4), d = (idx % (D / 4)) * 4;
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -656,6 +655,7 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         if (tid < nrows) {
             if (p.Mi) p.Mi[row_base + tid] = Mrow[tid] * p.scale;
             if (p.Li) p.Li[row_base + tid] = Lrow[tid];
+        }
         }
         return;
     }

@@ -186,15 +186,17 @@ def test_pointwise_argument_validation_without_gpu(kf_lib):
 
     assert rope(rot=136) == L.KF_ERR_INVALID_ARG               # rot_dim > D
     assert rope(rot=40) == L.KF_ERR_INVALID_ARG                # NeoX needs a multiple of 16
-    assert rope(rot=40, flags=L.KF_ROPE_GPTJ) != L.KF_ERR_INVALID_ARG
+    # Accepted argument sets are checked on empty problems (S = 0): they pass validation and
+    # return before any launch, so no kernel ever runs on these placeholder pointers.
+    assert rope(rot=40, flags=L.KF_ROPE_GPTJ, S=0) == L.KF_OK
     assert rope(rot=36, flags=L.KF_ROPE_GPTJ) == L.KF_ERR_INVALID_ARG
     assert rope(D=1032, rot=64) == L.KF_ERR_INVALID_ARG
     assert rope(theta=0.0) == L.KF_ERR_INVALID_ARG
-    assert rope(theta=0.0, inv=FAKE) != L.KF_ERR_INVALID_ARG   # a frequency table replaces theta
+    assert rope(theta=0.0, inv=FAKE, S=0) == L.KF_OK            # a frequency table replaces theta
     assert rope(qs=(4096, 1024, 130)) == L.KF_ERR_INVALID_ARG  # stride not a multiple of 8
     assert rope(ks=(-2048, 1024, 128)) == L.KF_ERR_INVALID_ARG
     assert rope(k=ctypes.c_void_p(0)) == L.KF_ERR_INVALID_ARG
-    assert rope(k=ctypes.c_void_p(0), Hkv=0) != L.KF_ERR_INVALID_ARG
+    assert rope(k=ctypes.c_void_p(0), Hkv=0, S=0) == L.KF_OK
     assert rope(Hq=0, Hkv=0) == L.KF_ERR_INVALID_ARG
     assert rope(flags=8) == L.KF_ERR_INVALID_ARG
     assert rope(q=MISALIGNED) == L.KF_ERR_MISALIGNED
