@@ -826,9 +826,13 @@ def run_ours(args):
 
     achieved = flops_rank / (kern_ms * 1e-3) / 1e12
     traffic = profile_traffic("prefill_sm100_C2.md")
+    from kernelfoundry_b200 import plan
+    split = plan(1, H_Q, H_KV, S, S, D)["ctas"] > plan(1, H_Q, H_KV, S, S, D, workspace_bytes=0)["ctas"]
+    kernel_name = f"kf::prefill_fwd_kernel<128, false, {'true' if split else 'false'}>"
+
     roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"],
                 "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": traffic,
-                "kernel": "kf::prefill_fwd_kernel<128>", "kernel_ms": round(kern_ms, 5),
+                "kernel": kernel_name, "kernel_ms": round(kern_ms, 5),
                 "kernel_ms_src": "CUDA events around the K timed launches / K (launch gaps included)",
                 "flops_per_launch": flops_rank, "peak_src": f"{peaks['src']} bf16 dense (burst)"}
 

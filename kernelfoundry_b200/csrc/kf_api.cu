@@ -244,7 +244,7 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
         pl->pf_units = static_cast<int>(units);
         pl->pf_plain = pl->pf_units;
         // One CTA per SM: a last wave at most half full is split along KV so it
-        // finishes in 1/k of a unit's time (partials merged by the last chunk).
+        // finishes in 1/k of a unit's time (chunk t merges tile t of the unit).
         const int cap = sm_count;
         const int rem = static_cast<int>(units % cap);
         const int n_kv = (S_kv + bc - 1) / bc;
@@ -376,8 +376,11 @@ int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, 
                    bool causal, int out_type) {
     using C = kf::PrefillCfg<D>;
     int bps = 0;
-    int rc = causal ? kernel_setup<kf::prefill_fwd_kernel<D, true>>(C::SMEM_BYTES, C::THREADS, &bps)
-                    : kernel_setup<kf::prefill_fwd_kernel<D, false>>(C::SMEM_BYTES, C::THREADS, &bps);
+    const bool split = pl.pf_plain < pl.pf_units;
+    if (causal && split) return KF_ERR_INVALID_ARG;    // the planner never splits causal units
+    int rc = causal  ? kernel_setup<kf::prefill_fwd_kernel<D, true, false>>(C::SMEM_BYTES, C::THREADS, &bps)
+             : split ? kernel_setup<kf::prefill_fwd_kernel<D, false, true>>(C::SMEM_BYTES, C::THREADS, &bps)
+                     : kernel_setup<kf::prefill_fwd_kernel<D, false, false>>(C::SMEM_BYTES, C::THREADS, &bps);
     if (rc != KF_OK) return rc;
     // A TMA box may not exceed the tensor: short sequences load S rows and the
     // kernel keeps the remaining tile rows zero.
@@ -387,8 +390,6 @@ int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, 
     if ((rc = make_map(&mq, Q, D, S_q, static_cast<long long>(B) * H_q, q_box, C::SWB)) != KF_OK) return rc;
     if ((rc = make_map(&mk, K, D, S_kv, static_cast<long long>(B) * H_kv, kv_box, C::SWB)) != KF_OK) return rc;
     if ((rc = make_map(&mv, V, D, S_kv, static_cast<long long>(B) * H_kv, kv_box, C::SWB)) != KF_OK) return rc;
-    CUtensorMap mp;
-    std::memset(&mp, 0, sizeof(mp));
     if (C::TMA_STORE && out_type == kf::KF_OUT_F32) {
         if ((rc = make_map_f32(&mo, O, D, S_q, static_cast<long long>(B) * H_q, q_box)) != KF_OK) return rc;
     } else if (C::TMA_STORE) {
@@ -410,7 +411,9 @@ int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, 
     p.G = H_q / H_kv;
     p.scale = 1.0f / std::sqrt(static_cast<float>(D));
     p.scale_log2 = p.scale * 1.4426950408889634f;
-    p.unnormalized = unnorm;
+    // KF_PREFILL_TICKET_MERGE=1: split units merge by ticket only (no owner wait).
+    const char* tm = std::getenv("KF_PREFILL_TICKET_MERGE");
+    p.flags = (unnorm ? kf::KF_PF_UNNORMALIZED : 0) | (tm && std::atoi(tm) ? kf::KF_PF_TICKET_MERGE : 0);
     p.out_type = out_type;
     p.timeout_ns = g_timeout_ns.load();
     p.q_box = q_box;
@@ -423,14 +426,8 @@ int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, 
     p.n_plain = pl.pf_plain;
     p.split_k = pl.pf_k;
     p.per = pl.pf_per;
-    const bool split = pl.pf_plain < pl.pf_units;
     p.counters = split ? static_cast<unsigned*>(ws) : nullptr;
     p.part = split ? reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kCounterBytes) : nullptr;
-    if (split && C::TMA_STORE) {
-        // Partial O_u slots as a [rows][D] fp32 tensor, written by the chunks' TMA stores.
-        const long long slot_rows = static_cast<long long>(pl.pf_units - pl.pf_plain) * pl.pf_k * C::NQ * C::BM;
-        if ((rc = make_map_f32(&mp, p.part, D, static_cast<int>(slot_rows), 1, C::BM)) != KF_OK) return rc;
-    }
     const long long n_items = pl.ctas;          // whole units + KV chunks of split units
     if (n_items <= 0 || n_items > 0x7fffffffll) return KF_ERR_INVALID_ARG;
     p.n_items = static_cast<int>(n_items);
@@ -440,10 +437,13 @@ int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, 
     if ((rc = device_info(&di)) != KF_OK) return rc;
     const bool persistent = q_box == C::BM && kv_box == C::BC;
     const long long ctas = persistent && n_items > di->sm_count ? di->sm_count : n_items;
+    const unsigned grid = static_cast<unsigned>(ctas);
     if (causal)
-        kf::prefill_fwd_kernel<D, true><<<static_cast<unsigned>(ctas), C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, mo, mp, p);
+        kf::prefill_fwd_kernel<D, true, false><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, mo, p);
+    else if (split)
+        kf::prefill_fwd_kernel<D, false, true><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, mo, p);
     else
-        kf::prefill_fwd_kernel<D, false><<<static_cast<unsigned>(ctas), C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, mo, mp, p);
+        kf::prefill_fwd_kernel<D, false, false><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, mo, p);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KF_OK : cuda_fail(e);
 }

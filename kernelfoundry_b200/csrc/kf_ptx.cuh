@@ -177,6 +177,13 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* ptr) {
     return v;
 }
 
+// Acquire load at GPU scope: a counter other CTAs of this GPU advance.
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* ptr) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+    return v;
+}
+
 // atomicAdd with acquire-release semantics at GPU scope (orders this thread's
 // earlier accesses, and what a CTA barrier ordered before them, with the add).
 __device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* ptr, unsigned v) {

@@ -77,23 +77,33 @@ struct PrefillCfg {
     static_assert(TMEM_USED <= 512, "TMEM over budget");
 };
 
+// How long the owner chunk of a split unit waits for the other chunks' partials before
+// it falls back to the ticket merge.  The chunks of a split unit run in the same last
+// wave, so they normally finish within a few KV steps of each other.
+constexpr uint64_t kOwnerWaitNs = 50000;
+
+constexpr int KF_PF_UNNORMALIZED = 1;
+constexpr int KF_PF_TICKET_MERGE = 2;
+
 struct PrefillParams {
-    void* O;            // [B,H_q,S_q,D] of out_type (fp32 when unnormalized)
+    void* O;           // [B,H_q,S_q,D] of out_type (fp32 when unnormalized)
     float* Mi;   // nullable
     float* Li;   // nullable
     int H_q, H_kv, S_q, S_kv, G;
     int B_H;            // B * H_q
     float scale_log2;   // (1/sqrt(D)) * log2(e)
     float scale;        // 1/sqrt(D)
-    int unnormalized;   // 1: write O_u = sum exp(s - Mi) v (partial form), Mi/Li required
+    int flags;          // KF_PF_UNNORMALIZED: write O_u = sum exp(s - Mi) v (partial form), Mi/Li
+                        // required; KF_PF_TICKET_MERGE: split units skip the owner wait
     int out_type;       // KF_OUT_F32 / KF_OUT_F16 / KF_OUT_BF16
     int q_box;          // rows per Q TMA box: min(BM, S_q)
     int kv_box;         // rows per K/V TMA box: min(BC, S_kv)
     // Work list (1-D grid).  Unit u = (b, h_q, 256-row block) with the block index
     // fastest.  Units [0, n_plain) take one CTA over all keys; each of the units
     // [n_plain, n_units) -- the partial last wave -- is split over split_k CTAs,
-    // each taking `per` KV tiles, which write softmax partials to `part` and the
-    // last to finish (ticket in `counters`) merges them into O.
+    // each taking `per` KV tiles: chunk 0 waits on the unit's counter in `counters`
+    // until the other chunks have written softmax partials to `part` and merges them
+    // with its own O (or, past a short wait, the last chunk to take a ticket merges).
     int n_qblk;         // query blocks of unit_tiles * 128 rows per (b, h_q)
     int unit_tiles;     // query tiles per unit: NQ, or 1 when two-tile units would leave most SMs idle
     int kv_off;         // S_kv - S_q (>= 0); causal kernels: query i sees keys j <= i + kv_off
@@ -126,18 +136,18 @@ struct PrefillItem {
     bool split;
 };
 
-template <int D, bool CAUSAL>
+template <int D, bool CAUSAL, bool SPLIT>
 __device__ __forceinline__ PrefillItem prefill_item(const PrefillParams& p, int item) {
     using C = PrefillCfg<D>;
     PrefillItem it;
     it.chunk = 0;
-    if (item < p.n_plain) {
+    if (!SPLIT || item < p.n_plain) {
         it.unit = item;
     } else {
         it.unit = p.n_plain + (item - p.n_plain) / p.split_k;
         it.chunk = (item - p.n_plain) % p.split_k;
     }
-    it.split = it.unit >= p.n_plain;
+    it.split = SPLIT && it.unit >= p.n_plain;
     // Causal: heaviest query blocks (most visible keys) first, (b, h) fastest, so the
     // long units start first; otherwise the query block is fastest.
     it.qblk = CAUSAL ? p.n_qblk - 1 - it.unit / p.B_H : it.unit % p.n_qblk;
@@ -162,11 +172,38 @@ __device__ __forceinline__ PrefillItem prefill_item(const PrefillParams& p, int 
 // the slot's size, each staged as 128-B swizzled spans (32 fp32 or 64 fp16/bf16
 // columns, the map's box and swizzle) and TMA-stored; rows past the tensor are
 // dropped.  Called by the tile's 128 softmax threads; named barrier `bar` orders the
-// passes.  With `complete`, thread row 0 waits until the stores are written, else
-// until read.
+// passes; thread row 0 waits until the last pass's stores have read the slot.
+// With don.n > 0 each output element is sc * O + sum_d don.w[d] * (donor d's value):
+// the owner chunk of a split unit adds the other chunks' partial rows (fp32, global
+// memory, float4 q of this row at don.col[d] + q * don.stride) to its own O from TMEM.
+struct DonorRows {
+    int n = 0;
+    int stride = 0;
+    const float4* col[3] = {nullptr, nullptr, nullptr};
+    float w[3] = {0.f, 0.f, 0.f};
+};
+
 template <int D, int BM, int SLOT_BYTES>
 __device__ __forceinline__ void stage_store_tile(uint8_t* slot, uint32_t tO, int row, int bar, float sc, int out,
-                                                 const CUtensorMap* map, int c1, int c2, bool complete) {
+                                                 const CUtensorMap* map, int c1, int c2,
+                                                 const DonorRows& don = DonorRows{}) {
+    // o[0..31] = sc * O[cols c0 .. c0+31] (+ the donors' rows), in place.
+    auto add_donors = [&](uint32_t (&o)[32], int c0) {
+#pragma unroll
+        for (int d = 0; d < 3; ++d) {
+            if (d >= don.n) break;
+            const float4* src = don.col[d] + static_cast<size_t>(c0 / 4) * don.stride;
+            const float wd = don.w[d];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const float4 v = __ldcg(src + static_cast<size_t>(q) * don.stride);
+                o[4 * q] = __float_as_uint(__uint_as_float(o[4 * q]) + wd * v.x);
+                o[4 * q + 1] = __float_as_uint(__uint_as_float(o[4 * q + 1]) + wd * v.y);
+                o[4 * q + 2] = __float_as_uint(__uint_as_float(o[4 * q + 2]) + wd * v.z);
+                o[4 * q + 3] = __float_as_uint(__uint_as_float(o[4 * q + 3]) + wd * v.w);
+            }
+        }
+    };
     constexpr int SPAN = BM * 128;
     constexpr int SPP = SLOT_BYTES / SPAN;                // spans per pass
     static_assert(SPP >= 1, "staging slot");
@@ -185,10 +222,13 @@ __device__ __forceinline__ void stage_store_tile(uint8_t* slot, uint32_t tO, int
                 tmem_ld32(tO + sp * 32, o);
                 tmem_wait_ld();
 #pragma unroll
+                for (int k2 = 0; k2 < 32; ++k2) o[k2] = __float_as_uint(__uint_as_float(o[k2]) * sc);
+                add_donors(o, sp * 32);
+#pragma unroll
                 for (int q = 0; q < 8; ++q)
                     *reinterpret_cast<float4*>(rowp + ((q ^ (row & 7)) << 4)) =
-                        make_float4(__uint_as_float(o[4 * q]) * sc, __uint_as_float(o[4 * q + 1]) * sc,
-                                    __uint_as_float(o[4 * q + 2]) * sc, __uint_as_float(o[4 * q + 3]) * sc);
+                        make_float4(__uint_as_float(o[4 * q]), __uint_as_float(o[4 * q + 1]),
+                                    __uint_as_float(o[4 * q + 2]), __uint_as_float(o[4 * q + 3]));
             } else {
 #pragma unroll
                 for (int hh = 0; hh < 2; ++hh) {              // 32 columns -> 4 chunks of 16 B
@@ -196,12 +236,15 @@ __device__ __forceinline__ void stage_store_tile(uint8_t* slot, uint32_t tO, int
                     tmem_ld32(tO + sp * 64 + hh * 32, o);
                     tmem_wait_ld();
 #pragma unroll
+                    for (int k2 = 0; k2 < 32; ++k2) o[k2] = __float_as_uint(__uint_as_float(o[k2]) * sc);
+                    add_donors(o, sp * 64 + hh * 32);
+#pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         uint4 w;
-                        w.x = pack_out2(__uint_as_float(o[8 * q]) * sc, __uint_as_float(o[8 * q + 1]) * sc, out);
-                        w.y = pack_out2(__uint_as_float(o[8 * q + 2]) * sc, __uint_as_float(o[8 * q + 3]) * sc, out);
-                        w.z = pack_out2(__uint_as_float(o[8 * q + 4]) * sc, __uint_as_float(o[8 * q + 5]) * sc, out);
-                        w.w = pack_out2(__uint_as_float(o[8 * q + 6]) * sc, __uint_as_float(o[8 * q + 7]) * sc, out);
+                        w.x = pack_out2(__uint_as_float(o[8 * q]), __uint_as_float(o[8 * q + 1]), out);
+                        w.y = pack_out2(__uint_as_float(o[8 * q + 2]), __uint_as_float(o[8 * q + 3]), out);
+                        w.z = pack_out2(__uint_as_float(o[8 * q + 4]), __uint_as_float(o[8 * q + 5]), out);
+                        w.w = pack_out2(__uint_as_float(o[8 * q + 6]), __uint_as_float(o[8 * q + 7]), out);
                         const int cq = hh * 4 + q;
                         *reinterpret_cast<uint4*>(rowp + ((cq ^ (row & 7)) << 4)) = w;
                     }
@@ -213,7 +256,7 @@ __device__ __forceinline__ void stage_store_tile(uint8_t* slot, uint32_t tO, int
         if (row == 0) {
             for (int k = 0; k < k_end; ++k) tma_store_3d(map, slot + k * SPAN, (ps * SPP + k) * cols, c1, c2);
             bulk_commit_group();
-            if (complete && ps + 1 == n_pass) bulk_wait_group0(); else bulk_wait_group_read0();
+            bulk_wait_group_read0();
         }
         if (ps + 1 < n_pass) named_bar_sync(bar, 128);    // slot read: next pass may write it
     }
@@ -226,12 +269,14 @@ __device__ __forceinline__ void stage_store_tile(uint8_t* slot, uint32_t tO, int
 // stages O through the ring slot of the item's last K (tile 0) or V (tile 1) tile,
 // which the producer refills only after that epilogue's stores have read it.
 // CAUSAL: bottom-right causal mask (PrefillParams::kv_off); a separate instantiation
-// so the unmasked kernel carries none of its registers.
-template <int D, bool CAUSAL>
+// so the unmasked kernel carries none of its registers.  SPLIT: the work list has split
+// units (a partial last wave, never causal); likewise its own instantiation, so plans
+// without split units run a kernel without the split epilogue.
+template <int D, bool CAUSAL, bool SPLIT>
 __global__ void __launch_bounds__(PrefillCfg<D>::THREADS, 1)
 prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
-                   const __grid_constant__ CUtensorMap tmP, const PrefillParams p) {
+                   const PrefillParams p) {
     using C = PrefillCfg<D>;
     constexpr int BM = C::BM, BC = C::BC, NQ = C::NQ, SWB = C::SWB, SWE = C::SWE, NSPAN = C::NSPAN;
     constexpr int NSLOT = C::NSLOT;
@@ -255,7 +300,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     uint64_t* mma_done = q_empty + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    volatile int* ticket_last = abort_flag + 1;
+    volatile int* ticket_last = abort_flag + 1;     // one flag per tile
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -282,7 +327,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         mbar_init(q_empty, 1);
         mbar_init(mma_done, 1);
         *abort_flag = 0;
-        *ticket_last = 0;
+        for (int t = 0; t < NQ; ++t) ticket_last[t] = 0;
         fence_mbar_init();
     }
     if (p.q_box < BM || p.kv_box < BC) {
@@ -301,7 +346,9 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
+    // The TMEM base is read from shared memory inside each role (after its setmaxnreg),
+    // not held in a register across the register reallocation.
+    auto tmem_base = [&]() { return *reinterpret_cast<volatile uint32_t*>(tmem_slot); };
 
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
@@ -322,7 +369,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             for (int rnd = 0; rnd * static_cast<int>(gridDim.x) < p.n_items && ok; ++rnd) {
                 const int item = prefill_item_index(rnd);
                 if (item >= p.n_items) continue;
-                const PrefillItem it = prefill_item<D, CAUSAL>(p, item);
+                const PrefillItem it = prefill_item<D, CAUSAL, SPLIT>(p, item);
                 const int bh_q = it.b * p.H_q + it.h;
                 const int bh_kv = it.b * p.H_kv + it.h_kv;
                 // Q of this item once the previous item's QK MMAs stopped reading Q.
@@ -395,6 +442,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         // ------------------------------------------------------------ MMA issuer
         if constexpr (C::REBALANCE) setmaxnreg_dec<C::REG_CTRL>();
         if (lane == 0) {
+            const uint32_t tmem = tmem_base();
             constexpr uint32_t idesc_qk = umma_idesc_f16_f32(BM, BC, false, false);
             constexpr uint32_t idesc_pv = umma_idesc_f16_f32(BM, D, false, true);
             // Descriptors as (low, high) words: the high word is a constant and every
@@ -414,7 +462,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             for (int rnd = 0; rnd * static_cast<int>(gridDim.x) < p.n_items && ok; ++rnd) {
                 const int item = prefill_item_index(rnd);
                 if (item >= p.n_items) continue;
-                const PrefillItem it = prefill_item<D, CAUSAL>(p, item);
+                const PrefillItem it = prefill_item<D, CAUSAL, SPLIT>(p, item);
                 const int n_kv = it.n_kv, nq_active = it.nq_active;
 #pragma unroll
                 for (int t = 0; t < NQ; ++t) {
@@ -511,7 +559,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         const int t = (warp - 4) >> 2;
         const int wq = warp & 3;                 // TMEM sub-partition of this warp
         const int row = wq * 32 + lane;          // query row within the tile
-        const uint32_t tl = tmem + (static_cast<uint32_t>(wq * 32) << 16);
+        const uint32_t tl = tmem_base() + (static_cast<uint32_t>(wq * 32) << 16);
         const uint32_t tS = tl + t * BC;
         const uint32_t tO = tl + NQ * BC + t * D;
         const float c = p.scale_log2;
@@ -521,15 +569,16 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         for (int rnd = 0; rnd * static_cast<int>(gridDim.x) < p.n_items && ok; ++rnd) {
             const int item = prefill_item_index(rnd);
             if (item >= p.n_items) continue;
-            const PrefillItem it = prefill_item<D, CAUSAL>(p, item);
-            const int n_kv = it.n_kv, nq_active = it.nq_active, q_row0 = it.q_row0, kt0 = it.kt0;
-            const int b = it.b, h = it.h, unit = it.unit, chunk = it.chunk;
-            const bool split = it.split;
-            const int pos0 = pos;
-            pos += 2 * n_kv;
-            if (t >= nq_active) continue;
-            // Causal: keys of tile j visible to this row are those below diag - j*BC.
-            const int diag = CAUSAL ? q_row0 + t * BM + row + p.kv_off - kt0 * BC + 1 : 0;
+            int n_kv, kt0, diag;
+            {
+                const PrefillItem it = prefill_item<D, CAUSAL, SPLIT>(p, item);
+                n_kv = it.n_kv;
+                kt0 = it.kt0;
+                pos += 2 * n_kv;
+                if (t >= it.nq_active) continue;
+                // Causal: keys of tile j visible to this row are those below diag - j*BC.
+                diag = CAUSAL ? it.q_row0 + t * BM + row + p.kv_off - kt0 * BC + 1 : 0;
+            }
             float m_ref = -CUDART_INF_F, m_true = -CUDART_INF_F, l = 0.f;
             for (int j = 0; j < n_kv; ++j) {
                 ok = mbar_wait_bounded(&s_full[t], (sst + j) & 1, abort_flag, p.timeout_ns);
@@ -652,144 +701,210 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 if (!ok) atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_MMA);
             }
             ++o_cnt;
+            // Rebase to the true row max: O_t * f and l * f are relative to m_true.
+            const float f = ex2_approx((m_ref - m_true) * c);
+            const float l_true = l * f;
+            // The item's fields for the epilogue, recomputed from its index (an opaque
+            // copy, so the compiler does not keep them in registers across the KV loop).
+            int item_e;
+            asm volatile("mov.b32 %0, %1;" : "=r"(item_e) : "r"(item));
+            const PrefillItem ie = prefill_item<D, CAUSAL, SPLIT>(p, item_e);
+            const int q_row0 = ie.q_row0, b = ie.b, h = ie.h, unit = ie.unit, chunk = ie.chunk;
+            const bool split = ie.split;
             // Staging slot of this tile: the ring slot of the item's last K (tile 0) or
             // last V (tile 1); every MMA reading it completed before o_full[t] fired.
-            uint8_t* stage = sKV + ((pos0 + 2 * n_kv - 2 + t) % NSLOT) * C::KV_BYTES;
+            uint8_t* stage = sKV + ((pos - 2 + t) % NSLOT) * C::KV_BYTES;
             const int qrow = q_row0 + t * BM + row;
             const bool store = qrow < p.S_q;
             const size_t orow = ((static_cast<size_t>(b) * p.H_q + h) * p.S_q + (store ? qrow : 0)) * D;   // element index
             const size_t mi = (static_cast<size_t>(b) * p.H_q + h) * p.S_q + (store ? qrow : 0);
             if (split) {
-                // KV chunk of a split unit: write this tile's partial (O_u, m, l) relative
-                // to its own max; the last chunk to finish merges the unit's partials.
-                // Layout: O_u [split unit][chunk][ROWS][D], then (m, l) [..][ROWS][2].
+                // KV chunk of a split unit.  Tile t of the unit is owned by chunk t: the
+                // other chunks write their partial (O_u, m, l) of tile t, relative to their
+                // own max, and add 1 to the tile's counter; the owner waits (within a short
+                // limit) for the k-1 partials and merges them with its own O straight from
+                // TMEM.  If that wait runs out (chunks not running at the same time), the
+                // owner writes its partial too and adds 1: the add that makes the count k
+                // (owner or last donor) merges the tile from the k partials.
+                // Partials: O_u as float4 columns [split unit][chunk][D/4][ROWS] (lane =
+                // row, so every warp access is 512 contiguous bytes), then (m, l) as float2
+                // [split unit][chunk][ROWS].
                 const int su = unit - p.n_plain;
                 constexpr int ROWS = NQ * BM;
-                const size_t n_slots = static_cast<size_t>(p.n_units - p.n_plain) * p.split_k * ROWS;
-                const size_t unit0 = static_cast<size_t>(su) * p.split_k * ROWS;           // chunk 0, row 0
-                const size_t tile0 = unit0 + static_cast<size_t>(chunk) * ROWS + t * BM;   // this tile's rows
+                const int k = p.split_k;
+                const size_t n_slots = static_cast<size_t>(p.n_units - p.n_plain) * k * ROWS;
+                float4* part4 = reinterpret_cast<float4*>(p.part);
                 float2* part_ml = reinterpret_cast<float2*>(p.part + n_slots * D);
+                const int r_u = t * BM + row;                             // row within the unit
+                auto o_part = [&](int ch, int q) -> float4* {             // float4 q of row r_u, chunk ch
+                    return part4 + ((static_cast<size_t>(su) * k + ch) * (D / 4) + q) * ROWS + r_u;
+                };
+                auto ml_part = [&](int ch) -> float2* {
+                    return part_ml + (static_cast<size_t>(su) * k + ch) * ROWS + r_u;
+                };
+                unsigned* counter = &p.counters[su * NQ + t];
+                volatile int* flag = ticket_last + t;
+                const bool owner = chunk == t;
                 if constexpr (C::TMA_STORE) ok = named_bar_and(2 + t, 128, ok);
-                if (ok) {
-                    tc_fence_after();
-                    const float f = ex2_approx((m_ref - m_true) * c);
-                    if constexpr (C::TMA_STORE) {
-                        // The stores must be complete (not only read) before the ticket.
-                        stage_store_tile<D, BM, C::KV_BYTES>(stage, tO, row, 2 + t, f, KF_OUT_F32, &tmP,
-                                                            static_cast<int>(tile0), 0, true);
-                        if (row == 0) {
-                            fence_proxy_async_global();
-                            mbar_arrive(&stage_free[t]);
+                bool owner_merge = false;
+                if (owner && !(p.flags & KF_PF_TICKET_MERGE)) {
+                    if (row == 0) {
+                        const unsigned want = static_cast<unsigned>(k - 1);
+                        const uint64_t lim = p.timeout_ns < kOwnerWaitNs ? p.timeout_ns : kOwnerWaitNs;
+                        const uint64_t t0 = global_timer_ns();
+                        int got = 0;
+                        for (unsigned spins = 0; !*abort_flag; ++spins) {
+                            if (ld_acquire_gpu(counter) >= want) { got = 1; break; }
+                            if ((spins & 15u) == 15u && global_timer_ns() - t0 > lim) break;
+                            __nanosleep(32);
                         }
-                    } else {
-                        float* prow = p.part + (tile0 + row) * D;
+                        if (got) *counter = 0u;          // every donor has added: zero for the next call
+                        *flag = got;
+                    }
+                    named_bar_sync(2 + t, 128);
+                    owner_merge = *flag != 0;
+                    named_bar_sync(2 + t, 128);          // flag read before it is reused
+                }
+                if (owner_merge) {
+                    __threadfence();
+                    if (ok) {
+                        tc_fence_after();
+                        DonorRows don;
+                        don.n = k - 1;
+                        float md[3], ld[3];
+                        float M = m_true;
+#pragma unroll
+                        for (int d = 0; d < 3; ++d) {
+                            const int ch = d < t ? d : d + 1;            // the chunks other than t
+                            const float2 ml = d < don.n ? __ldcg(ml_part(ch)) : make_float2(-CUDART_INF_F, 0.f);
+                            md[d] = ml.x;
+                            ld[d] = ml.y;
+                            M = fmaxf(M, ml.x);
+                        }
+                        const float w_own = ex2_approx((m_true - M) * c);
+                        float L = w_own * l_true;
+#pragma unroll
+                        for (int d = 0; d < 3; ++d) {
+                            don.w[d] = d < don.n ? ex2_approx((md[d] - M) * c) : 0.f;
+                            L += don.w[d] * ld[d];
+                        }
+                        const float osc = (p.flags & KF_PF_UNNORMALIZED) ? 1.0f : 1.0f / L;
+#pragma unroll
+                        for (int d = 0; d < 3; ++d) {
+                            don.w[d] *= osc;
+                            don.col[d] = o_part(d < t ? d : d + 1, 0);
+                        }
+                        don.stride = ROWS;
+                        if constexpr (C::TMA_STORE) {
+                            stage_store_tile<D, BM, C::KV_BYTES>(stage, tO, row, 2 + t, f * w_own * osc, p.out_type,
+                                                                &tmO, q_row0 + t * BM, b * p.H_q + h, don);
+                            if (row == 0) mbar_arrive(&stage_free[t]);
+                        } else {
+                            const float so = f * w_own * osc;
+#pragma unroll
+                            for (int dc = 0; dc < D / OCH; ++dc) {
+                                uint32_t o[OCH];
+                                tmem_ld_chunk<OCH>(tO + dc * OCH, o);
+                                tmem_wait_ld();
+#pragma unroll
+                                for (int kk = 0; kk < OCH; kk += 4) {
+                                    float4 v = make_float4(__uint_as_float(o[kk]) * so, __uint_as_float(o[kk + 1]) * so,
+                                                           __uint_as_float(o[kk + 2]) * so, __uint_as_float(o[kk + 3]) * so);
+#pragma unroll
+                                    for (int d = 0; d < 3; ++d) {
+                                        if (d < don.n) {
+                                            const float4 u = __ldcg(don.col[d] + static_cast<size_t>((dc * OCH + kk) / 4) * ROWS);
+                                            v.x += don.w[d] * u.x; v.y += don.w[d] * u.y;
+                                            v.z += don.w[d] * u.z; v.w += don.w[d] * u.w;
+                                        }
+                                    }
+                                    if (store) store_out4(p.O, orow + dc * OCH + kk, v, p.out_type);
+                                }
+                            }
+                        }
+                        if (store) {
+                            if (p.Mi) p.Mi[mi] = M * p.scale;
+                            if (p.Li) p.Li[mi] = L;
+                        }
+                    }
+                } else {
+                    // Donor (or an owner past its wait): this tile's partial, then a ticket.
+                    if (ok) {
+                        tc_fence_after();
 #pragma unroll
                         for (int dc = 0; dc < D / OCH; ++dc) {
                             uint32_t o[OCH];
                             tmem_ld_chunk<OCH>(tO + dc * OCH, o);
                             tmem_wait_ld();
 #pragma unroll
-                            for (int k = 0; k < OCH; k += 4)
-                                *reinterpret_cast<float4*>(prow + dc * OCH + k) =
-                                    make_float4(__uint_as_float(o[k]) * f, __uint_as_float(o[k + 1]) * f,
-                                                __uint_as_float(o[k + 2]) * f, __uint_as_float(o[k + 3]) * f);
+                            for (int kk = 0; kk < OCH; kk += 4)
+                                *o_part(chunk, (dc * OCH + kk) / 4) =
+                                    make_float4(__uint_as_float(o[kk]) * f, __uint_as_float(o[kk + 1]) * f,
+                                                __uint_as_float(o[kk + 2]) * f, __uint_as_float(o[kk + 3]) * f);
+                        }
+                        *ml_part(chunk) = make_float2(m_true, l_true);
+                        if constexpr (C::TMA_STORE) {
+                            if (row == 0) mbar_arrive(&stage_free[t]);    // the staging slot was not used
                         }
                     }
-                    part_ml[tile0 + row] = make_float2(m_true, l * f);
-                }
-                __threadfence();
-                named_bar_sync(1, 128 * nq_active);     // every active softmax thread, ok or not
-                if (threadIdx.x == 128 && !*abort_flag) {
-                    const unsigned tk = atomicAdd(&p.counters[su], 1u);
-                    *ticket_last = (tk == static_cast<unsigned>(p.split_k - 1)) ? 1 : 0;
-                }
-                named_bar_sync(1, 128 * nq_active);
-                    if (*ticket_last) {
+                    __threadfence();
+                    named_bar_sync(2 + t, 128);          // every thread of the tile, ok or not
+                    if (row == 0) {
+                        int last = 0;
+                        if (!*abort_flag) last = atomicAdd(counter, 1u) == static_cast<unsigned>(k - 1);
+                        *flag = last;
+                    }
+                    named_bar_sync(2 + t, 128);
+                    const bool last = *flag != 0;
+                    named_bar_sync(2 + t, 128);          // flag read before it is reused
+                    if (last) {
+                        // Merge the tile from the k partials: lane = row, every access coalesced.
                         __threadfence();
-                        // Merge, one warp per 32 consecutive rows: lane i computes the weights of
-                        // row i from the chunks' (m, l); then for each row the lanes read the
-                        // chunks' O_u rows (coalesced, several rows in flight) and write O.
-                        const int wi = warp - 4;                      // 0 .. 4*nq_active-1
-                        const int r = wi * 32 + lane;                 // row of the unit this lane weighs
                         float2 ml[4];
+                        float M = -CUDART_INF_F;
 #pragma unroll
-                        for (int c2 = 0; c2 < 4; ++c2)
-                            ml[c2] = c2 < p.split_k ? __ldcg(part_ml + unit0 + static_cast<size_t>(c2) * ROWS + r)
-                                                    : make_float2(-CUDART_INF_F, 0.f);
-                        const float M = fmaxf(fmaxf(ml[0].x, ml[1].x), fmaxf(ml[2].x, ml[3].x));
+                        for (int ch = 0; ch < 4; ++ch) {
+                            ml[ch] = ch < k ? __ldcg(ml_part(ch)) : make_float2(-CUDART_INF_F, 0.f);
+                            M = fmaxf(M, ml[ch].x);
+                        }
                         float w[4], L = 0.f;
 #pragma unroll
-                        for (int c2 = 0; c2 < 4; ++c2) {
-                            w[c2] = c2 < p.split_k ? ex2_approx((ml[c2].x - M) * c) : 0.f;
-                            L += w[c2] * ml[c2].y;
+                        for (int ch = 0; ch < 4; ++ch) {
+                            w[ch] = ch < k ? ex2_approx((ml[ch].x - M) * c) : 0.f;
+                            L += w[ch] * ml[ch].y;
                         }
-                        const float osc = p.unnormalized ? 1.0f : 1.0f / L;
+                        const float osc = (p.flags & KF_PF_UNNORMALIZED) ? 1.0f : 1.0f / L;
 #pragma unroll
-                        for (int c2 = 0; c2 < 4; ++c2) w[c2] *= osc;
-                        const int qrow_l = q_row0 + r;
-                        if (qrow_l < p.S_q) {
-                            const size_t mi_l = (static_cast<size_t>(b) * p.H_q + h) * p.S_q + qrow_l;
-                            if (p.Mi) p.Mi[mi_l] = M * p.scale;
-                            if (p.Li) p.Li[mi_l] = L;
-                        }
-                        const float* part_o = p.part + unit0 * D;
-                        const size_t obase = ((static_cast<size_t>(b) * p.H_q + h) * p.S_q) * D;       // element index
-                        constexpr int RU = D <= 128 ? 8 : 4;          // rows in flight per lane
+                        for (int ch = 0; ch < 4; ++ch) w[ch] *= osc;
 #pragma unroll 1
-                        for (int j0 = 0; j0 < 32; j0 += RU) {
-                            float4 acc[RU][(D / 4 + 31) / 32];
+                        for (int q = 0; q < D / 4; ++q) {
+                            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-                            for (int u = 0; u < RU; ++u) {
-                                const int rr = wi * 32 + j0 + u;
-                                float wj[4];
-#pragma unroll
-                                for (int c2 = 0; c2 < 4; ++c2) wj[c2] = __shfl_sync(0xffffffffu, w[c2], j0 + u);
-#pragma unroll
-                                for (int ci = 0; ci < (D / 4 + 31) / 32; ++ci) {
-                                    const int cidx = lane + ci * 32;
-                                    acc[u][ci] = make_float4(0.f, 0.f, 0.f, 0.f);
-                                    if (cidx < D / 4) {
-#pragma unroll
-                                        for (int c2 = 0; c2 < 4; ++c2) {
-                                            if (c2 < p.split_k) {
-                                                const float4 v = __ldcg(reinterpret_cast<const float4*>(
-                                                    part_o + (static_cast<size_t>(c2) * ROWS + rr) * D) + cidx);
-                                                acc[u][ci].x += wj[c2] * v.x; acc[u][ci].y += wj[c2] * v.y;
-                                                acc[u][ci].z += wj[c2] * v.z; acc[u][ci].w += wj[c2] * v.w;
-                                            }
-                                        }
-                                    }
+                            for (int ch = 0; ch < 4; ++ch) {
+                                if (ch < k) {
+                                    const float4 u = __ldcg(o_part(ch, q));
+                                    v.x += w[ch] * u.x; v.y += w[ch] * u.y; v.z += w[ch] * u.z; v.w += w[ch] * u.w;
                                 }
                             }
-#pragma unroll
-                            for (int u = 0; u < RU; ++u) {
-                                const int qr = q_row0 + wi * 32 + j0 + u;
-                                if (qr < p.S_q) {
-#pragma unroll
-                                    for (int ci = 0; ci < (D / 4 + 31) / 32; ++ci) {
-                                        const int cidx = lane + ci * 32;
-                                        if (cidx < D / 4)
-                                            store_out4(p.O, obase + static_cast<size_t>(qr) * D + cidx * 4, acc[u][ci],
-                                                       p.out_type);
-                                    }
-                                }
-                            }
+                            if (store) store_out4(p.O, orow + q * 4, v, p.out_type);
                         }
-                        if (threadIdx.x == 128) p.counters[su] = 0u;
+                        if (store) {
+                            if (p.Mi) p.Mi[mi] = M * p.scale;
+                            if (p.Li) p.Li[mi] = L;
+                        }
+                        if (row == 0) *counter = 0u;
                     }
-                named_bar_sync(1, 128 * nq_active);     // ticket_last read by all before the next item
+                }
             } else {
                 // Every thread of the tile reaches this barrier, ok or not, so the staged
                 // epilogue below (which synchronizes the tile's threads) runs for all or none.
                 if constexpr (C::TMA_STORE) ok = named_bar_and(2 + t, 128, ok);
                 if (ok) {
                     tc_fence_after();
-                    const float f = ex2_approx((m_ref - m_true) * c);   // rebase to the true max
-                    const float l_true = l * f;
-                    const float osc = p.unnormalized ? f : 1.0f / l;
+                    const float osc = (p.flags & KF_PF_UNNORMALIZED) ? f : 1.0f / l;
                     if constexpr (C::TMA_STORE) {
                         stage_store_tile<D, BM, C::KV_BYTES>(stage, tO, row, 2 + t, osc, p.out_type, &tmO,
-                                                            q_row0 + t * BM, b * p.H_q + h, false);
+                                                            q_row0 + t * BM, b * p.H_q + h);
                         if (row == 0) mbar_arrive(&stage_free[t]);
                     } else {
 #pragma unroll
@@ -819,7 +934,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, C::TMEM_COLS);
+        tmem_dealloc(tmem_base(), C::TMEM_COLS);
     }
 }
 

@@ -100,15 +100,25 @@ def test_ragged_shapes(cuda, shape):
     assert np.abs(Li / rLi - 1).max() < 1e-3
 
 
-@pytest.mark.parametrize("shape", [(1, 32, 8, 4096, 4096, 128), (3, 8, 2, 700, 1500, 64), (1, 4, 1, 129, 4097, 256)],
-                         ids=lambda s: "B{}_Hq{}_Hkv{}_Sq{}_Skv{}_D{}".format(*s))
-def test_tail_split_matches_unsplit(cuda, shape):
-    """A partial last wave split along KV (needs a workspace) gives the unsplit result."""
+_SPLIT_SHAPES = [(1, 32, 8, 4096, 4096, 128), (3, 8, 2, 700, 1500, 64), (1, 4, 1, 129, 4097, 256),
+                 (1, 8, 2, 600, 2048, 128)]     # the last: 4 chunks per split unit (3 donors)
+
+
+@pytest.mark.parametrize("merge", ["owner", "ticket"])
+@pytest.mark.parametrize("shape", _SPLIT_SHAPES, ids=lambda s: "B{}_Hq{}_Hkv{}_Sq{}_Skv{}_D{}".format(*s))
+def test_tail_split_matches_unsplit(cuda, shape, merge, monkeypatch):
+    """A partial last wave split along KV (needs a workspace) gives the unsplit result.
+
+    ``owner``: chunk 0 waits for the other chunks' partials and merges them with its
+    own O from TMEM (the default); ``ticket``: the owner's wait is zero, so every chunk
+    writes a partial and the last to take a ticket merges (the fallback path)."""
     import torch
 
     from kernelfoundry_b200 import flash_attn_fwd, plan
     from kernelfoundry_b200.attention import new_workspace, workspace_bytes
 
+    if merge == "ticket":
+        monkeypatch.setenv("KF_PREFILL_TICKET_MERGE", "1")
     need = workspace_bytes(*shape)
     assert need > 0, "expected a split plan for this shape"
     assert plan(*shape)["ctas"] > plan(*shape, workspace_bytes=0)["ctas"]
@@ -125,6 +135,29 @@ def test_tail_split_matches_unsplit(cuda, shape):
     assert np.abs(split_mi - rMi).max() < 1e-3
     assert np.abs(split_li / rLi - 1).max() < 1e-3
     assert int(ws[:65536].view(torch.int32).abs().sum()) == 0     # tickets reset
+    half = flash_attn_fwd(q, k, v, workspace=ws, out_dtype=torch.float16).float().cpu().numpy()
+    assert_close(half, O, "split fp16 out", max_abs=4e-3)
+    assert int(ws[:65536].view(torch.int32).abs().sum()) == 0
+
+
+@pytest.mark.parametrize("merge", ["owner", "ticket"])
+def test_partial_form_split(cuda, merge, monkeypatch):
+    """Unnormalized partials (O_u, m, l) of a split plan: O_u / l is the softmax output."""
+    from kernelfoundry_b200 import flash_attn_partial
+    from kernelfoundry_b200.attention import new_workspace, workspace_bytes
+
+    if merge == "ticket":
+        monkeypatch.setenv("KF_PREFILL_TICKET_MERGE", "1")
+    shape = (1, 8, 2, 600, 2048, 128)
+    need = workspace_bytes(*shape)
+    assert need > 0
+    Q, K, V = normal_qkv(*shape, seed=91)
+    ws = new_workspace(need, cuda)
+    O_u, m, l = (t.cpu().numpy() for t in flash_attn_partial(*(to_dev(x, cuda) for x in (Q, K, V)), workspace=ws))
+    O, rMi, rLi = oracle64(Q, K, V)
+    assert_close(O_u / l[..., None], O, "split partial O_u/l")
+    assert np.abs(m - rMi).max() < 1e-3
+    assert np.abs(l / rLi - 1).max() < 1e-3
 
 
 def test_partial_form_prefill(cuda):
