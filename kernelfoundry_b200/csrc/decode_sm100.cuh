@@ -65,6 +65,12 @@ struct DecodeCfg {
     static constexpr int BIG0 = STAGES_BYTES > RED0 ? STAGES_BYTES : RED0;
     static constexpr int BIG = BIG0 > CMB_BYTES ? BIG0 : CMB_BYTES;
     static constexpr int SMEM_BYTES = 1024 + BIG + Q_BYTES + 256;   // + barriers/flags
+    // Cluster merge (CL kernels): the CTA's partial (O_u [QROWS][D], then (m, l) [QROWS])
+    // at the end of the big region, above the CTA reduction's scratch.
+    static constexpr int RED_FLOATS = NW * QROWS * (D + 3) + 2 * QROWS;
+    static constexpr int CL_BYTES = QROWS * D * 4 + QROWS * 8;
+    static constexpr int CL_OFF = BIG - CL_BYTES;
+    static constexpr int MAX_CLUSTER = 16;
     static constexpr int THREADS = 32 * (NCW + 1);
     static_assert(NW * 16 == TK, "each consumer warp owns 16 rows of a stage");
     static_assert(NSTAGE % NG == 0, "ring depth a multiple of the consumer groups");
@@ -236,7 +242,11 @@ __device__ __forceinline__ void xch_unit(const DecodeParams& p, size_t cidx, int
 // without the split-merge code so that code does not shape the streaming loop.
 // XW > 0: the unit's result is exchanged with XW - 1 peer GPUs and merged (xch_unit)
 // instead of written.
-template <int D, int MT, bool PAGED = false, bool SPLIT = true, bool DEEP = false, int XW = 0>
+// CL: the n_split CTAs of a unit form one thread-block cluster (grid x = cluster x =
+// n_split): each keeps its partial in its own shared memory and, after a cluster
+// barrier, merges 1/n_split of the unit's output from all the partials through
+// distributed shared memory (no workspace, no ticket, no global round trip).
+template <int D, int MT, bool PAGED = false, bool SPLIT = true, bool DEEP = false, int XW = 0, bool CL = false>
 __global__ void __launch_bounds__(DecodeCfg<D, MT, DEEP>::THREADS)
 decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                   const DecodeParams p) {
@@ -266,10 +276,6 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
     // Global row index (over B*H_q*S_q) of this CTA's local row 0.
     const size_t row_base = (static_cast<size_t>(b) * p.H_q + static_cast<size_t>(hk) * p.G) * p.S_q + r0;
     const int kv_lo = split * p.chunk;
-    int S_b = p.S_kv;                          // keys of this sequence
-    if constexpr (PAGED) S_b = min(max(__ldg(p.seq_lens + b), 0), p.max_blocks * p.block_size);
-    const int kv_hi = min(S_b, kv_lo + p.chunk);
-    const int n_st = kv_hi > kv_lo ? (kv_hi - kv_lo + TK - 1) / TK : 0;   // 0: an empty split
     const float c = p.scale_log2;
 
     if (tid == 0) {
@@ -289,6 +295,14 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
             reinterpret_cast<uint4*>(sBig)[i] = make_uint4(0, 0, 0, 0);
         fence_proxy_async_smem();
     }
+    // Set-up above touches shared memory only; global memory (this launch's inputs, the
+    // workspace counters) is read after the previous launch on the stream has completed.
+    grid_dep_wait();
+    grid_dep_launch_dependents();
+    int S_b = p.S_kv;                          // keys of this sequence
+    if constexpr (PAGED) S_b = min(max(__ldg(p.seq_lens + b), 0), p.max_blocks * p.block_size);
+    const int kv_hi = min(S_b, kv_lo + p.chunk);
+    const int n_st = kv_hi > kv_lo ? (kv_hi - kv_lo + TK - 1) / TK : 0;   // 0: an empty split
     __syncthreads();
     if (warp < NCW) {
         // Consumers stage Q (padded, rows >= nrows zero) while the producer's first
@@ -515,7 +529,65 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
     __syncthreads();   // every stage consumed: the ring memory becomes reduction scratch
     const bool aborted = *abort_flag != 0;
     if (aborted && (!SPLIT || p.n_split == 1)) return;
-    if (aborted) {
+    // Cluster merge: the partial of this CTA at CL_OFF, then every CTA of the cluster
+    // merges the output items i with i % n_split == its rank.  Every CTA reaches both
+    // cluster barriers (an aborted one publishes an empty partial: m = -inf, l = 0).
+    float* cl_o = reinterpret_cast<float*>(sBig + C::CL_OFF);    // [QROWS][D]
+    float2* cl_ml = reinterpret_cast<float2*>(cl_o + QROWS * D);  // [QROWS]
+    auto cluster_merge = [&]() {
+        cluster_sync_all();
+        const uint32_t n = static_cast<uint32_t>(p.n_split);
+        const uint32_t rank = cluster_ctarank();
+        const uint32_t o_base = smem_u32(cl_o), ml_base = smem_u32(cl_ml);
+        const int items = nrows * (D / 4);
+        for (int it = static_cast<int>(rank) + static_cast<int>(n) * tid; it < items;
+             it += static_cast<int>(n) * C::THREADS) {
+            const int row = it / (D / 4), d = (it % (D / 4)) * 4;
+            // Every peer's (m, l) and O slice are requested before any is used, so the
+            // distributed-shared-memory round trips overlap.
+            float2 ml[C::MAX_CLUSTER];
+            float4 v[C::MAX_CLUSTER];
+#pragma unroll
+            for (int r = 0; r < C::MAX_CLUSTER; ++r) {
+                if (r < static_cast<int>(n)) {
+                    ml[r] = ld_dsmem_f2(dsmem_map(ml_base + row * 8, r));
+                    v[r] = ld_dsmem_f4(dsmem_map(o_base + (row * D + d) * 4, r));
+                } else {
+                    ml[r] = make_float2(-CUDART_INF_F, 0.f);
+                    v[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+            float M = -CUDART_INF_F;
+#pragma unroll
+            for (int r = 0; r < C::MAX_CLUSTER; ++r) M = fmaxf(M, ml[r].x);
+            const float Mu = (M == -CUDART_INF_F) ? 0.f : M;
+            float L = 0.f;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int r = 0; r < C::MAX_CLUSTER; ++r) {
+                const float wt = ex2_approx((ml[r].x - Mu) * c);
+                L += wt * ml[r].y;
+                acc.x += wt * v[r].x; acc.y += wt * v[r].y; acc.z += wt * v[r].z; acc.w += wt * v[r].w;
+            }
+            const float sc = p.unnormalized ? 1.f : (L > 0.f ? 1.f / L : 0.f);
+            store_out4(p.O, (row_base + row) * D + d, make_float4(acc.x * sc, acc.y * sc, acc.z * sc, acc.w * sc),
+                       p.out_type);
+            if (d == 0) {
+                if (p.Mi) p.Mi[row_base + row] = M * p.scale;
+                if (p.Li) p.Li[row_base + row] = L;
+            }
+        }
+        cluster_sync_all();   // the other CTAs have read this CTA's partial
+    };
+    if constexpr (CL) {
+        static_assert(SPLIT && !DEEP && XW == 0 && !PAGED, "cluster merge: plain split kernels only");
+        static_assert(C::RED_FLOATS * 4 <= C::CL_OFF, "cluster partial overlaps the reduction scratch");
+        if (aborted) {
+            if (tid < QROWS) cl_ml[tid] = make_float2(-CUDART_INF_F, 0.f);
+            cluster_merge();
+            return;
+        }
+    } else if (aborted) {
         // A wait expired (the device error word says so).  The split still takes its
         // ticket, and the last one resets the unit's counter without merging, so the
         // counters are zero again after the call and the next call's merge is right.
@@ -657,6 +729,23 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
             if (p.Li) p.Li[row_base + tid] = Lrow[tid];
         }
         }
+        return;
+    }
+
+    if constexpr (CL) {
+        for (int idx = tid; idx < nrows * (D / 4); idx += C::THREADS) {
+            const int row = idx / (D / 4), d = (idx % (D / 4)) * 4;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int w = 0; w < NW; ++w) {
+                const float wt = wts[w * QROWS + row];
+                const float4 v = *reinterpret_cast<const float4*>(red_o + (w * QROWS + row) * D + d);
+                acc.x += wt * v.x; acc.y += wt * v.y; acc.z += wt * v.z; acc.w += wt * v.w;
+            }
+            *reinterpret_cast<float4*>(cl_o + row * D + d) = acc;
+        }
+        if (tid < nrows) cl_ml[tid] = make_float2(Mrow[tid], Lrow[tid]);
+        cluster_merge();
         return;
     }
 

@@ -183,6 +183,7 @@ struct Plan {
     int n_rg = 1;        // decode: row groups per (b, h_kv)
     int n_split = 1;     // decode: KV splits
     bool deep = false;   // decode: the deep-ring kernel (one CTA per SM, all CTAs resident)
+    bool cluster = false;  // decode: a unit's splits form a thread-block cluster (merge in DSMEM)
     int chunk = 0;       // decode: KV rows per split
     size_t ws_bytes = 0; // workspace the plan uses
     long long ctas = 0;
@@ -211,6 +212,57 @@ int decode_blocks_per_sm(int* bps) {
     return kernel_setup<kf::decode_fwd_kernel<D, MT>>(C::SMEM_BYTES, C::THREADS, bps);
 }
 
+// Largest cluster of split CTAs (16 or 8, 0 when none fits) the cluster-merge decode
+// kernel of (D, MT) can be launched with on this device; cached per device.
+template <int D, int MT>
+int decode_cluster_max(int* out) {
+    using C = kf::DecodeCfg<D, MT>;
+    constexpr auto kern = kf::decode_fwd_kernel<D, MT, false, true, false, 0, true>;
+    struct Slot { std::atomic<int> v{-1}; };
+    static Slot slots[kMaxDevices];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e);
+    int v = slots[dev].v.load(std::memory_order_acquire);
+    if (v < 0) {
+        if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES)) != cudaSuccess ||
+            (e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1)) != cudaSuccess)
+            return cuda_fail(e);
+        v = 0;
+        for (int cs = C::MAX_CLUSTER; cs >= 8; cs /= 2) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(static_cast<unsigned>(cs));
+            cfg.blockDim = dim3(C::THREADS);
+            cfg.dynamicSmemBytes = C::SMEM_BYTES;
+            cudaLaunchAttribute a[1];
+            a[0].id = cudaLaunchAttributeClusterDimension;
+            a[0].val.clusterDim.x = static_cast<unsigned>(cs);
+            a[0].val.clusterDim.y = 1;
+            a[0].val.clusterDim.z = 1;
+            cfg.attrs = a;
+            cfg.numAttrs = 1;
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0) {
+                v = cs;
+                break;
+            }
+            cudaGetLastError();    // a size the device cannot place is not an error of the call
+        }
+        slots[dev].v.store(v, std::memory_order_release);
+    }
+    *out = v;
+    return KF_OK;
+}
+
+int decode_cl_max(int D, int mt, int* out) {
+    switch (D) {
+        case 16: return mt == 2 ? decode_cluster_max<16, 2>(out) : decode_cluster_max<16, 1>(out);
+        case 64: return mt == 2 ? decode_cluster_max<64, 2>(out) : decode_cluster_max<64, 1>(out);
+        case 128: return mt == 2 ? decode_cluster_max<128, 2>(out) : decode_cluster_max<128, 1>(out);
+        default: return decode_cluster_max<256, 1>(out);
+    }
+}
+
 int decode_bps(int D, int mt, int* bps) {
     switch (D) {
         case 16: return mt == 2 ? decode_blocks_per_sm<16, 2>(bps) : decode_blocks_per_sm<16, 1>(bps);
@@ -222,7 +274,7 @@ int decode_bps(int D, int mt, int* bps) {
 
 int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_bytes, int sm_count,
               int blocks_per_sm, Plan* pl, bool causal = false, double cta_rate = 1.0, bool allow_deep = true,
-              bool deep_only = false) {
+              bool deep_only = false, int cl_max = 0) {
     const int G = H_q / H_kv;
     // Causal with several query rows takes the prefill kernel (the decode kernel has
     // no per-row mask); with one row the mask keeps every key, so decode is exact.
@@ -291,11 +343,14 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
     // 19.8 us), so its splits must buy more streaming time.
     const double kBwMerge = 200.0;   // GB/s == bytes/ns -> x1e-3 per us
     const double kT0 = 2.0, kMerge0 = pl->mt == 1 ? 3.0 : 10.0;
+    // Cluster merge (splits of a unit in one thread-block cluster, partials in shared
+    // memory, two cluster barriers and distributed-shared-memory loads): no workspace.
+    const double kMergeCl = 1.0;
     const double stage_bytes = 2.0 * TK * D * 2;
     const double total_bytes = static_cast<double>(units) * total_stages * stage_bytes;
     const int nrows = R < 16 * pl->mt ? R : 16 * pl->mt;
     int best_s = 1;
-    bool best_deep = false;
+    bool best_deep = false, best_cl = false;
     double best_cost = 1e300;
     const int max_s = total_stages < kf::DecodeCfg<128, 1>::MAX_SPLIT ? total_stages : kf::DecodeCfg<128, 1>::MAX_SPLIT;
     const long long rows = static_cast<long long>(B) * H_q * S_q;
@@ -318,18 +373,20 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
             const int nst = (total_stages + s - 1) / s;
             const int s_eff = (total_stages + nst - 1) / nst;
             if (s_eff != s) continue;
-            if (s > 1 && (units > kCounterSlots || split_ws_bytes(rows, s, D) > ws_bytes)) break;
+            const bool cl = !deep && s >= 2 && s <= cl_max;
+            if (s > 1 && !cl && (units > kCounterSlots || split_ws_bytes(rows, s, D) > ws_bytes)) break;
             const double ctas = static_cast<double>(units) * s;
             if (deep && ctas > cap_d) break;
             const double bw = ctas * kBwCta < kBwTotal ? ctas * kBwCta : kBwTotal;
             const double t_stream = total_bytes / (bw * 1e3) + kT0 * std::ceil(ctas / cap_d);
             const double t_cta = kT0 + nst * stage_bytes / (kBwCta * 1e3);
-            const double t_merge = s > 1 ? kMerge0 + s * nrows * D * 4.0 / (kBwMerge * 1e3) : 0.0;
+            const double t_merge = s == 1 ? 0.0 : cl ? kMergeCl : kMerge0 + s * nrows * D * 4.0 / (kBwMerge * 1e3);
             const double cost = (t_stream > t_cta ? t_stream : t_cta) + t_merge + t_fixed;
             if (cost < best_cost * 0.999) {
                 best_cost = cost;
                 best_s = s;
                 best_deep = deep != 0;
+                best_cl = cl;
             }
         }
     }
@@ -337,16 +394,22 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
     // count when the workspace allows it.
     if (const char* ov = std::getenv("KF_DECODE_NSPLIT")) {
         int want = std::atoi(ov);
-        if (want >= 1 && want <= max_s && (want == 1 || (units <= kCounterSlots &&
-                                                        split_ws_bytes(rows, want, D) <= ws_bytes)))
-            best_s = (total_stages + ((total_stages + want - 1) / want) - 1) / ((total_stages + want - 1) / want);
+        const int s_ov = want >= 1 ? (total_stages + ((total_stages + want - 1) / want) - 1) /
+                                         ((total_stages + want - 1) / want) : 0;
+        const bool cl_ov = !best_deep && s_ov >= 2 && s_ov <= cl_max;
+        if (want >= 1 && want <= max_s && (want == 1 || cl_ov || (units <= kCounterSlots &&
+                                                                 split_ws_bytes(rows, want, D) <= ws_bytes))) {
+            best_s = s_ov;
+            best_cl = cl_ov;
+        }
     }
     const int nst = (total_stages + best_s - 1) / best_s;
     if (best_deep && static_cast<long long>(units) * best_s > sm_count) best_deep = false;   // after an override
     pl->deep = best_deep;
+    pl->cluster = best_cl && !best_deep && best_s >= 2;
     pl->n_split = best_s;
     pl->chunk = nst * TK;
-    pl->ws_bytes = best_s > 1 ? split_ws_bytes(rows, best_s, D) : 0;
+    pl->ws_bytes = (best_s > 1 && !pl->cluster) ? split_ws_bytes(rows, best_s, D) : 0;
     pl->ctas = units * best_s;
     return KF_OK;
 }
@@ -357,19 +420,64 @@ int plan_for_call(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_
     int rc = device_info(&di);
     if (rc != KF_OK) return rc;
     const int G = H_q / H_kv;
-    int bps = 1;
+    int bps = 1, cl_max = 0;
     if (use_decode(G, S_q, D) && !(causal && S_q > 1)) {
         const int R = G * S_q;
         const int mt = R <= 16 ? 1 : decode_max_mt(D);
         rc = decode_bps(D, mt, &bps);
         if (rc != KF_OK) return rc;
+        // KF_DECODE_CLUSTER=0: no cluster-merge plans (the workspace ticket merge only).
+        const char* ce = std::getenv("KF_DECODE_CLUSTER");
+        if (cta_rate >= 1.0 && !deep_only && !(ce && std::atoi(ce) == 0) && (rc = decode_cl_max(D, mt, &cl_max)) != KF_OK)
+            return rc;
     }
     return make_plan(B, H_q, H_kv, S_q, S_kv, D, ws_bytes, di->sm_count, bps, pl, causal, cta_rate,
-                     cta_rate >= 1.0,    // paged K/V (cta_rate < 1) has no deep-ring kernel
-                     deep_only);
+                     cta_rate >= 1.0,    // paged K/V (cta_rate < 1) has no deep-ring or cluster kernel
+                     deep_only, cl_max);
 }
 
 // ------------------------------------------------------------------ launches
+// Kernel launch with programmatic stream serialization (programmatic dependent launch)
+// unless KF_PDL=0: the kernel's CTAs may be dispatched while the previous kernel on the
+// stream drains.  Every kernel launched this way runs griddepcontrol.wait before its first
+// global-memory (and TMEM) access, so results do not depend on it.
+// cluster_x > 0: thread-block clusters of (cluster_x, 1, 1) CTAs.  pdl = false: no
+// early dispatch (the deep-ring decode, one CTA per SM, measured slower with it:
+// B=16 42.6 against 41.6 us, KV=131072 83.9 against 80.7 us).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_ex(void (*kern)(KArgs...), dim3 grid, int threads, int smem_bytes, cudaStream_t s,
+                      unsigned cluster_x, bool pdl, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(static_cast<unsigned>(threads));
+    cfg.dynamicSmemBytes = static_cast<size_t>(smem_bytes);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    unsigned n = 0;
+    const char* e = std::getenv("KF_PDL");
+    if (pdl && !(e && std::atoi(e) == 0)) {
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n].val.programmaticStreamSerializationAllowed = 1;
+        ++n;
+    }
+    if (cluster_x > 0) {
+        attr[n].id = cudaLaunchAttributeClusterDimension;
+        attr[n].val.clusterDim.x = cluster_x;
+        attr[n].val.clusterDim.y = 1;
+        attr[n].val.clusterDim.z = 1;
+        ++n;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = n;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, int threads, int smem_bytes, cudaStream_t s,
+                       Args... args) {
+    return launch_ex(kern, grid, threads, smem_bytes, s, 0u, true, args...);
+}
+
 template <int D>
 int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, void* O, float* Mi, float* Li,
                    int unnorm, int B, int H_q, int H_kv, int S_q, int S_kv, void* ws, cudaStream_t s,
@@ -437,14 +545,14 @@ int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, 
     if ((rc = device_info(&di)) != KF_OK) return rc;
     const bool persistent = q_box == C::BM && kv_box == C::BC;
     const long long ctas = persistent && n_items > di->sm_count ? di->sm_count : n_items;
-    const unsigned grid = static_cast<unsigned>(ctas);
+    const dim3 grid(static_cast<unsigned>(ctas));
+    cudaError_t e;
     if (causal)
-        kf::prefill_fwd_kernel<D, true, false><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, mo, p);
+        e = launch_pdl(kf::prefill_fwd_kernel<D, true, false>, grid, C::THREADS, C::SMEM_BYTES, s, mq, mk, mv, mo, p);
     else if (split)
-        kf::prefill_fwd_kernel<D, false, true><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, mo, p);
+        e = launch_pdl(kf::prefill_fwd_kernel<D, false, true>, grid, C::THREADS, C::SMEM_BYTES, s, mq, mk, mv, mo, p);
     else
-        kf::prefill_fwd_kernel<D, false, false><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mq, mk, mv, mo, p);
-    cudaError_t e = cudaGetLastError();
+        e = launch_pdl(kf::prefill_fwd_kernel<D, false, false>, grid, C::THREADS, C::SMEM_BYTES, s, mq, mk, mv, mo, p);
     return e == cudaSuccess ? KF_OK : cuda_fail(e);
 }
 
@@ -540,41 +648,55 @@ int launch_decode_t(const Plan& pl, const void* Q, const void* K, const void* V,
         p.xcalls = reinterpret_cast<unsigned*>(p.xown + kf::peer_unit_calls_off(xa->part_stride, xa->world));
     }
     dim3 grid(pl.n_split, H_kv * pl.n_rg, B);
+    cudaError_t e;
     if constexpr (XW > 0) {
+        // The exchange waits on peer GPUs: a plain launch (no early dispatch next to the
+        // previous kernel).
         if (split)
             kf::decode_fwd_kernel<D, MT, false, true, true, XW><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
         else
             kf::decode_fwd_kernel<D, MT, false, false, true, XW><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
+        e = cudaGetLastError();
     } else if constexpr (DEEP) {
-        if (split)
-            kf::decode_fwd_kernel<D, MT, false, true, true><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
-        else
-            kf::decode_fwd_kernel<D, MT, false, false, true><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
-    } else if (pg && split) {
-        kf::decode_fwd_kernel<D, MT, true, true><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
+        e = split ? launch_ex(kf::decode_fwd_kernel<D, MT, false, true, true>, grid, C::THREADS, C::SMEM_BYTES, s, 0u,
+                              false, mk, mv, p)
+                  : launch_ex(kf::decode_fwd_kernel<D, MT, false, false, true>, grid, C::THREADS, C::SMEM_BYTES, s, 0u,
+                              false, mk, mv, p);
     } else if (pg) {
-        kf::decode_fwd_kernel<D, MT, true, false><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
-    } else if (split) {
-        kf::decode_fwd_kernel<D, MT, false, true><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
+        e = split ? launch_pdl(kf::decode_fwd_kernel<D, MT, true, true>, grid, C::THREADS, C::SMEM_BYTES, s, mk, mv, p)
+                  : launch_pdl(kf::decode_fwd_kernel<D, MT, true, false>, grid, C::THREADS, C::SMEM_BYTES, s, mk, mv, p);
+    } else if (split && pl.cluster) {
+        int cl_max = 0;
+        if ((rc = decode_cluster_max<D, MT>(&cl_max)) != KF_OK) return rc;
+        if (pl.n_split > cl_max) return KF_ERR_INVALID_ARG;      // the planner keeps within it
+        e = launch_ex(kf::decode_fwd_kernel<D, MT, false, true, false, 0, true>, grid, C::THREADS, C::SMEM_BYTES, s,
+                      static_cast<unsigned>(pl.n_split), true, mk, mv, p);
     } else {
-        kf::decode_fwd_kernel<D, MT, false, false><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
+        e = split ? launch_pdl(kf::decode_fwd_kernel<D, MT, false, true>, grid, C::THREADS, C::SMEM_BYTES, s, mk, mv, p)
+                  : launch_pdl(kf::decode_fwd_kernel<D, MT, false, false>, grid, C::THREADS, C::SMEM_BYTES, s, mk, mv,
+                               p);
     }
-    cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KF_OK : cuda_fail(e);
 }
 
 int launch_decode(const Plan& pl, int D, const void* Q, const void* K, const void* V, void* O, float* Mi,
                   float* Li, int unnorm, int B, int H_q, int H_kv, int S_q, int S_kv, void* ws, cudaStream_t s,
                   const Paged* pg = nullptr, int out_type = kf::KF_OUT_F32) {
-#define KF_DEC(DV, MTV)                                                                                        \
-    return pl.deep ? launch_decode_t<DV, MTV, true>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s, \
-                                                    pg, out_type)                                                  \
-                   : launch_decode_t<DV, MTV, false>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s,\
-                                                     pg, out_type)
+    // The deep-ring kernel exists for 16-row tiles only (the planner offers it for mt == 1).
+#define KF_DEC(DV, MTV)                                                                                          \
+    if constexpr (MTV == 1) {                                                                                     \
+        if (pl.deep)                                                                                              \
+            return launch_decode_t<DV, MTV, true>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s, \
+                                                  pg, out_type);                                                  \
+    } else {                                                                                                      \
+        if (pl.deep) return KF_ERR_INVALID_ARG;                                                                   \
+    }                                                                                                             \
+    return launch_decode_t<DV, MTV, false>(pl, Q, K, V, O, Mi, Li, unnorm, B, H_q, H_kv, S_q, S_kv, ws, s, pg,    \
+                                           out_type)
     switch (D) {
-        case 16: if (pl.mt == 2) KF_DEC(16, 2); KF_DEC(16, 1);
-        case 64: if (pl.mt == 2) KF_DEC(64, 2); KF_DEC(64, 1);
-        case 128: if (pl.mt == 2) KF_DEC(128, 2); KF_DEC(128, 1);
+        case 16: if (pl.mt == 2) { KF_DEC(16, 2); } KF_DEC(16, 1);
+        case 64: if (pl.mt == 2) { KF_DEC(64, 2); } KF_DEC(64, 1);
+        case 128: if (pl.mt == 2) { KF_DEC(128, 2); } KF_DEC(128, 1);
         default: KF_DEC(256, 1);
     }
 #undef KF_DEC

@@ -177,6 +177,46 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* ptr) {
     return v;
 }
 
+// Programmatic dependent launch.  grid_dep_wait: block until the grids this launch
+// depends on have completed and their writes are visible (a no-op for a launch without
+// a programmatic dependency); every global-memory access of a kernel launched with one
+// comes after it.  grid_dep_launch_dependents: let the next launch on the stream start
+// dispatching its CTAs (they wait in their own grid_dep_wait).
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Thread-block clusters.  cluster_sync_all: every thread of every CTA of the cluster
+// arrives (release) and waits (acquire), so shared-memory writes before it are visible to
+// the cluster's other CTAs after it, and no CTA passes it while another is still before
+// it.  dsmem_map: the address of the same shared-memory offset in CTA `rank` of the
+// cluster; ld_dsmem_*: loads through such an address.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t dsmem_map(uint32_t smem_addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
+    float4 v;
+    asm("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ float2 ld_dsmem_f2(uint32_t addr) {
+    float2 v;
+    asm("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
+    return v;
+}
+
 // Acquire load at GPU scope: a counter other CTAs of this GPU advance.
 __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* ptr) {
     unsigned v;

@@ -339,6 +339,11 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             reinterpret_cast<uint4*>(sQ)[i] = make_uint4(0, 0, 0, 0);
         fence_proxy_async_smem();
     }
+    // Set-up above touches shared memory only.  Global memory, and TMEM (which a CTA of
+    // the previous launch on this SM may still hold), come after the previous launch on
+    // the stream has completed.
+    grid_dep_wait();
+    grid_dep_launch_dependents();
     if (warp == 1) {
         tmem_alloc(tmem_slot, C::TMEM_COLS);
         tmem_relinquish();

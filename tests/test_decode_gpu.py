@@ -68,13 +68,15 @@ def test_decode_shapes(cuda, shape):
     assert np.abs(Li / rLi - 1).max() < 1e-3
 
 
-def test_workspace_optional_and_reusable(cuda):
-    """No workspace (single split) and a shared workspace reused across shapes give correct results."""
+def test_workspace_optional_and_reusable(cuda, monkeypatch):
+    """Split merges through the workspace (the cluster merge off): no workspace (single
+    split) and a shared workspace reused across shapes give correct results."""
     import torch
 
     from kernelfoundry_b200 import flash_attn_fwd, plan
     from kernelfoundry_b200.attention import new_workspace, workspace_bytes
 
+    monkeypatch.setenv("KF_DECODE_CLUSTER", "0")
     assert plan(1, 32, 8, 1, 4096, 128, workspace_bytes=0)["n_split"] == 1
     ws = new_workspace(max(workspace_bytes(1, 32, 8, 1, 8192, 128), workspace_bytes(4, 32, 8, 1, 3000, 128)), cuda)
     for shape in [(1, 32, 8, 1, 8192, 128), (4, 32, 8, 1, 3000, 128), (1, 32, 8, 1, 8192, 128), (2, 8, 2, 1, 999, 128)]:
@@ -157,15 +159,19 @@ def test_long_decode_forward_single_process(cuda):
     assert_close(out.cpu().numpy(), oracle64(Q, K, V)[0], "long decode, one rank")
 
 
+@pytest.mark.parametrize("cluster", ["0", "1"])
 @pytest.mark.parametrize("nsplit", ["8", "16", "32"])
-def test_split_merge_paths(cuda, nsplit, monkeypatch):
-    """Forced split counts (KF_DECODE_NSPLIT): the last CTA's ticket merge of 8, 16 and 32
-    partials gives the oracle's result."""
+def test_split_merge_paths(cuda, nsplit, cluster, monkeypatch):
+    """Forced split counts (KF_DECODE_NSPLIT): the merge of 8, 16 and 32 partials -- the
+    cluster merge in distributed shared memory (up to 16 splits) or the last CTA's ticket
+    merge through the workspace (KF_DECODE_CLUSTER=0, and 32 splits) -- gives the oracle's
+    result."""
     import torch
 
     from kernelfoundry_b200 import flash_attn_fwd, plan
 
     monkeypatch.setenv("KF_DECODE_NSPLIT", nsplit)
+    monkeypatch.setenv("KF_DECODE_CLUSTER", cluster)
     Q, K, V = normal_qkv(2, 32, 8, 1, 40000, 128, seed=int(nsplit))
     assert plan(2, 32, 8, 1, 40000, 128)["n_split"] == int(nsplit)
     got, Mi, Li = (t.cpu().numpy() for t in flash_attn_fwd(*(to_dev(x, cuda) for x in (Q, K, V)), return_lse=True))
@@ -201,3 +207,46 @@ def test_decode_ring_variants(cuda, shape, n_split, deep, monkeypatch):
     assert_close(got, O, f"deep={deep} n_split={n_split} {shape}")
     assert np.abs(Mi - rMi).max() < 1e-3
     assert np.abs(Li / rLi - 1).max() < 1e-3
+
+
+CLUSTER_SHAPES = [
+    (1, 32, 8, 1, 4096, 128),    # the C3 B=1 shape
+    (3, 32, 8, 1, 1000, 128),    # ragged last stage
+    (1, 32, 1, 1, 4096, 128),    # MQA: 32 packed rows (two 16-row MMA tiles per CTA)
+    (2, 8, 2, 1, 1100, 64),      # D=64
+    (2, 16, 8, 2, 1090, 16),     # D=16, S_q=2
+    (1, 8, 8, 1, 3000, 256),     # D=256
+]
+
+
+# Every shape has more 64-key stages than the largest forced split count (the override
+# applies only up to one stage per split).
+@pytest.mark.parametrize("n_split", [2, 5, 16])
+@pytest.mark.parametrize("shape", CLUSTER_SHAPES, ids=lambda s: "B{}_Hq{}_Hkv{}_Sq{}_Skv{}_D{}".format(*s))
+def test_cluster_merge(cuda, shape, n_split, monkeypatch):
+    """Split decode merged inside a thread-block cluster (the unit's splits read each other's
+    partials from distributed shared memory; no workspace): O, Mi, Li against the fp64
+    oracle, the fp16 output, and the unnormalized partial form."""
+    import torch
+
+    from kernelfoundry_b200 import flash_attn_fwd, flash_attn_partial, plan
+    from kernelfoundry_b200.attention import workspace_bytes
+
+    monkeypatch.setenv("KF_DECODE_NSPLIT", str(n_split))
+    monkeypatch.setenv("KF_DECODE_DEEP", "0")
+    stages = (shape[4] + 63) // 64
+    per = (stages + n_split - 1) // n_split
+    want = (stages + per - 1) // per
+    assert plan(*shape)["n_split"] == want
+    assert workspace_bytes(*shape) == 0          # the cluster plan needs no workspace
+    Q, K, V = normal_qkv(*shape, seed=sum(shape) + 7 * n_split)
+    q, k, v = (to_dev(x, cuda) for x in (Q, K, V))
+    got, Mi, Li = (t.cpu().numpy() for t in flash_attn_fwd(q, k, v, return_lse=True))
+    O, rMi, rLi = oracle64(Q, K, V)
+    assert_close(got, O, f"cluster n_split={n_split} {shape}")
+    assert np.abs(Mi - rMi).max() < 1e-3
+    assert np.abs(Li / rLi - 1).max() < 1e-3
+    half = flash_attn_fwd(q, k, v, out_dtype=torch.float16).float().cpu().numpy()
+    assert_close(half, O, "cluster fp16 out", max_abs=4e-3)
+    O_u, m, l = (t.cpu().numpy() for t in flash_attn_partial(q, k, v))
+    assert_close(O_u / l[..., None], O, "cluster partial O_u/l")
