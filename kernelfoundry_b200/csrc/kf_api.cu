@@ -289,6 +289,10 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
         const long long u1 = static_cast<long long>((S_q + 127) / 128) * H_q * B;
         const int n_kv_tiles = (S_kv + bc - 1) / bc;
         pl->pf_tiles = (nq == 2 && !causal && u1 > u2 && u1 <= sm_count && n_kv_tiles < 8) ? 1 : nq;
+        if (const char* ov = std::getenv("KF_PREFILL_UNIT_TILES")) {       // tuning sweeps
+            const int t = std::atoi(ov);
+            if (t == 1 || t == nq) pl->pf_tiles = t;
+        }
         const int rows_per_cta = pl->pf_tiles * 128;
         pl->pf_qblk = (S_q + rows_per_cta - 1) / rows_per_cta;
         const long long units = static_cast<long long>(pl->pf_qblk) * H_q * B;
@@ -305,7 +309,12 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
         // Each chunk keeps >= 4 KV tiles: writing and merging the partials costs about
         // as much as 3 KV steps (measured: S = 512, 4 tiles in 2 chunks, took 21 us
         // against 16 us unsplit).
-        k = k > n_kv / 4 ? n_kv / 4 : k;
+        int min_chunk = 4;
+        if (const char* ov = std::getenv("KF_PREFILL_MIN_CHUNK_TILES")) {  // tuning sweeps
+            const int m = std::atoi(ov);
+            if (m >= 1) min_chunk = m;
+        }
+        k = k > n_kv / min_chunk ? n_kv / min_chunk : k;
         if (k >= 2) {
             const int per = (n_kv + k - 1) / k;
             const int k_eff = (n_kv + per - 1) / per;
