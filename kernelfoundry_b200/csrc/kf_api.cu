@@ -191,6 +191,7 @@ struct Plan {
     // units (a partial last wave) are split over split_k CTAs of `per` KV tiles
     int pf_qblk = 1, pf_units = 0, pf_plain = 0, pf_k = 1, pf_per = 0;
     int pf_tiles = 2;    // prefill: 128-row query tiles per unit
+    bool pf_kvh = false; // prefill, one-tile units: the CTA's two tiles take the keys' two halves
 };
 
 int decode_max_mt(int D) { return D <= 128 ? 2 : 1; }
@@ -293,6 +294,11 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
             const int t = std::atoi(ov);
             if (t == 1 || t == nq) pl->pf_tiles = t;
         }
+        // One-tile units run the tile's two key halves as the CTA's two tiles (two chains in
+        // ping-pong instead of one), merged in TMEM; KF_PREFILL_KVH=0 turns it off.
+        const char* kvh = std::getenv("KF_PREFILL_KVH");
+        pl->pf_kvh = pl->pf_tiles == 1 && nq == 2 && !causal && n_kv_tiles >= 2 && n_kv_tiles % 2 == 0 &&
+                     !(kvh && std::atoi(kvh) == 0);
         const int rows_per_cta = pl->pf_tiles * 128;
         pl->pf_qblk = (S_q + rows_per_cta - 1) / rows_per_cta;
         const long long units = static_cast<long long>(pl->pf_qblk) * H_q * B;
@@ -495,7 +501,14 @@ int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, 
     int bps = 0;
     const bool split = pl.pf_plain < pl.pf_units;
     if (causal && split) return KF_ERR_INVALID_ARG;    // the planner never splits causal units
-    int rc = causal  ? kernel_setup<kf::prefill_fwd_kernel<D, true, false>>(C::SMEM_BYTES, C::THREADS, &bps)
+    const bool kvh = C::NQ == 2 && pl.pf_kvh;
+    if (kvh && (causal || split)) return KF_ERR_INVALID_ARG;
+    int rc;
+    if constexpr (C::NQ == 2) {
+        if (kvh) rc = kernel_setup<kf::prefill_fwd_kernel<D, false, false, true>>(C::SMEM_BYTES, C::THREADS, &bps);
+    }
+    if (!kvh)
+        rc = causal  ? kernel_setup<kf::prefill_fwd_kernel<D, true, false>>(C::SMEM_BYTES, C::THREADS, &bps)
              : split ? kernel_setup<kf::prefill_fwd_kernel<D, false, true>>(C::SMEM_BYTES, C::THREADS, &bps)
                      : kernel_setup<kf::prefill_fwd_kernel<D, false, false>>(C::SMEM_BYTES, C::THREADS, &bps);
     if (rc != KF_OK) return rc;
@@ -555,8 +568,14 @@ int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, 
     const bool persistent = q_box == C::BM && kv_box == C::BC;
     const long long ctas = persistent && n_items > di->sm_count ? di->sm_count : n_items;
     const dim3 grid(static_cast<unsigned>(ctas));
-    cudaError_t e;
-    if (causal)
+    cudaError_t e = cudaSuccess;
+    if constexpr (C::NQ == 2) {
+        if (kvh)
+            e = launch_pdl(kf::prefill_fwd_kernel<D, false, false, true>, grid, C::THREADS, C::SMEM_BYTES, s, mq, mk, mv,
+                           mo, p);
+    }
+    if (kvh) {
+    } else if (causal)
         e = launch_pdl(kf::prefill_fwd_kernel<D, true, false>, grid, C::THREADS, C::SMEM_BYTES, s, mq, mk, mv, mo, p);
     else if (split)
         e = launch_pdl(kf::prefill_fwd_kernel<D, false, true>, grid, C::THREADS, C::SMEM_BYTES, s, mq, mk, mv, mo, p);

@@ -130,13 +130,14 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, 
 }
 
 // One work item of the 1-D list: whole units [0, n_plain) (b, h, 256-row block),
-// then the KV chunks of the split units.
+// then the KV chunks of the split units.  KVH (one-tile units): both tiles of the CTA take
+// the unit's one query tile, tile t the keys of KV tiles [t * n_kv, (t + 1) * n_kv).
 struct PrefillItem {
     int unit, chunk, qblk, h, b, h_kv, q_row0, nq_active, kt0, n_kv;
     bool split;
 };
 
-template <int D, bool CAUSAL, bool SPLIT>
+template <int D, bool CAUSAL, bool SPLIT, bool KVH>
 __device__ __forceinline__ PrefillItem prefill_item(const PrefillParams& p, int item) {
     using C = PrefillCfg<D>;
     PrefillItem it;
@@ -164,6 +165,10 @@ __device__ __forceinline__ PrefillItem prefill_item(const PrefillParams& p, int 
         // Keys up to the unit's last (valid) query row + kv_off; the split path is off.
         const int last_row = min(it.q_row0 + C::NQ * C::BM, p.S_q) - 1;
         it.n_kv = min(n_kv_all, (last_row + p.kv_off) / C::BC + 1);
+    }
+    if constexpr (KVH) {
+        it.nq_active = 2;              // two key halves of one query tile (n_kv_all is even)
+        it.n_kv = n_kv_all / 2;        // per tile
     }
     return it;
 }
@@ -272,7 +277,7 @@ __device__ __forceinline__ void stage_store_tile(uint8_t* slot, uint32_t tO, int
 // so the unmasked kernel carries none of its registers.  SPLIT: the work list has split
 // units (a partial last wave, never causal); likewise its own instantiation, so plans
 // without split units run a kernel without the split epilogue.
-template <int D, bool CAUSAL, bool SPLIT>
+template <int D, bool CAUSAL, bool SPLIT, bool KVH = false>
 __global__ void __launch_bounds__(PrefillCfg<D>::THREADS, 1)
 prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
@@ -374,7 +379,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             for (int rnd = 0; rnd * static_cast<int>(gridDim.x) < p.n_items && ok; ++rnd) {
                 const int item = prefill_item_index(rnd);
                 if (item >= p.n_items) continue;
-                const PrefillItem it = prefill_item<D, CAUSAL, SPLIT>(p, item);
+                const PrefillItem it = prefill_item<D, CAUSAL, SPLIT, KVH>(p, item);
                 const int bh_q = it.b * p.H_q + it.h;
                 const int bh_kv = it.b * p.H_kv + it.h_kv;
                 // Q of this item once the previous item's QK MMAs stopped reading Q.
@@ -383,14 +388,14 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 }
 #pragma unroll
                 for (int t = 0; t < NQ; ++t) {
-                    if (t >= it.nq_active) break;
+                    if (t >= (KVH ? 1 : it.nq_active)) break;       // KVH: one query tile for both
                     mbar_arrive_expect_tx(&q_full[t], q_bytes);
                     for (int s = 0; s < NSPAN; ++s)
                         tma_load_3d(sQ + t * C::Q_BYTES + s * BM * SWB, &tmQ, &q_full[t], s * SWE,
                                     it.q_row0 + t * BM, bh_q);
                     ++q_cnt[t];
                 }
-                for (int i = 0; i < 2 * it.n_kv; ++i, ++pos) {
+                for (int i = 0; i < (KVH ? 4 : 2) * it.n_kv; ++i, ++pos) {
                     const int slot = pos % NSLOT;
                     const int round = pos / NSLOT;
                     if (round > 0 && !mbar_wait_bounded(&kv_empty[slot], (round - 1) & 1, abort_flag, p.timeout_ns)) {
@@ -412,8 +417,9 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     // mid-step and a V refill that of a K freed at the end of a step, so each
                     // load is issued 1.5 to 2 KV steps before its MMA needs it (TMA loads
                     // from L2 take about one step to land under full load).
-                    const bool is_v = (i & 1) != 0;
-                    const int tile = i >> 1;
+                    // KVH: per step K of the first half, K of the second half, then their V.
+                    const bool is_v = KVH ? (i & 3) >= 2 : (i & 1) != 0;
+                    const int tile = KVH ? (i >> 2) + ((i & 1) ? it.n_kv : 0) : i >> 1;
                     const CUtensorMap* map = is_v ? &tmV : &tmK;
                     uint8_t* dst = sKV + slot * C::KV_BYTES;
                     for (int s = 0; s < NSPAN; ++s)
@@ -421,12 +427,15 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     // Warm L2 with the same operand L2AHEAD tiles ahead: the CTAs of one KV
                     // head stream it in near lockstep, so without this every tile is a
                     // first touch that waits on HBM.
-                    if (C::L2AHEAD > 0 && tile + C::L2AHEAD < it.n_kv)
+                    if (C::L2AHEAD > 0 && tile + C::L2AHEAD < (KVH ? 2 : 1) * it.n_kv)
                         for (int s = 0; s < NSPAN; ++s)
                             tma_prefetch_l2_3d(map, s * SWE, (it.kt0 + tile + C::L2AHEAD) * BC, bh_kv);
                 }
                 if (!ok) break;
-                if constexpr (C::TMA_STORE) {
+                if constexpr (KVH) {
+                    // The merged tile is staged (by tile 0) in the slot of the last first-half K.
+                    pend[0] |= 1u << ((pos - 4) % NSLOT);
+                } else if constexpr (C::TMA_STORE) {
                     // The item's epilogue stages tile 0 in the slot of its last K and tile 1
                     // in the slot of its last V.
                     pend[0] |= 1u << ((pos - 2) % NSLOT);
@@ -460,6 +469,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             // loop keeps them few: ring slot/phase are counters, K and V are tested
             // together, and a completed p_full makes the p_half wait unnecessary.
             int slotK = 0, parK = 0;        // ring position of the item's K_j
+            int ring = 0;                   // KVH: ring position of the item's first load
             int q_cnt[NQ], steps[NQ];       // q_full completions, KV steps done, per tile
 #pragma unroll
             for (int t = 0; t < NQ; ++t) { q_cnt[t] = 0; steps[t] = 0; }
@@ -467,15 +477,81 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             for (int rnd = 0; rnd * static_cast<int>(gridDim.x) < p.n_items && ok; ++rnd) {
                 const int item = prefill_item_index(rnd);
                 if (item >= p.n_items) continue;
-                const PrefillItem it = prefill_item<D, CAUSAL, SPLIT>(p, item);
+                const PrefillItem it = prefill_item<D, CAUSAL, SPLIT, KVH>(p, item);
                 const int n_kv = it.n_kv, nq_active = it.nq_active;
 #pragma unroll
                 for (int t = 0; t < NQ; ++t) {
-                    if (t >= nq_active || !ok) break;
+                    if (t >= (KVH ? 1 : nq_active) || !ok) break;
                     ok = mbar_wait_bounded(&q_full[t], q_cnt[t] & 1, abort_flag, p.timeout_ns);
                     ++q_cnt[t];
                 }
                 if (!ok) { atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_TMA); break; }
+                if constexpr (KVH) {
+                    // Two key halves of one query tile: step j reads K_t(j) at ring position
+                    // ring + 4j + t and V_t(j - 1) at ring + 4(j - 1) + 2 + t; both tiles' QK use
+                    // the one Q tile.  Same issue order as below: PV_0(j-1), QK_0(j), PV_1(j-1),
+                    // QK_1(j), so each tile's MMAs overlap the other's softmax.
+                    for (int j = 0; j <= n_kv && ok; ++j) {
+                        int kpos[2], vpos[2];
+#pragma unroll
+                        for (int t = 0; t < 2; ++t) {
+                            kpos[t] = ring + 4 * j + t;
+                            vpos[t] = ring + 4 * (j - 1) + 2 + t;
+                            if (ok && j < n_kv &&
+                                !mbar_wait_bounded(&kv_full[kpos[t] % NSLOT], (kpos[t] / NSLOT) & 1, abort_flag,
+                                                   p.timeout_ns))
+                                ok = false;
+                            if (ok && j > 0 &&
+                                !mbar_wait_bounded(&kv_full[vpos[t] % NSLOT], (vpos[t] / NSLOT) & 1, abort_flag,
+                                                   p.timeout_ns))
+                                ok = false;
+                        }
+                        if (!ok) { atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_TMA); break; }
+                        tc_fence_after();
+#pragma unroll
+                        for (int t = 0; t < 2; ++t) {
+                            const uint32_t tS = tmem + t * BC;
+                            const uint32_t tO = tmem + NQ * BC + t * D;
+                            if (j > 0) {
+                                const uint32_t v_lo = kv_lo + (vpos[t] % NSLOT) * (C::KV_BYTES >> 4) +
+                                                      umma_desc_lbo(BC * SWB);
+                                const uint32_t ppar = (steps[t] + j - 1) & 1;
+#pragma unroll
+                                for (int hf = 0; hf < 2; ++hf) {
+                                    if (!mbar_wait_bounded(hf == 0 ? &p_half[t] : &p_full[t], ppar, abort_flag,
+                                                           p.timeout_ns)) {
+                                        atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_SOFTMAX); ok = false; break;
+                                    }
+                                    tc_fence_after();
+#pragma unroll
+                                    for (int kk = hf * BC / 32; kk < (hf + 1) * BC / 32; ++kk)
+                                        umma_ts(tO, tS + kk * 8,
+                                                umma_desc_join(v_lo + ((kk * 16 * SWB) >> 4), DESC_HI), idesc_pv,
+                                                (j > 1 || kk > 0) ? 1u : 0u);
+                                }
+                                if (!ok) break;
+                                if (j == n_kv) umma_commit(&o_full[t]);
+                                umma_commit(&kv_empty[vpos[t] % NSLOT]);
+                            }
+                            if (j < n_kv) {
+                                const uint32_t k_lo = kv_lo + (kpos[t] % NSLOT) * (C::KV_BYTES >> 4) + umma_desc_lbo(16);
+#pragma unroll
+                                for (int kk = 0; kk < D / 16; ++kk) {
+                                    const int span = (kk * 16) / SWE;
+                                    const int off = ((kk * 16) % SWE) * 2;
+                                    umma_ss(tS, umma_desc_join(q_lo + ((span * BM * SWB + off) >> 4), DESC_HI),
+                                            umma_desc_join(k_lo + ((span * BC * SWB + off) >> 4), DESC_HI), idesc_qk,
+                                            kk > 0 ? 1u : 0u);
+                                }
+                                umma_commit(&s_full[t]);
+                                umma_commit(&kv_empty[kpos[t] % NSLOT]);
+                            }
+                        }
+                        if (!ok) break;
+                        if (j == n_kv - 1) umma_commit(q_empty);      // Q is free once these QKs complete
+                    }
+                    ring += 4 * n_kv;
+                } else
                 for (int j = 0; j <= n_kv && ok; ++j) {
                     // V_{j-1} sits at ring position 2j - 1 of the item, just before K_j.
                     int slotV = slotK - 1, parV = parK;
@@ -576,10 +652,10 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             if (item >= p.n_items) continue;
             int n_kv, kt0, diag;
             {
-                const PrefillItem it = prefill_item<D, CAUSAL, SPLIT>(p, item);
+                const PrefillItem it = prefill_item<D, CAUSAL, SPLIT, KVH>(p, item);
                 n_kv = it.n_kv;
-                kt0 = it.kt0;
-                pos += 2 * n_kv;
+                kt0 = it.kt0 + (KVH ? t * it.n_kv : 0);     // KVH: this tile's half of the keys
+                pos += (KVH ? 4 : 2) * n_kv;
                 if (t >= it.nq_active) continue;
                 // Causal: keys of tile j visible to this row are those below diag - j*BC.
                 diag = CAUSAL ? it.q_row0 + t * BM + row + p.kv_off - kt0 * BC + 1 : 0;
@@ -713,17 +789,84 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             // copy, so the compiler does not keep them in registers across the KV loop).
             int item_e;
             asm volatile("mov.b32 %0, %1;" : "=r"(item_e) : "r"(item));
-            const PrefillItem ie = prefill_item<D, CAUSAL, SPLIT>(p, item_e);
+            const PrefillItem ie = prefill_item<D, CAUSAL, SPLIT, KVH>(p, item_e);
             const int q_row0 = ie.q_row0, b = ie.b, h = ie.h, unit = ie.unit, chunk = ie.chunk;
             const bool split = ie.split;
             // Staging slot of this tile: the ring slot of the item's last K (tile 0) or
-            // last V (tile 1); every MMA reading it completed before o_full[t] fired.
-            uint8_t* stage = sKV + ((pos - 2 + t) % NSLOT) * C::KV_BYTES;
-            const int qrow = q_row0 + t * BM + row;
+            // last V (tile 1); every MMA reading it completed before o_full[t] fired.  KVH:
+            // the slot of the last first-half K, for tile 0 (the one that stores).
+            uint8_t* stage = sKV + ((KVH ? pos - 4 : pos - 2 + t) % NSLOT) * C::KV_BYTES;
+            const int qrow = q_row0 + (KVH ? 0 : t * BM) + row;
             const bool store = qrow < p.S_q;
             const size_t orow = ((static_cast<size_t>(b) * p.H_q + h) * p.S_q + (store ? qrow : 0)) * D;   // element index
             const size_t mi = (static_cast<size_t>(b) * p.H_q + h) * p.S_q + (store ? qrow : 0);
-            if (split) {
+            if constexpr (KVH) {
+                // Key halves of one query tile: tile 1 hands its row's (m_ref, m_true, l) to
+                // tile 0 through the idle second Q buffer; tile 0 merges tile 1's O straight
+                // from TMEM (same lanes, tile 1's columns) into its staged store.  A second
+                // barrier keeps tile 1 from starting its next item (whose P.V overwrites its
+                // O) before tile 0 has read that O.
+                // Both barriers are reductions of ok over the two tiles, so the tiles leave
+                // the item loop together after an abort (neither is left at a barrier).
+                // (Addressed from sKV, which this role already holds: sQ + Q_BYTES == sKV - Q_BYTES.)
+                float4* xch = reinterpret_cast<float4*>(sKV - C::Q_BYTES);
+                if (t == 1) {
+                    xch[row] = make_float4(m_ref, m_true, l, 0.f);
+                    tc_fence_before();
+                }
+                ok = named_bar_and(4, 256, ok);
+                if (t == 0) {
+                    tc_fence_after();
+                    const float4 ob = xch[row];
+                    if (ok) {
+                        const float M = fmaxf(m_true, ob.y);
+                        const float wa = ex2_approx((m_ref - M) * c), wb = ex2_approx((ob.x - M) * c);
+                        const float L = wa * l + wb * ob.z;
+                        const float osc = (p.flags & KF_PF_UNNORMALIZED) ? 1.0f : 1.0f / L;
+                        // O_0 = wa * O_0 + wb * O_1 in TMEM (tile 1's O: same lanes, its columns).
+                        const uint32_t tO1 = tl + NQ * BC + D;
+#pragma unroll 1
+                        for (int dc = 0; dc < D / RCH; ++dc) {
+                            uint32_t oa[RCH], ob1[RCH];
+                            tmem_ld_chunk<RCH>(tO + dc * RCH, oa);
+                            tmem_ld_chunk<RCH>(tO1 + dc * RCH, ob1);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int k2 = 0; k2 < RCH; ++k2)
+                                oa[k2] = __float_as_uint(wa * __uint_as_float(oa[k2]) + wb * __uint_as_float(ob1[k2]));
+                            tmem_st_chunk<RCH>(tO + dc * RCH, oa);
+                        }
+                        tmem_wait_st();
+                        if constexpr (C::TMA_STORE) {
+                            stage_store_tile<D, BM, C::KV_BYTES>(stage, tO, row, 2, osc, p.out_type, &tmO, q_row0,
+                                                                b * p.H_q + h);
+                            if (row == 0) mbar_arrive(&stage_free[0]);
+                        } else {
+#pragma unroll
+                            for (int dc = 0; dc < D / OCH; ++dc) {
+                                uint32_t o[OCH];
+                                tmem_ld_chunk<OCH>(tO + dc * OCH, o);
+                                tmem_wait_ld();
+                                if (store) {
+#pragma unroll
+                                    for (int k2 = 0; k2 < OCH; k2 += 4)
+                                        store_out4(p.O, orow + dc * OCH + k2,
+                                                   make_float4(__uint_as_float(o[k2]) * osc, __uint_as_float(o[k2 + 1]) * osc,
+                                                               __uint_as_float(o[k2 + 2]) * osc,
+                                                               __uint_as_float(o[k2 + 3]) * osc),
+                                                   p.out_type);
+                                }
+                            }
+                        }
+                        if (store) {
+                            if (p.Mi) p.Mi[mi] = M * p.scale;
+                            if (p.Li) p.Li[mi] = L;
+                        }
+                    }
+                    tc_fence_before();
+                }
+                ok = named_bar_and(4, 256, ok);
+            } else if (split) {
                 // KV chunk of a split unit.  Tile t of the unit is owned by chunk t: the
                 // other chunks write their partial (O_u, m, l) of tile t, relative to their
                 // own max, and add 1 to the tile's counter; the owner waits (within a short

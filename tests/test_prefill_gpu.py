@@ -307,14 +307,19 @@ def test_lazy_rescale_paths(cuda, D, causal):
     assert_close(got, ref, f"rescale D={D} causal={causal}")
 
 
+@pytest.mark.parametrize("kvh", ["1", "0"])
 @pytest.mark.parametrize("shape", [(1, 32, 8, 512, 512, 128), (1, 32, 8, 300, 300, 64), (1, 16, 4, 384, 500, 16),
-                                   (2, 8, 8, 129, 700, 128)],
+                                   (2, 8, 8, 129, 700, 128), (1, 32, 8, 256, 256, 128), (1, 32, 8, 512, 500, 128),
+                                   (1, 16, 4, 300, 512, 64), (2, 8, 8, 200, 256, 16)],
                          ids=lambda s: "B{}_Hq{}_Hkv{}_Sq{}_Skv{}_D{}".format(*s))
-def test_single_tile_units(cuda, shape):
-    """Short sequences run one 128-row query tile per CTA (twice the CTAs of two-tile units);
-    results and softmax state match the fp64 oracle."""
+def test_single_tile_units(cuda, shape, kvh, monkeypatch):
+    """Short sequences run one 128-row query tile per CTA (twice the CTAs of two-tile units).
+    With an even count of 128-key tiles the CTA's two softmax warpgroups take the keys' two
+    halves and the halves are merged in TMEM (KF_PREFILL_KVH=0: one warpgroup over all keys).
+    Results and softmax state match the fp64 oracle."""
     from kernelfoundry_b200 import plan
 
+    monkeypatch.setenv("KF_PREFILL_KVH", kvh)
     B, H_q, H_kv, S_q, S_kv, D = shape
     assert plan(*shape)["ctas"] == B * H_q * ((S_q + 127) // 128)
     Q, K, V = normal_qkv(*shape, seed=sum(shape) + 9)
@@ -323,3 +328,20 @@ def test_single_tile_units(cuda, shape):
     assert_close(got, O, str(shape))
     assert np.abs(Mi - rMi).max() < 1e-3
     assert np.abs(Li / rLi - 1).max() < 1e-3
+
+
+def test_key_half_units_outputs(cuda):
+    """Key-half units (C1's shape): fp16 output and the unnormalized partial form."""
+    import torch
+
+    from kernelfoundry_b200 import flash_attn_fwd, flash_attn_partial
+
+    Q, K, V = normal_qkv(1, 32, 8, 512, 512, 128, seed=4242)
+    q, k, v = (to_dev(x, cuda) for x in (Q, K, V))
+    O, rMi, rLi = oracle64(Q, K, V)
+    half = flash_attn_fwd(q, k, v, out_dtype=torch.float16).float().cpu().numpy()
+    assert_close(half, O, "key halves, fp16 out", max_abs=4e-3)
+    O_u, m, l = (t.cpu().numpy() for t in flash_attn_partial(q, k, v))
+    assert_close(O_u / l[..., None], O, "key halves, partial O_u/l")
+    assert np.abs(m - rMi).max() < 1e-3
+    assert np.abs(l / rLi - 1).max() < 1e-3
