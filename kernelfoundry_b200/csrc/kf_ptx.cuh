@@ -456,6 +456,24 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
     return d;
 }
 
+// 2^x on the FMA pipe, two lanes per instruction, for x in [-125, 8] (softmax exponents:
+// scores minus a reference max): round-to-nearest split x = j + f, f in [-0.5, 0.5], with the
+// 1.5 * 2^23 shift; 2^f by a degree-3 polynomial least-squares fitted for relative error
+// 7.5e-5 (below fp16 rounding); j added to the exponent field.  Smaller inputs are clamped to
+// -125 (their fp16 P is 0 either way).
+__device__ __forceinline__ float2 ex2_fma2(float2 x) {
+    x.x = fmaxf(x.x, -125.0f);
+    x.y = fmaxf(x.y, -125.0f);
+    const float2 t = fadd2(x, make_float2(12582912.0f, 12582912.0f));
+    const float2 j = fadd2(t, make_float2(-12582912.0f, -12582912.0f));
+    const float2 f = fadd2(x, make_float2(-j.x, -j.y));
+    float2 q = ffma2(make_float2(0.0551716685f, 0.0551716685f), f, make_float2(0.242611155f, 0.242611155f));
+    q = ffma2(q, f, make_float2(0.693260968f, 0.693260968f));
+    q = ffma2(q, f, make_float2(0.999928057f, 0.999928057f));
+    return make_float2(__uint_as_float(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23)),
+                       __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23)));
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&h);
