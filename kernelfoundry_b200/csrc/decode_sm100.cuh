@@ -580,7 +580,7 @@ decode_fwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         cluster_sync_all();   // the other CTAs have read this CTA's partial
     };
     if constexpr (CL) {
-        static_assert(SPLIT && !DEEP && XW == 0 && !PAGED, "cluster merge: plain split kernels only");
+        static_assert(SPLIT && XW == 0 && !PAGED, "cluster merge: contiguous split kernels only");
         static_assert(C::RED_FLOATS * 4 <= C::CL_OFF, "cluster partial overlaps the reduction scratch");
         if (aborted) {
             if (tid < QROWS) cl_ml[tid] = make_float2(-CUDART_INF_F, 0.f);

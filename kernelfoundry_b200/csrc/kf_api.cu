@@ -213,55 +213,67 @@ int decode_blocks_per_sm(int* bps) {
     return kernel_setup<kf::decode_fwd_kernel<D, MT>>(C::SMEM_BYTES, C::THREADS, bps);
 }
 
-// Largest cluster of split CTAs (16 or 8, 0 when none fits) the cluster-merge decode
-// kernel of (D, MT) can be launched with on this device; cached per device.
-template <int D, int MT>
-int decode_cluster_max(int* out) {
-    using C = kf::DecodeCfg<D, MT>;
-    constexpr auto kern = kf::decode_fwd_kernel<D, MT, false, true, false, 0, true>;
-    struct Slot { std::atomic<int> v{-1}; };
+// Cluster-merge decode: for each cluster size s (2..16) of split CTAs, how many such
+// clusters of the (D, MT, DEEP) cluster-merge kernel the device can hold at once
+// (cudaOccupancyMaxActiveClusters; 0: not launchable).  Cached per device.
+struct ClusterCaps {
+    int act[2][17];      // [deep][s]
+};
+
+template <int D, int MT, bool DEEP>
+int decode_cluster_act(int* act) {      // act[0..16]
+    using C = kf::DecodeCfg<D, MT, DEEP>;
+    constexpr auto kern = kf::decode_fwd_kernel<D, MT, false, true, DEEP, 0, true>;
+    struct Slot { std::atomic<int> ready{0}; int act[17]; };
     static Slot slots[kMaxDevices];
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_fail(e);
-    int v = slots[dev].v.load(std::memory_order_acquire);
-    if (v < 0) {
+    Slot& sl = slots[dev];
+    if (!sl.ready.load(std::memory_order_acquire)) {
         if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES)) != cudaSuccess ||
             (e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1)) != cudaSuccess)
             return cuda_fail(e);
-        v = 0;
-        for (int cs = C::MAX_CLUSTER; cs >= 8; cs /= 2) {
+        int tmp[17] = {0};
+        for (int cs = 2; cs <= C::MAX_CLUSTER; ++cs) {
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = dim3(static_cast<unsigned>(cs));
             cfg.blockDim = dim3(C::THREADS);
             cfg.dynamicSmemBytes = C::SMEM_BYTES;
-            cudaLaunchAttribute a[1];
-            a[0].id = cudaLaunchAttributeClusterDimension;
-            a[0].val.clusterDim.x = static_cast<unsigned>(cs);
-            a[0].val.clusterDim.y = 1;
-            a[0].val.clusterDim.z = 1;
-            cfg.attrs = a;
+            cudaLaunchAttribute at[1];
+            at[0].id = cudaLaunchAttributeClusterDimension;
+            at[0].val.clusterDim.x = static_cast<unsigned>(cs);
+            at[0].val.clusterDim.y = 1;
+            at[0].val.clusterDim.z = 1;
+            cfg.attrs = at;
             cfg.numAttrs = 1;
             int n = 0;
-            if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0) {
-                v = cs;
-                break;
-            }
-            cudaGetLastError();    // a size the device cannot place is not an error of the call
+            if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess) tmp[cs] = n;
+            else cudaGetLastError();   // a size the device cannot place is not an error of the call
         }
-        slots[dev].v.store(v, std::memory_order_release);
+        for (int i = 0; i < 17; ++i) sl.act[i] = tmp[i];
+        sl.ready.store(1, std::memory_order_release);
     }
-    *out = v;
+    for (int i = 0; i < 17; ++i) act[i] = sl.act[i];
     return KF_OK;
 }
 
-int decode_cl_max(int D, int mt, int* out) {
-    switch (D) {
-        case 16: return mt == 2 ? decode_cluster_max<16, 2>(out) : decode_cluster_max<16, 1>(out);
-        case 64: return mt == 2 ? decode_cluster_max<64, 2>(out) : decode_cluster_max<64, 1>(out);
-        case 128: return mt == 2 ? decode_cluster_max<128, 2>(out) : decode_cluster_max<128, 1>(out);
-        default: return decode_cluster_max<256, 1>(out);
+// The deep-ring kernel exists for 16-row tiles only (act[1] stays zero for MT = 2).
+int decode_cluster_caps(int D, int mt, ClusterCaps* caps) {
+    std::memset(caps, 0, sizeof(*caps));
+#define KF_CAPS(DV, MTV)                                                               \
+    {                                                                                  \
+        int rc = decode_cluster_act<DV, MTV, false>(caps->act[0]);                     \
+        if (rc == KF_OK && MTV == 1) rc = decode_cluster_act<DV, 1, true>(caps->act[1]); \
+        return rc;                                                                     \
     }
+    switch (D) {
+        case 16: if (mt == 2) KF_CAPS(16, 2) KF_CAPS(16, 1)
+        case 64: if (mt == 2) KF_CAPS(64, 2) KF_CAPS(64, 1)
+        case 128: if (mt == 2) KF_CAPS(128, 2) KF_CAPS(128, 1)
+        default: KF_CAPS(256, 1)
+    }
+#undef KF_CAPS
 }
 
 int decode_bps(int D, int mt, int* bps) {
@@ -275,7 +287,7 @@ int decode_bps(int D, int mt, int* bps) {
 
 int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_bytes, int sm_count,
               int blocks_per_sm, Plan* pl, bool causal = false, double cta_rate = 1.0, bool allow_deep = true,
-              bool deep_only = false, int cl_max = 0) {
+              bool deep_only = false, const ClusterCaps* caps = nullptr) {
     const int G = H_q / H_kv;
     // Causal with several query rows takes the prefill kernel (the decode kernel has
     // no per-row mask); with one row the mask keeps every key, so decode is exact.
@@ -359,8 +371,10 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
     const double kBwMerge = 200.0;   // GB/s == bytes/ns -> x1e-3 per us
     const double kT0 = 2.0, kMerge0 = pl->mt == 1 ? 3.0 : 10.0;
     // Cluster merge (splits of a unit in one thread-block cluster, partials in shared
-    // memory, two cluster barriers and distributed-shared-memory loads): no workspace.
-    const double kMergeCl = 1.0;
+    // memory, two cluster barriers and distributed-shared-memory loads): no workspace, and
+    // measured 0.3 us below the workspace merge at 16-row tiles (B=1, KV=4096: 8.85 against
+    // 9.15 us); at 32-row tiles far below it (MQA, KV=4096: 11.0 against 33.6 us).
+    const double kMergeCl = 2.7;
     const double stage_bytes = 2.0 * TK * D * 2;
     const double total_bytes = static_cast<double>(units) * total_stages * stage_bytes;
     const int nrows = R < 16 * pl->mt ? R : 16 * pl->mt;
@@ -380,23 +394,38 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
     if (deep_only) deep_opt = 1;                     // the caller rejects a plan that is not deep
     for (int deep = 0; deep < 2; ++deep) {
         if ((deep == 1 && deep_opt == 0) || (deep == 0 && deep_opt == 1)) continue;
-        const double kBwCta = (deep ? 55.0 : 50.0) * cta_rate;
+        // Per-CTA stream rate (GB/s): one consumer group ~51, two (deep) 68 (84 measured with
+        // 32 CTAs streaming, about 67 with 96).
+        const double kBwCta = (deep ? 68.0 : 50.0) * cta_rate;
         const double kBwTotal = deep ? 6.6e3 : 6.0e3;
-        const double t_fixed = deep ? 0.6 : 0.0;
         const double cap_d = deep ? static_cast<double>(sm_count) : cap;
         for (int s = 1; s <= max_s; ++s) {
             const int nst = (total_stages + s - 1) / s;
             const int s_eff = (total_stages + nst - 1) / nst;
             if (s_eff != s) continue;
-            const bool cl = !deep && s >= 2 && s <= cl_max;
+            // Cluster merge: a launchable cluster size; the deep kernel also needs every
+            // cluster resident at once (its CTAs all fit on the SMs).
+            const bool cl = caps && s >= 2 && s <= 16 && caps->act[deep][s] > 0 &&
+                            (!deep || caps->act[1][s] >= units);
             if (s > 1 && !cl && (units > kCounterSlots || split_ws_bytes(rows, s, D) > ws_bytes)) break;
             const double ctas = static_cast<double>(units) * s;
             if (deep && ctas > cap_d) break;
+            // The deep kernel pays its larger set-up only when each CTA streams at least 8
+            // stages and the launch keeps at least 85 % of the SMs busy (B=1 sweep: KV=512 in
+            // 8 one-stage splits 5.9 us deep against 4.6 one group; KV=131072 in 12 splits
+            // 83.0 us against 81.0 in 16).
+            // (A deep-only plan -- the fused exchange -- takes the deep kernel regardless.)
+            if (deep && !deep_only && (nst < 8 || ctas < 0.85 * sm_count)) continue;
             const double bw = ctas * kBwCta < kBwTotal ? ctas * kBwCta : kBwTotal;
             const double t_stream = total_bytes / (bw * 1e3) + kT0 * std::ceil(ctas / cap_d);
             const double t_cta = kT0 + nst * stage_bytes / (kBwCta * 1e3);
             const double t_merge = s == 1 ? 0.0 : cl ? kMergeCl : kMerge0 + s * nrows * D * 4.0 / (kBwMerge * 1e3);
+            // The deep kernel's extra fixed cost (group merge, larger ring set-up).
+            const double t_fixed = deep ? (cl ? 0.2 : 0.4) : 0.0;
             const double cost = (t_stream > t_cta ? t_stream : t_cta) + t_merge + t_fixed;
+            if (std::getenv("KF_PLAN_DEBUG"))        // tuning aid: every candidate to stderr
+                std::fprintf(stderr, "decode plan: deep %d splits %d cluster %d act %d cost %.3f us\n", deep, s,
+                             cl ? 1 : 0, caps ? caps->act[deep][s < 17 ? s : 0] : -1, cost);
             if (cost < best_cost * 0.999) {
                 best_cost = cost;
                 best_s = s;
@@ -411,7 +440,8 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
         int want = std::atoi(ov);
         const int s_ov = want >= 1 ? (total_stages + ((total_stages + want - 1) / want) - 1) /
                                          ((total_stages + want - 1) / want) : 0;
-        const bool cl_ov = !best_deep && s_ov >= 2 && s_ov <= cl_max;
+        const bool cl_ov = caps && s_ov >= 2 && s_ov <= 16 && caps->act[best_deep][s_ov] > 0 &&
+                           (!best_deep || caps->act[1][s_ov] >= units);
         if (want >= 1 && want <= max_s && (want == 1 || cl_ov || (units <= kCounterSlots &&
                                                                  split_ws_bytes(rows, want, D) <= ws_bytes))) {
             best_s = s_ov;
@@ -420,8 +450,11 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
     }
     const int nst = (total_stages + best_s - 1) / best_s;
     if (best_deep && static_cast<long long>(units) * best_s > sm_count) best_deep = false;   // after an override
+    if (best_cl)
+        best_cl = caps && best_s >= 2 && best_s <= 16 && caps->act[best_deep][best_s] > 0 &&
+                  (!best_deep || caps->act[1][best_s] >= units);
     pl->deep = best_deep;
-    pl->cluster = best_cl && !best_deep && best_s >= 2;
+    pl->cluster = best_cl && best_s >= 2;
     pl->n_split = best_s;
     pl->chunk = nst * TK;
     pl->ws_bytes = (best_s > 1 && !pl->cluster) ? split_ws_bytes(rows, best_s, D) : 0;
@@ -435,7 +468,9 @@ int plan_for_call(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_
     int rc = device_info(&di);
     if (rc != KF_OK) return rc;
     const int G = H_q / H_kv;
-    int bps = 1, cl_max = 0;
+    int bps = 1;
+    ClusterCaps caps;
+    bool have_caps = false;
     if (use_decode(G, S_q, D) && !(causal && S_q > 1)) {
         const int R = G * S_q;
         const int mt = R <= 16 ? 1 : decode_max_mt(D);
@@ -443,12 +478,14 @@ int plan_for_call(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_
         if (rc != KF_OK) return rc;
         // KF_DECODE_CLUSTER=0: no cluster-merge plans (the workspace ticket merge only).
         const char* ce = std::getenv("KF_DECODE_CLUSTER");
-        if (cta_rate >= 1.0 && !deep_only && !(ce && std::atoi(ce) == 0) && (rc = decode_cl_max(D, mt, &cl_max)) != KF_OK)
-            return rc;
+        if (cta_rate >= 1.0 && !deep_only && !(ce && std::atoi(ce) == 0)) {
+            if ((rc = decode_cluster_caps(D, mt, &caps)) != KF_OK) return rc;
+            have_caps = true;
+        }
     }
     return make_plan(B, H_q, H_kv, S_q, S_kv, D, ws_bytes, di->sm_count, bps, pl, causal, cta_rate,
                      cta_rate >= 1.0,    // paged K/V (cta_rate < 1) has no deep-ring or cluster kernel
-                     deep_only, cl_max);
+                     deep_only, have_caps ? &caps : nullptr);
 }
 
 // ------------------------------------------------------------------ launches
@@ -686,6 +723,14 @@ int launch_decode_t(const Plan& pl, const void* Q, const void* K, const void* V,
             kf::decode_fwd_kernel<D, MT, false, false, true, XW><<<grid, C::THREADS, C::SMEM_BYTES, s>>>(mk, mv, p);
         e = cudaGetLastError();
     } else if constexpr (DEEP) {
+        if (split && pl.cluster) {
+            int act[17];
+            if ((rc = decode_cluster_act<D, MT, true>(act)) != KF_OK) return rc;
+            if (pl.n_split > 16 || act[pl.n_split] <= 0) return KF_ERR_INVALID_ARG;
+            e = launch_ex(kf::decode_fwd_kernel<D, MT, false, true, true, 0, true>, grid, C::THREADS, C::SMEM_BYTES, s,
+                          static_cast<unsigned>(pl.n_split), false, mk, mv, p);
+            return e == cudaSuccess ? KF_OK : cuda_fail(e);
+        }
         e = split ? launch_ex(kf::decode_fwd_kernel<D, MT, false, true, true>, grid, C::THREADS, C::SMEM_BYTES, s, 0u,
                               false, mk, mv, p)
                   : launch_ex(kf::decode_fwd_kernel<D, MT, false, false, true>, grid, C::THREADS, C::SMEM_BYTES, s, 0u,
@@ -694,9 +739,9 @@ int launch_decode_t(const Plan& pl, const void* Q, const void* K, const void* V,
         e = split ? launch_pdl(kf::decode_fwd_kernel<D, MT, true, true>, grid, C::THREADS, C::SMEM_BYTES, s, mk, mv, p)
                   : launch_pdl(kf::decode_fwd_kernel<D, MT, true, false>, grid, C::THREADS, C::SMEM_BYTES, s, mk, mv, p);
     } else if (split && pl.cluster) {
-        int cl_max = 0;
-        if ((rc = decode_cluster_max<D, MT>(&cl_max)) != KF_OK) return rc;
-        if (pl.n_split > cl_max) return KF_ERR_INVALID_ARG;      // the planner keeps within it
+        int act[17];
+        if ((rc = decode_cluster_act<D, MT, false>(act)) != KF_OK) return rc;
+        if (pl.n_split > 16 || act[pl.n_split] <= 0) return KF_ERR_INVALID_ARG;   // the planner keeps within it
         e = launch_ex(kf::decode_fwd_kernel<D, MT, false, true, false, 0, true>, grid, C::THREADS, C::SMEM_BYTES, s,
                       static_cast<unsigned>(pl.n_split), true, mk, mv, p);
     } else {

@@ -250,3 +250,28 @@ def test_cluster_merge(cuda, shape, n_split, monkeypatch):
     assert_close(half, O, "cluster fp16 out", max_abs=4e-3)
     O_u, m, l = (t.cpu().numpy() for t in flash_attn_partial(q, k, v))
     assert_close(O_u / l[..., None], O, "cluster partial O_u/l")
+
+
+@pytest.mark.parametrize("shape", [(1, 32, 8, 1, 4096, 128), (2, 8, 2, 1, 1100, 64), (1, 16, 4, 1, 9000, 128)],
+                         ids=lambda s: "B{}_Hq{}_Hkv{}_Sq{}_Skv{}_D{}".format(*s))
+def test_cluster_merge_deep_ring(cuda, shape, monkeypatch):
+    """The deep-ring kernel (two consumer groups, one CTA per SM) with its splits merged in a
+    thread-block cluster, where every cluster of the launch fits on the GPU at once."""
+    from kernelfoundry_b200 import plan
+    from kernelfoundry_b200.attention import workspace_bytes
+
+    monkeypatch.setenv("KF_DECODE_DEEP", "1")
+    monkeypatch.setenv("KF_DECODE_NSPLIT", "16")
+    stages = (shape[4] + 63) // 64
+    per = (stages + 15) // 16
+    assert plan(*shape)["n_split"] == (stages + per - 1) // per
+    Q, K, V = normal_qkv(*shape, seed=sum(shape) + 77)
+    got, Mi, Li = run_fwd(Q, K, V, cuda, return_lse=True)
+    O, rMi, rLi = oracle64(Q, K, V)
+    assert_close(got, O, f"deep cluster {shape}")
+    assert np.abs(Mi - rMi).max() < 1e-3
+    assert np.abs(Li / rLi - 1).max() < 1e-3
+    # Whether the cluster merge or the workspace merge ran depends on how many 16-CTA
+    # clusters of one-CTA-per-SM blocks this GPU can hold; both must agree with the oracle.
+    assert workspace_bytes(*shape) >= 0
+
