@@ -484,7 +484,7 @@ int plan_for_call(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_
         }
     }
     return make_plan(B, H_q, H_kv, S_q, S_kv, D, ws_bytes, di->sm_count, bps, pl, causal, cta_rate,
-                     cta_rate >= 1.0,    // paged K/V (cta_rate < 1) has no deep-ring or cluster kernel
+                     cta_rate >= 1.0,    // paged K/V (cta_rate < 1): no deep-ring or cluster kernel
                      deep_only, have_caps ? &caps : nullptr);
 }
 
@@ -649,7 +649,9 @@ int launch_decode_t(const Plan& pl, const void* Q, const void* K, const void* V,
         rc = split ? kernel_setup<kf::decode_fwd_kernel<D, MT, false, true, true, XW>>(C::SMEM_BYTES, C::THREADS, &bps)
                    : kernel_setup<kf::decode_fwd_kernel<D, MT, false, false, true, XW>>(C::SMEM_BYTES, C::THREADS, &bps);
     } else if constexpr (DEEP) {
-        if (pg) return KF_ERR_INVALID_ARG;    // no deep-ring paged kernel (the planner never asks)
+        // No deep-ring paged kernel: with one producer per SM issuing 2 KB page copies it
+        // measured 80 us against 47 us one group (B=16, KV=4096, 16-row pages).
+        if (pg) return KF_ERR_INVALID_ARG;
         rc = split ? kernel_setup<kf::decode_fwd_kernel<D, MT, false, true, true>>(C::SMEM_BYTES, C::THREADS, &bps)
                    : kernel_setup<kf::decode_fwd_kernel<D, MT, false, false, true>>(C::SMEM_BYTES, C::THREADS, &bps);
     } else {
