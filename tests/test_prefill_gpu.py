@@ -345,3 +345,50 @@ def test_key_half_units_outputs(cuda):
     assert_close(O_u / l[..., None], O, "key halves, partial O_u/l")
     assert np.abs(m - rMi).max() < 1e-3
     assert np.abs(l / rLi - 1).max() < 1e-3
+
+
+@pytest.mark.parametrize("shape", [(1, 32, 8, 512, 512, 128), (1, 8, 2, 1, 4096, 128), (1, 4, 1, 4096, 4096, 128)],
+                         ids=lambda s: "B{}_Hq{}_Hkv{}_Sq{}_Skv{}_D{}".format(*s))
+def test_back_to_back_dependent_calls(cuda, shape):
+    """Launch overlap (programmatic dependent launch) must not let a call read inputs before the
+    previous call on the stream has written them: call i+1 takes call i's fp16 output as its Q,
+    with no host synchronisation between the calls, eagerly and replayed in a CUDA graph."""
+    import torch
+
+    from kernelfoundry_b200 import flash_attn_fwd
+    from kernelfoundry_b200.attention import new_workspace, workspace_bytes
+
+    B, H_q, H_kv, S_q, S_kv, D = shape
+    Q, K, V = normal_qkv(*shape, seed=sum(shape) + 3)
+    k, v = to_dev(K, cuda), to_dev(V, cuda)
+    ws = new_workspace(max(workspace_bytes(*shape), 16), cuda)
+    n = 4
+    outs = [torch.empty((B, H_q, S_q, D), dtype=torch.float16, device=cuda) for _ in range(n)]
+    q0 = to_dev(Q, cuda)
+
+    def chain():
+        q = q0
+        for i in range(n):
+            flash_attn_fwd(q, k, v, out=outs[i], workspace=ws)
+            q = outs[i]
+
+    # Reference: the same chain on the host, each step's fp16 output as the next Q.
+    ref_q = Q
+    refs = []
+    for i in range(n):
+        o = oracle64(ref_q, K, V)[0]
+        refs.append(o)
+        ref_q = o.astype(np.float16)
+    chain()
+    for i in range(n):
+        assert_close(outs[i].float().cpu().numpy(), refs[i], f"eager step {i}", max_abs=4e-3)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        chain()
+    for o in outs:
+        o.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    for i in range(n):
+        assert_close(outs[i].float().cpu().numpy(), refs[i], f"graph step {i}", max_abs=4e-3)
+    del g
