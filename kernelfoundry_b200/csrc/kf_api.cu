@@ -389,8 +389,9 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
     // reaches ~6.6 instead of ~6.0 TB/s, for ~0.6 us more fixed cost (the groups'
     // merge, the larger ring's set-up): it wins from about 8K keys at B=1 and at B=16,
     // KV=4096.
-    int deep_opt = (allow_deep && pl->mt == 1)
-                       ? (std::getenv("KF_DECODE_DEEP") ? std::atoi(std::getenv("KF_DECODE_DEEP")) : -1) : 0;
+    const char* deep_env = std::getenv("KF_DECODE_DEEP");
+    const bool plan_debug = std::getenv("KF_PLAN_DEBUG") != nullptr;
+    int deep_opt = (allow_deep && pl->mt == 1) ? (deep_env ? std::atoi(deep_env) : -1) : 0;
     if (deep_only) deep_opt = 1;                     // the caller rejects a plan that is not deep
     for (int deep = 0; deep < 2; ++deep) {
         if ((deep == 1 && deep_opt == 0) || (deep == 0 && deep_opt == 1)) continue;
@@ -423,7 +424,7 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
             // The deep kernel's extra fixed cost (group merge, larger ring set-up).
             const double t_fixed = deep ? (cl ? 0.2 : 0.4) : 0.0;
             const double cost = (t_stream > t_cta ? t_stream : t_cta) + t_merge + t_fixed;
-            if (std::getenv("KF_PLAN_DEBUG"))        // tuning aid: every candidate to stderr
+            if (plan_debug)                          // tuning aid: every candidate to stderr
                 std::fprintf(stderr, "decode plan: deep %d splits %d cluster %d act %d cost %.3f us\n", deep, s,
                              cl ? 1 : 0, caps ? caps->act[deep][s < 17 ? s : 0] : -1, cost);
             if (cost < best_cost * 0.999) {
