@@ -53,15 +53,22 @@ const char* kf_version(void);
  *           launch of flash_attn_kernel<D> (tests/bench_flash_attn.cu:39-54,
  *           raw kernel signature kernels/flash_attn.cu:384-398).
  * Differences, by design: asynchronous (no stream synchronize), no per-call
- * cudaMalloc of Mi/Li scratch (the softmax state stays on chip; short-query
- * split-KV partials go to the caller's workspace).
+ * cudaMalloc of Mi/Li scratch (the softmax state stays on chip; split partials
+ * stay in shared memory or go to the caller's workspace).  Kernels are launched
+ * with programmatic stream serialization: their CTAs may be dispatched while the
+ * previous kernel on the stream drains, and they read and write global memory
+ * only after that kernel has completed (KF_PDL=0 in the environment: plain
+ * launches).
  *
- * workspace: optional device buffer used by the split-KV decode path.  Size it
- * with kf_attn_workspace_bytes(); zero-fill it once before its first use
+ * workspace: optional device buffer used by split-KV decode plans that merge
+ * through global memory (more than 16 splits per KV head, paged K/V) and by the
+ * prefill's split last wave; decode splits that merge inside a thread-block
+ * cluster need none (kf_attn_workspace_bytes then returns 0).  Size it with
+ * kf_attn_workspace_bytes(); zero-fill it once before its first use
  * (kf_attn_workspace_init); every successful call leaves it ready for the
  * next.  Two calls that overlap on the GPU must not share a workspace.
- * workspace == NULL (or too small) is valid: the decode path then uses fewer
- * KV splits (slower for small batches, same results).
+ * workspace == NULL (or too small) is valid: decode then merges in a cluster or
+ * uses fewer KV splits, and the prefill's last wave is not split (same results).
  */
 int kf_attn_fwd(const void* Q, const void* K, const void* V, float* O,
                 int B, int H_q, int H_kv, int S_q, int S_kv, int D,
