@@ -1075,17 +1075,18 @@ int kf_attn_exchange_combine(void* const* windows, int world, int rank, long lon
     p.Li = Li;
     p.timeout_ns = g_timeout_ns.load();
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const dim3 grid(static_cast<unsigned>(n_chunks));
+    cudaError_t e;
     switch (world) {
-        case 1: kf::exchange_combine_kernel<1><<<n_chunks, 256, 0, st>>>(p); break;
-        case 2: kf::exchange_combine_kernel<2><<<n_chunks, 256, 0, st>>>(p); break;
-        case 3: kf::exchange_combine_kernel<3><<<n_chunks, 256, 0, st>>>(p); break;
-        case 4: kf::exchange_combine_kernel<4><<<n_chunks, 256, 0, st>>>(p); break;
-        case 5: kf::exchange_combine_kernel<5><<<n_chunks, 256, 0, st>>>(p); break;
-        case 6: kf::exchange_combine_kernel<6><<<n_chunks, 256, 0, st>>>(p); break;
-        case 7: kf::exchange_combine_kernel<7><<<n_chunks, 256, 0, st>>>(p); break;
-        default: kf::exchange_combine_kernel<8><<<n_chunks, 256, 0, st>>>(p); break;
+        case 1: e = launch_pdl(kf::exchange_combine_kernel<1>, grid, 256, 0, st, p); break;
+        case 2: e = launch_pdl(kf::exchange_combine_kernel<2>, grid, 256, 0, st, p); break;
+        case 3: e = launch_pdl(kf::exchange_combine_kernel<3>, grid, 256, 0, st, p); break;
+        case 4: e = launch_pdl(kf::exchange_combine_kernel<4>, grid, 256, 0, st, p); break;
+        case 5: e = launch_pdl(kf::exchange_combine_kernel<5>, grid, 256, 0, st, p); break;
+        case 6: e = launch_pdl(kf::exchange_combine_kernel<6>, grid, 256, 0, st, p); break;
+        case 7: e = launch_pdl(kf::exchange_combine_kernel<7>, grid, 256, 0, st, p); break;
+        default: e = launch_pdl(kf::exchange_combine_kernel<8>, grid, 256, 0, st, p); break;
     }
-    cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KF_OK : cuda_fail(e);
 }
 

@@ -84,6 +84,10 @@ __device__ __forceinline__ unsigned long long ld_word(const unsigned long long* 
 template <int W>
 __global__ void __launch_bounds__(256) exchange_combine_kernel(const ExchangeParams p) {
     __shared__ unsigned s_seq;
+    // Launched with programmatic stream serialization: the partial this kernel sends is the
+    // previous launch's output, so nothing global is touched before that launch completes.
+    grid_dep_wait();
+    grid_dep_launch_dependents();
     const int c = blockIdx.x;
     const long long rows_per = (p.rows + p.n_chunks - 1) / p.n_chunks;
     const long long r0 = c * rows_per;
