@@ -213,6 +213,7 @@ CLUSTER_SHAPES = [
     (1, 32, 8, 1, 4096, 128),    # the C3 B=1 shape
     (3, 32, 8, 1, 1000, 128),    # ragged last stage
     (1, 32, 1, 1, 4096, 128),    # MQA: 32 packed rows (two 16-row MMA tiles per CTA)
+    (2, 32, 1, 2, 1500, 128),    # 64 packed rows: two row groups per KV head (grid y = 2)
     (2, 8, 2, 1, 1100, 64),      # D=64
     (2, 16, 8, 2, 1090, 16),     # D=16, S_q=2
     (1, 8, 8, 1, 3000, 256),     # D=256

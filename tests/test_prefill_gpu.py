@@ -310,7 +310,8 @@ def test_lazy_rescale_paths(cuda, D, causal):
 @pytest.mark.parametrize("kvh", ["1", "0"])
 @pytest.mark.parametrize("shape", [(1, 32, 8, 512, 512, 128), (1, 32, 8, 300, 300, 64), (1, 16, 4, 384, 500, 16),
                                    (2, 8, 8, 129, 700, 128), (1, 32, 8, 256, 256, 128), (1, 32, 8, 512, 500, 128),
-                                   (1, 16, 4, 300, 512, 64), (2, 8, 8, 200, 256, 16)],
+                                   (1, 16, 4, 300, 512, 64), (2, 8, 8, 200, 256, 16), (1, 8, 2, 64, 512, 128),
+                                   (2, 4, 4, 100, 256, 64)],
                          ids=lambda s: "B{}_Hq{}_Hkv{}_Sq{}_Skv{}_D{}".format(*s))
 def test_single_tile_units(cuda, shape, kvh, monkeypatch):
     """Short sequences run one 128-row query tile per CTA (twice the CTAs of two-tile units).
