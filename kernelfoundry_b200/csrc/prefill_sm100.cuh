@@ -134,6 +134,7 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, 
 // the unit's one query tile, tile t the keys of KV tiles [t * n_kv, (t + 1) * n_kv).
 struct PrefillItem {
     int unit, chunk, qblk, h, b, h_kv, q_row0, nq_active, kt0, n_kv;
+    int n_kv0;          // KV steps of tile 0 (causal: one fewer where its rows end before the last tile)
     bool split;
 };
 
@@ -161,14 +162,19 @@ __device__ __forceinline__ PrefillItem prefill_item(const PrefillParams& p, int 
     const int n_kv_all = (p.S_kv + C::BC - 1) / C::BC;
     it.kt0 = it.split ? it.chunk * p.per : 0;                                         // first KV tile
     it.n_kv = it.split ? min(p.per, n_kv_all - it.kt0) : n_kv_all;                   // KV tiles of the item
+    it.n_kv0 = it.n_kv;
     if constexpr (CAUSAL) {
         // Keys up to the unit's last (valid) query row + kv_off; the split path is off.
         const int last_row = min(it.q_row0 + C::NQ * C::BM, p.S_q) - 1;
         it.n_kv = min(n_kv_all, (last_row + p.kv_off) / C::BC + 1);
+        // Tile 0 of a two-tile unit stops at the KV tile holding its own last row's
+        // diagonal: the unit's last KV tile is fully masked for it.
+        it.n_kv0 = it.nq_active == 2 ? min(it.n_kv, (it.q_row0 + C::BM - 1 + p.kv_off) / C::BC + 1) : it.n_kv;
     }
     if constexpr (KVH) {
         it.nq_active = 2;              // two key halves of one query tile (n_kv_all is even)
         it.n_kv = n_kv_all / 2;        // per tile
+        it.n_kv0 = it.n_kv;
     }
     return it;
 }
@@ -438,7 +444,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 } else if constexpr (C::TMA_STORE) {
                     // The item's epilogue stages tile 0 in the slot of its last K and tile 1
                     // in the slot of its last V.
-                    pend[0] |= 1u << ((pos - 2) % NSLOT);
+                    pend[0] |= 1u << ((pos - 2 - 2 * (it.n_kv - it.n_kv0)) % NSLOT);
                     if (NQ == 2 && it.nq_active == 2) pend[NQ - 1] |= 1u << ((pos - 1) % NSLOT);
                 }
                 ++n_done;
@@ -551,7 +557,8 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                         if (j == n_kv - 1) umma_commit(q_empty);      // Q is free once these QKs complete
                     }
                     ring += 4 * n_kv;
-                } else
+                } else {
+                const int n_kv0 = it.n_kv0;        // tile 0's steps (<= n_kv; causal only fewer)
                 for (int j = 0; j <= n_kv && ok; ++j) {
                     // V_{j-1} sits at ring position 2j - 1 of the item, just before K_j.
                     int slotV = slotK - 1, parV = parK;
@@ -572,7 +579,8 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                         if (t >= nq_active) break;
                         const uint32_t tS = tmem + t * BC;
                         const uint32_t tO = tmem + NQ * BC + t * D;
-                        if (j > 0) {
+                        const int n_t = (CAUSAL && t == 0) ? n_kv0 : n_kv;
+                        if (j > 0 && j <= n_t) {
                             // P_t arrives in two halves (keys [0, BC/2) then [BC/2, BC)): the
                             // first half of the PV MMAs runs while the softmax finishes the rest.
                             // Every softmax thread arrives on p_half before p_full, so a
@@ -598,11 +606,12 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                                 }
                             }
                             if (!ok) break;
-                            if (j == n_kv) umma_commit(&o_full[t]);
-                            // V_{j-1} is free once the last tile's PV has read it (before QK_B(j)).
+                            if (j == n_t) umma_commit(&o_full[t]);
+                            // V_{j-1} is free once the last tile's PV has read it (before QK_B(j));
+                            // the last tile has all n_kv steps.
                             if (t == nq_active - 1) umma_commit(&kv_empty[slotV]);
                         }
-                        if (j < n_kv) {
+                        if (j < n_t) {
                             const uint32_t a_lo = q_lo + t * (C::Q_BYTES >> 4);
 #pragma unroll
                             for (int kk = 0; kk < D / 16; ++kk) {
@@ -624,9 +633,10 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                         if (slotK >= NSLOT) { slotK -= NSLOT; ++parK; }
                     }
                 }
+                }
 #pragma unroll
                 for (int t = 0; t < NQ; ++t)
-                    if (t < nq_active) steps[t] += n_kv;
+                    if (t < nq_active) steps[t] += (t == 0) ? it.n_kv0 : n_kv;
             }
             // Every MMA issued above must complete before TMEM is released.
             umma_commit(mma_done);
@@ -653,9 +663,9 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             int n_kv, kt0, diag;
             {
                 const PrefillItem it = prefill_item<D, CAUSAL, SPLIT, KVH>(p, item);
-                n_kv = it.n_kv;
+                n_kv = t == 0 ? it.n_kv0 : it.n_kv;         // this tile's KV steps
                 kt0 = it.kt0 + (KVH ? t * it.n_kv : 0);     // KVH: this tile's half of the keys
-                pos += (KVH ? 4 : 2) * n_kv;
+                pos += (KVH ? 4 : 2) * it.n_kv;
                 if (t >= it.nq_active) continue;
                 // Causal: keys of tile j visible to this row are those below diag - j*BC.
                 diag = CAUSAL ? it.q_row0 + t * BM + row + p.kv_off - kt0 * BC + 1 : 0;
@@ -800,7 +810,10 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             // Staging slot of this tile: the ring slot of the item's last K (tile 0) or
             // last V (tile 1); every MMA reading it completed before o_full[t] fired.  KVH:
             // the slot of the last first-half K, for tile 0 (the one that stores).
-            uint8_t* stage = sKV + ((KVH ? pos - 4 : pos - 2 + t) % NSLOT) * C::KV_BYTES;
+            // (Causal: tile 0 stages in the slot of its own last K, whose QKs were issued before
+            // its o_full; the item's later loads stay within the ring depth of it.)
+            uint8_t* stage = sKV + ((KVH ? pos - 4 : t == 0 ? pos - 2 - 2 * (ie.n_kv - ie.n_kv0) : pos - 1) % NSLOT) *
+                                   C::KV_BYTES;
             const int qrow = q_row0 + (KVH ? 0 : t * BM) + row;
             const bool store = qrow < p.S_q;
             const size_t orow = ((static_cast<size_t>(b) * p.H_q + h) * p.S_q + (store ? qrow : 0)) * D;   // element index
