@@ -322,7 +322,14 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
         const int cap = sm_count;
         const int rem = static_cast<int>(units % cap);
         const int n_kv = (S_kv + bc - 1) / bc;
-        int k = (rem > 0 && !causal && pl->pf_tiles == nq) ? cap / rem : 1;   // causal units differ in size: no split
+        // Causal units differ in size; with a long cache (S_kv >= 2 S_q, chunked prefill)
+        // they differ little, and each split unit's keys are divided evenly over its chunks.
+        const int kv_off = S_kv - S_q;
+        const bool causal_split = causal && S_kv >= 2 * S_q;
+        int k = (rem > 0 && (!causal || causal_split) && pl->pf_tiles == nq) ? cap / rem : 1;
+        // Causal: every row must see a key of every chunk (kv_off >= 384 (k - 1): the lightest
+        // unit's last chunk starts at most 384 (k - 1) keys past its first row's diagonal).
+        if (causal && k > kv_off / 384 + 1) k = kv_off / 384 + 1;
         k = k > 4 ? 4 : k;
         // Each chunk keeps >= 4 KV tiles: writing and merging the partials costs about
         // as much as 3 KV steps (measured: S = 512, 4 tiles in 2 chunks, took 21 us
@@ -332,10 +339,12 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
             const int m = std::atoi(ov);
             if (m >= 1) min_chunk = m;
         }
-        k = k > n_kv / min_chunk ? n_kv / min_chunk : k;
+        // (Causal: the lightest unit's tile count, that of the first query block.)
+        const int n_kv_min = causal ? ((rows_per_cta < S_q ? rows_per_cta : S_q) - 1 + kv_off) / bc + 1 : n_kv;
+        k = k > n_kv_min / min_chunk ? n_kv_min / min_chunk : k;
         if (k >= 2) {
             const int per = (n_kv + k - 1) / k;
-            const int k_eff = (n_kv + per - 1) / per;
+            const int k_eff = causal ? k : (n_kv + per - 1) / per;   // causal: even division, k chunks
             const size_t part = static_cast<size_t>(rem) * k_eff * rows_per_cta * (D + 2) * sizeof(float);
             const size_t need = kCounterBytes + ((part + 255) / 256) * 256;
             if (k_eff >= 2 && need <= ws_bytes) {
@@ -538,7 +547,6 @@ int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, 
     using C = kf::PrefillCfg<D>;
     int bps = 0;
     const bool split = pl.pf_plain < pl.pf_units;
-    if (causal && split) return KF_ERR_INVALID_ARG;    // the planner never splits causal units
     const bool kvh = C::NQ == 2 && pl.pf_kvh;
     if (kvh && (causal || split)) return KF_ERR_INVALID_ARG;
     int rc;
@@ -546,7 +554,8 @@ int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, 
         if (kvh) rc = kernel_setup<kf::prefill_fwd_kernel<D, false, false, true>>(C::SMEM_BYTES, C::THREADS, &bps);
     }
     if (!kvh)
-        rc = causal  ? kernel_setup<kf::prefill_fwd_kernel<D, true, false>>(C::SMEM_BYTES, C::THREADS, &bps)
+        rc = causal  ? (split ? kernel_setup<kf::prefill_fwd_kernel<D, true, true>>(C::SMEM_BYTES, C::THREADS, &bps)
+                              : kernel_setup<kf::prefill_fwd_kernel<D, true, false>>(C::SMEM_BYTES, C::THREADS, &bps))
              : split ? kernel_setup<kf::prefill_fwd_kernel<D, false, true>>(C::SMEM_BYTES, C::THREADS, &bps)
                      : kernel_setup<kf::prefill_fwd_kernel<D, false, false>>(C::SMEM_BYTES, C::THREADS, &bps);
     if (rc != KF_OK) return rc;
@@ -613,7 +622,9 @@ int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, 
                            mo, p);
     }
     if (kvh) {
-    } else if (causal)
+    } else if (causal && split)
+        e = launch_pdl(kf::prefill_fwd_kernel<D, true, true>, grid, C::THREADS, C::SMEM_BYTES, s, mq, mk, mv, mo, p);
+    else if (causal)
         e = launch_pdl(kf::prefill_fwd_kernel<D, true, false>, grid, C::THREADS, C::SMEM_BYTES, s, mq, mk, mv, mo, p);
     else if (split)
         e = launch_pdl(kf::prefill_fwd_kernel<D, false, true>, grid, C::THREADS, C::SMEM_BYTES, s, mq, mk, mv, mo, p);

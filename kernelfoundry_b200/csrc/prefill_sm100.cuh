@@ -164,12 +164,22 @@ __device__ __forceinline__ PrefillItem prefill_item(const PrefillParams& p, int 
     it.n_kv = it.split ? min(p.per, n_kv_all - it.kt0) : n_kv_all;                   // KV tiles of the item
     it.n_kv0 = it.n_kv;
     if constexpr (CAUSAL) {
-        // Keys up to the unit's last (valid) query row + kv_off; the split path is off.
+        // Keys up to the unit's last (valid) query row + kv_off.
         const int last_row = min(it.q_row0 + C::NQ * C::BM, p.S_q) - 1;
-        it.n_kv = min(n_kv_all, (last_row + p.kv_off) / C::BC + 1);
-        // Tile 0 of a two-tile unit stops at the KV tile holding its own last row's
-        // diagonal: the unit's last KV tile is fully masked for it.
-        it.n_kv0 = it.nq_active == 2 ? min(it.n_kv, (it.q_row0 + C::BM - 1 + p.kv_off) / C::BC + 1) : it.n_kv;
+        const int u = min(n_kv_all, (last_row + p.kv_off) / C::BC + 1);
+        if (it.split) {
+            // Split unit (chunked prefill, S_kv >= 2 S_q): the unit's own u key tiles are
+            // divided evenly over the split_k chunks.  The host keeps kv_off >= 384 (split_k - 1),
+            // so every row of the unit sees at least one key of every chunk.
+            it.kt0 = (it.chunk * u) / p.split_k;
+            it.n_kv = ((it.chunk + 1) * u) / p.split_k - it.kt0;
+            it.n_kv0 = it.n_kv;
+        } else {
+            it.n_kv = u;
+            // Tile 0 of a two-tile unit stops at the KV tile holding its own last row's
+            // diagonal: the unit's last KV tile is fully masked for it.
+            it.n_kv0 = it.nq_active == 2 ? min(it.n_kv, (it.q_row0 + C::BM - 1 + p.kv_off) / C::BC + 1) : it.n_kv;
+        }
     }
     if constexpr (KVH) {
         it.nq_active = 2;              // two key halves of one query tile (n_kv_all is even)

@@ -393,3 +393,38 @@ def test_back_to_back_dependent_calls(cuda, shape):
     for i in range(n):
         assert_close(outs[i].float().cpu().numpy(), refs[i], f"graph step {i}", max_abs=4e-3)
     del g
+
+
+CAUSAL_SPLIT = [(1, 32, 8, 512, 4096, 128), (1, 16, 4, 256, 2048, 64), (2, 8, 2, 300, 1500, 128),
+                (1, 8, 8, 128, 1024, 256), (1, 8, 2, 1024, 2048, 128)]
+
+
+@pytest.mark.parametrize("merge", ["owner", "ticket"])
+@pytest.mark.parametrize("shape", CAUSAL_SPLIT, ids=lambda s: "B{}_Hq{}_Hkv{}_Sq{}_Skv{}_D{}".format(*s))
+def test_causal_chunked_prefill_split(cuda, shape, merge, monkeypatch):
+    """Causal chunked prefill over a long cache (S_kv >= 2 S_q) with few units: the last wave's
+    units are split along their own keys (evenly, every row seeing keys in every chunk) and
+    merged; results, softmax state and the zeroed counters against the causal oracle."""
+    import torch
+
+    from oracle.attn_oracle import causal_attn_lse
+
+    from kernelfoundry_b200 import flash_attn_fwd
+    from kernelfoundry_b200.attention import new_workspace, workspace_bytes
+
+    if merge == "ticket":
+        monkeypatch.setenv("KF_PREFILL_TICKET_MERGE", "1")
+    need = workspace_bytes(*shape)
+    Q, K, V = normal_qkv(*shape, seed=13 * sum(shape))
+    q, k, v = (to_dev(x, cuda) for x in (Q, K, V))
+    ws = new_workspace(max(need, 16), cuda)
+    got, Mi, Li = (t.cpu().numpy() for t in flash_attn_fwd(q, k, v, causal=True, return_lse=True, workspace=ws))
+    O, rMi, rLi = causal_attn_lse(*(x.astype(np.float64) for x in (Q, K, V)))
+    assert np.isfinite(got).all()
+    assert_close(got, O, f"causal split {shape}")
+    assert np.abs(Mi - rMi).max() < 1e-3
+    assert np.abs(Li / rLi - 1).max() < 1e-3
+    assert int(ws[:65536].view(torch.int32).abs().sum()) == 0
+    plain = flash_attn_fwd(q, k, v, causal=True, workspace=torch.empty(0, dtype=torch.uint8, device=cuda))
+    ma, rl = error_stats(got, plain.cpu().numpy())
+    assert ma <= 2e-3 and rl <= 1e-3, (ma, rl)
