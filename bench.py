@@ -424,6 +424,12 @@ def run_extras(args, rank, world, dev, peaks):
     out["prefill_causal_S4096_B1"] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 1),
                                       "frac_tensor": round(tf / peaks["bf16_tflops"], 3),
                                       "flops": "4*D per visible (query, key) pair"}
+    # Chunked prefill: a 512-token chunk over a 4096-key cache, causal (bottom-right mask).
+    ms, rot, pl = bench_cfg(1, H_Q, H_KV, 512, S, D, causal=True)
+    tf = causal_flops(1, H_Q, 512, S, D) / (ms * 1e-3) / 1e12
+    out["prefill_causal_chunk_Sq512_Skv4096_B1"] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 1),
+                                                    "frac_tensor": round(tf / peaks["bf16_tflops"], 3),
+                                                    "flops": "4*D per visible (query, key) pair"}
     torch.cuda.empty_cache()
     out.update(bench_pointwise(stream, gen, dev, peaks, iters))
     out["reference_bench_sweep"] = run_ref_sweep(stream, gen, dev, peaks, l2)
