@@ -308,9 +308,13 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
         }
         // One-tile units run the tile's two key halves as the CTA's two tiles (two chains in
         // ping-pong instead of one), merged in TMEM; KF_PREFILL_KVH=0 turns it off.
+        // Also S_q <= 128 (every two-tile unit would have one tile): one-tile units whose
+        // two chains take the keys' halves, split along KV as below when few.
         const char* kvh = std::getenv("KF_PREFILL_KVH");
-        pl->pf_kvh = pl->pf_tiles == 1 && nq == 2 && !causal && n_kv_tiles >= 2 && n_kv_tiles % 2 == 0 &&
-                     !(kvh && std::atoi(kvh) == 0);
+        const bool kvh_off = kvh && std::atoi(kvh) == 0;
+        if (nq == 2 && !causal && S_q <= 128 && n_kv_tiles >= 4 && n_kv_tiles % 2 == 0 && !kvh_off)
+            pl->pf_tiles = 1;
+        pl->pf_kvh = pl->pf_tiles == 1 && nq == 2 && !causal && n_kv_tiles >= 2 && n_kv_tiles % 2 == 0 && !kvh_off;
         const int rows_per_cta = pl->pf_tiles * 128;
         pl->pf_qblk = (S_q + rows_per_cta - 1) / rows_per_cta;
         const long long units = static_cast<long long>(pl->pf_qblk) * H_q * B;
@@ -326,7 +330,7 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
         // they differ little, and each split unit's keys are divided evenly over its chunks.
         const int kv_off = S_kv - S_q;
         const bool causal_split = causal && S_kv >= 2 * S_q;
-        int k = (rem > 0 && (!causal || causal_split) && pl->pf_tiles == nq) ? cap / rem : 1;
+        int k = (rem > 0 && (!causal || causal_split) && (pl->pf_tiles == nq || pl->pf_kvh)) ? cap / rem : 1;
         // Causal: every row must see a key of every chunk (kv_off >= 384 (k - 1): the lightest
         // unit's last chunk starts at most 384 (k - 1) keys past its first row's diagonal).
         if (causal && k > kv_off / 384 + 1) k = kv_off / 384 + 1;
@@ -343,9 +347,11 @@ int make_plan(int B, int H_q, int H_kv, int S_q, int S_kv, int D, size_t ws_byte
         const int n_kv_min = causal ? ((rows_per_cta < S_q ? rows_per_cta : S_q) - 1 + kv_off) / bc + 1 : n_kv;
         k = k > n_kv_min / min_chunk ? n_kv_min / min_chunk : k;
         if (k >= 2) {
-            const int per = (n_kv + k - 1) / k;
+            int per = (n_kv + k - 1) / k;
+            if (pl->pf_kvh) per += per & 1;         // key-half units: even chunks (n_kv is even)
             const int k_eff = causal ? k : (n_kv + per - 1) / per;   // causal: even division, k chunks
-            const size_t part = static_cast<size_t>(rem) * k_eff * rows_per_cta * (D + 2) * sizeof(float);
+            // Partials are laid out per full unit (nq tiles of 128 rows) in the kernel.
+            const size_t part = static_cast<size_t>(rem) * k_eff * (nq * 128) * (D + 2) * sizeof(float);
             const size_t need = kCounterBytes + ((part + 255) / 256) * 256;
             if (k_eff >= 2 && need <= ws_bytes) {
                 pl->pf_plain = pl->pf_units - rem;
@@ -548,10 +554,12 @@ int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, 
     int bps = 0;
     const bool split = pl.pf_plain < pl.pf_units;
     const bool kvh = C::NQ == 2 && pl.pf_kvh;
-    if (kvh && (causal || split)) return KF_ERR_INVALID_ARG;
+    if (kvh && causal) return KF_ERR_INVALID_ARG;
     int rc;
     if constexpr (C::NQ == 2) {
-        if (kvh) rc = kernel_setup<kf::prefill_fwd_kernel<D, false, false, true>>(C::SMEM_BYTES, C::THREADS, &bps);
+        if (kvh)
+            rc = split ? kernel_setup<kf::prefill_fwd_kernel<D, false, true, true>>(C::SMEM_BYTES, C::THREADS, &bps)
+                       : kernel_setup<kf::prefill_fwd_kernel<D, false, false, true>>(C::SMEM_BYTES, C::THREADS, &bps);
     }
     if (!kvh)
         rc = causal  ? (split ? kernel_setup<kf::prefill_fwd_kernel<D, true, true>>(C::SMEM_BYTES, C::THREADS, &bps)
@@ -617,7 +625,10 @@ int launch_prefill(const Plan& pl, const void* Q, const void* K, const void* V, 
     const dim3 grid(static_cast<unsigned>(ctas));
     cudaError_t e = cudaSuccess;
     if constexpr (C::NQ == 2) {
-        if (kvh)
+        if (kvh && split)
+            e = launch_pdl(kf::prefill_fwd_kernel<D, false, true, true>, grid, C::THREADS, C::SMEM_BYTES, s, mq, mk, mv,
+                           mo, p);
+        else if (kvh)
             e = launch_pdl(kf::prefill_fwd_kernel<D, false, false, true>, grid, C::THREADS, C::SMEM_BYTES, s, mq, mk, mv,
                            mo, p);
     }

@@ -182,8 +182,8 @@ __device__ __forceinline__ PrefillItem prefill_item(const PrefillParams& p, int 
         }
     }
     if constexpr (KVH) {
-        it.nq_active = 2;              // two key halves of one query tile (n_kv_all is even)
-        it.n_kv = n_kv_all / 2;        // per tile
+        it.nq_active = 2;              // two key halves of one query tile (item's tile count is even)
+        it.n_kv = it.n_kv / 2;         // per tile (all keys, or the split chunk's)
         it.n_kv0 = it.n_kv;
     }
     return it;
@@ -808,8 +808,8 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             }
             ++o_cnt;
             // Rebase to the true row max: O_t * f and l * f are relative to m_true.
-            const float f = ex2_approx((m_ref - m_true) * c);
-            const float l_true = l * f;
+            float f = ex2_approx((m_ref - m_true) * c);
+            float l_true = l * f;
             // The item's fields for the epilogue, recomputed from its index (an opaque
             // copy, so the compiler does not keep them in registers across the KV loop).
             int item_e;
@@ -865,7 +865,15 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                             tmem_st_chunk<RCH>(tO + dc * RCH, oa);
                         }
                         tmem_wait_st();
-                        if constexpr (C::TMA_STORE) {
+                        if (split) {
+                            // A split chunk: the merged tile goes on to the split epilogue below
+                            // as this chunk's tile 0 (O relative to M, sum L).
+                            m_ref = M;
+                            m_true = M;
+                            l = L;
+                            f = 1.0f;
+                            l_true = L;
+                        } else if constexpr (C::TMA_STORE) {
                             stage_store_tile<D, BM, C::KV_BYTES>(stage, tO, row, 2, osc, p.out_type, &tmO, q_row0,
                                                                 b * p.H_q + h);
                             if (row == 0) mbar_arrive(&stage_free[0]);
@@ -886,7 +894,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                                 }
                             }
                         }
-                        if (store) {
+                        if (store && !split) {
                             if (p.Mi) p.Mi[mi] = M * p.scale;
                             if (p.Li) p.Li[mi] = L;
                         }
@@ -894,7 +902,8 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     tc_fence_before();
                 }
                 ok = named_bar_and(4, 256, ok);
-            } else if (split) {
+            }
+            if ((!KVH || t == 0) && split) {
                 // KV chunk of a split unit.  Tile t of the unit is owned by chunk t: the
                 // other chunks write their partial (O_u, m, l) of tile t, relative to their
                 // own max, and add 1 to the tile's counter; the owner waits (within a short
@@ -1071,7 +1080,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                         if (row == 0) *counter = 0u;
                     }
                 }
-            } else {
+            } else if (!KVH) {
                 // Every thread of the tile reaches this barrier, ok or not, so the staged
                 // epilogue below (which synchronizes the tile's threads) runs for all or none.
                 if constexpr (C::TMA_STORE) ok = named_bar_and(2 + t, 128, ok);

@@ -428,3 +428,39 @@ def test_causal_chunked_prefill_split(cuda, shape, merge, monkeypatch):
     plain = flash_attn_fwd(q, k, v, causal=True, workspace=torch.empty(0, dtype=torch.uint8, device=cuda))
     ma, rl = error_stats(got, plain.cpu().numpy())
     assert ma <= 2e-3 and rl <= 1e-3, (ma, rl)
+
+
+SHORT_CHUNKS = [(1, 32, 8, 128, 4096, 128), (2, 8, 2, 100, 2048, 64), (1, 16, 4, 128, 3000, 128),
+                (1, 8, 8, 64, 1024, 16), (8, 32, 8, 128, 1024, 128), (3, 8, 2, 128, 512, 128)]
+
+
+@pytest.mark.parametrize("merge", ["owner", "ticket"])
+@pytest.mark.parametrize("shape", SHORT_CHUNKS, ids=lambda s: "B{}_Hq{}_Hkv{}_Sq{}_Skv{}_D{}".format(*s))
+def test_short_query_chunks(cuda, shape, merge, monkeypatch):
+    """Up to 128 queries over a longer cache: one-tile units whose two chains take the keys'
+    halves (merged in TMEM), split along KV when the units are few (each chunk's halves merged
+    in TMEM, then the chunks by the owner or by ticket), and over several rounds when many.
+    Results, softmax state and zeroed counters against the fp64 oracle and the one-chain form."""
+    import torch
+
+    from kernelfoundry_b200 import flash_attn_fwd
+    from kernelfoundry_b200.attention import new_workspace, workspace_bytes
+
+    if merge == "ticket":
+        monkeypatch.setenv("KF_PREFILL_TICKET_MERGE", "1")
+    Q, K, V = normal_qkv(*shape, seed=17 * sum(shape))
+    q, k, v = (to_dev(x, cuda) for x in (Q, K, V))
+    ws = new_workspace(max(workspace_bytes(*shape), 16), cuda)
+    got, Mi, Li = (t.cpu().numpy() for t in flash_attn_fwd(q, k, v, return_lse=True, workspace=ws))
+    O, rMi, rLi = oracle64(Q, K, V)
+    assert np.isfinite(got).all()
+    assert_close(got, O, f"short chunk {shape}")
+    assert np.abs(Mi - rMi).max() < 1e-3
+    assert np.abs(Li / rLi - 1).max() < 1e-3
+    assert int(ws[:65536].view(torch.int32).abs().sum()) == 0
+    half = flash_attn_fwd(q, k, v, out_dtype=torch.float16, workspace=ws).float().cpu().numpy()
+    assert_close(half, O, "short chunk fp16 out", max_abs=4e-3)
+    monkeypatch.setenv("KF_PREFILL_KVH", "0")
+    one_chain = flash_attn_fwd(q, k, v, workspace=ws).cpu().numpy()
+    ma, rl = error_stats(got, one_chain)
+    assert ma <= 2e-3 and rl <= 1e-3, (ma, rl)
