@@ -930,6 +930,7 @@ CASES = {
     "prefill_C2": (1, H_Q, H_KV, S, S, D),
     "prefill_C2_B8": (8, H_Q, H_KV, S, S, D),
     "prefill_C1": (1, H_Q, H_KV, 512, 512, D),
+    "prefill_chunk_q128": (1, H_Q, H_KV, 128, S, D),
     "mqa_C4": (4, 32, 1, 2048, 2048, 64),
     "decode_B1": (1, H_Q, H_KV, 1, 4096, D),
     "decode_B16": (16, H_Q, H_KV, 1, 4096, D),
