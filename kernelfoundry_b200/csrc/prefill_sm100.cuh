@@ -974,6 +974,15 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                             L += don.w[d] * ld[d];
                         }
                         const float osc = (p.flags & KF_PF_UNNORMALIZED) ? 1.0f : 1.0f / L;
+                        auto store_ml = [&]() {
+                            if (store) {
+                                if (p.Mi) p.Mi[mi] = M * p.scale;
+                                if (p.Li) p.Li[mi] = L;
+                            }
+                        };
+                        // Key-half units write the row's (M, L) before the O store: kept live
+                        // across it, the row's index spilled in that instance.
+                        if constexpr (KVH) store_ml();
 #pragma unroll
                         for (int d = 0; d < 3; ++d) {
                             don.w[d] *= osc;
@@ -1007,10 +1016,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                                 }
                             }
                         }
-                        if (store) {
-                            if (p.Mi) p.Mi[mi] = M * p.scale;
-                            if (p.Li) p.Li[mi] = L;
-                        }
+                        if constexpr (!KVH) store_ml();
                     }
                 } else {
                     // Donor (or an owner past its wait): this tile's partial, then a ticket.
