@@ -207,7 +207,7 @@ struct DonorRows {
 template <int D, int BM, int SLOT_BYTES>
 __device__ __forceinline__ void stage_store_tile(uint8_t* slot, uint32_t tO, int row, int bar, float sc, int out,
                                                  const CUtensorMap* map, int c1, int c2,
-                                                 const DonorRows& don = DonorRows{}) {
+                                                 const DonorRows& don = DonorRows{}, uint8_t* slot2 = nullptr) {
     // o[0..31] = sc * O[cols c0 .. c0+31] (+ the donors' rows), in place.
     auto add_donors = [&](uint32_t (&o)[32], int c0) {
 #pragma unroll
@@ -233,11 +233,14 @@ __device__ __forceinline__ void stage_store_tile(uint8_t* slot, uint32_t tO, int
     const int n_pass = (n_spans + SPP - 1) / SPP;
 #pragma unroll 1
     for (int ps = 0; ps < n_pass; ++ps) {
+        // With a second slot, pass 1 is built there while pass 0's stores still read the
+        // first; the wait after pass 1 covers both.
+        uint8_t* sl = (slot2 != nullptr && ps == 1) ? slot2 : slot;
         const int k_end = min(SPP, n_spans - ps * SPP);
 #pragma unroll 1
         for (int k = 0; k < k_end; ++k) {
             const int sp = ps * SPP + k;
-            uint8_t* rowp = slot + k * SPAN + row * 128;
+            uint8_t* rowp = sl + k * SPAN + row * 128;
             if (out == KF_OUT_F32) {
                 uint32_t o[32];
                 tmem_ld32(tO + sp * 32, o);
@@ -274,12 +277,13 @@ __device__ __forceinline__ void stage_store_tile(uint8_t* slot, uint32_t tO, int
         }
         fence_proxy_async_smem();
         named_bar_sync(bar, 128);
+        const bool overlap = slot2 != nullptr && ps == 0 && n_pass > 1;    // pass 1 goes to slot2
         if (row == 0) {
-            for (int k = 0; k < k_end; ++k) tma_store_3d(map, slot + k * SPAN, (ps * SPP + k) * cols, c1, c2);
+            for (int k = 0; k < k_end; ++k) tma_store_3d(map, sl + k * SPAN, (ps * SPP + k) * cols, c1, c2);
             bulk_commit_group();
-            bulk_wait_group_read0();
+            if (!overlap) bulk_wait_group_read0();
         }
-        if (ps + 1 < n_pass) named_bar_sync(bar, 128);    // slot read: next pass may write it
+        if (!overlap && ps + 1 < n_pass) named_bar_sync(bar, 128);    // slots read: next pass may write
     }
 }
 
@@ -448,10 +452,13 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                             tma_prefetch_l2_3d(map, s * SWE, (it.kt0 + tile + C::L2AHEAD) * BC, bh_kv);
                 }
                 if (!ok) break;
-                if constexpr (KVH) {
-                    // The merged tile is staged (by tile 0) in the slot of the last first-half K.
+                if constexpr (KVH && C::TMA_STORE) {
+                    // The merged tile is staged (by tile 0) in the slots of the last step's two
+                    // K tiles: the first half's (released on stage_free[0]) and the second
+                    // half's (on stage_free[1], which key-half units use for nothing else).
                     pend[0] |= 1u << ((pos - 4) % NSLOT);
-                } else if constexpr (C::TMA_STORE) {
+                    pend[1] |= 1u << ((pos - 3) % NSLOT);
+                } else if constexpr (!KVH && C::TMA_STORE) {
                     // The item's epilogue stages tile 0 in the slot of its last K and tile 1
                     // in the slot of its last V.
                     pend[0] |= 1u << ((pos - 2 - 2 * (it.n_kv - it.n_kv0)) % NSLOT);
@@ -819,11 +826,16 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             const bool split = ie.split;
             // Staging slot of this tile: the ring slot of the item's last K (tile 0) or
             // last V (tile 1); every MMA reading it completed before o_full[t] fired.  KVH:
-            // the slot of the last first-half K, for tile 0 (the one that stores).
+            // the slots of the last first-half K and second-half K (stage2), for tile 0 (the
+            // one that stores): both were last read by QKs issued before tile 0's last P.V.
+            // The split owner's merge stages in the first only (the second in both staged
+            // stores spilled), and releases both.
             // (Causal: tile 0 stages in the slot of its own last K, whose QKs were issued before
             // its o_full; the item's later loads stay within the ring depth of it.)
             uint8_t* stage = sKV + ((KVH ? pos - 4 : t == 0 ? pos - 2 - 2 * (ie.n_kv - ie.n_kv0) : pos - 1) % NSLOT) *
                                    C::KV_BYTES;
+            // (Formed where it is used, from pos: a pointer held across the merge spills.)
+            auto stage2 = [&]() -> uint8_t* { return KVH ? sKV + ((pos - 3) % NSLOT) * C::KV_BYTES : nullptr; };
             const int qrow = q_row0 + (KVH ? 0 : t * BM) + row;
             const bool store = qrow < p.S_q;
             const size_t orow = ((static_cast<size_t>(b) * p.H_q + h) * p.S_q + (store ? qrow : 0)) * D;   // element index
@@ -875,8 +887,11 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                             l_true = L;
                         } else if constexpr (C::TMA_STORE) {
                             stage_store_tile<D, BM, C::KV_BYTES>(stage, tO, row, 2, osc, p.out_type, &tmO, q_row0,
-                                                                b * p.H_q + h);
-                            if (row == 0) mbar_arrive(&stage_free[0]);
+                                                                b * p.H_q + h, DonorRows{}, stage2());
+                            if (row == 0) {
+                                mbar_arrive(&stage_free[0]);
+                                mbar_arrive(&stage_free[1]);
+                            }
                         } else {
 #pragma unroll
                             for (int dc = 0; dc < D / OCH; ++dc) {
@@ -992,7 +1007,10 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                         if constexpr (C::TMA_STORE) {
                             stage_store_tile<D, BM, C::KV_BYTES>(stage, tO, row, 2 + t, f * w_own * osc, p.out_type,
                                                                 &tmO, q_row0 + t * BM, b * p.H_q + h, don);
-                            if (row == 0) mbar_arrive(&stage_free[t]);
+                            if (row == 0) {
+                                mbar_arrive(&stage_free[t]);
+                                if constexpr (KVH) mbar_arrive(&stage_free[1]);
+                            }
                         } else {
                             const float so = f * w_own * osc;
 #pragma unroll
@@ -1035,7 +1053,10 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                         }
                         *ml_part(chunk) = make_float2(m_true, l_true);
                         if constexpr (C::TMA_STORE) {
-                            if (row == 0) mbar_arrive(&stage_free[t]);    // the staging slot was not used
+                            if (row == 0) {                    // the staging slots were not used
+                                mbar_arrive(&stage_free[t]);
+                                if constexpr (KVH) mbar_arrive(&stage_free[1]);
+                            }
                         }
                     }
                     __threadfence();

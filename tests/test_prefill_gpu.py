@@ -430,8 +430,11 @@ def test_causal_chunked_prefill_split(cuda, shape, merge, monkeypatch):
     assert ma <= 2e-3 and rl <= 1e-3, (ma, rl)
 
 
+# (8, 32, 8, 128, 512, 16): D = 16 (no staged store) with two items on most CTAs;
+# (8, 32, 8, 128, 1024, 64): the eight-slot ring of D = 64 over several items.
 SHORT_CHUNKS = [(1, 32, 8, 128, 4096, 128), (2, 8, 2, 100, 2048, 64), (1, 16, 4, 128, 3000, 128),
-                (1, 8, 8, 64, 1024, 16), (8, 32, 8, 128, 1024, 128), (3, 8, 2, 128, 512, 128)]
+                (1, 8, 8, 64, 1024, 16), (8, 32, 8, 128, 1024, 128), (3, 8, 2, 128, 512, 128),
+                (8, 32, 8, 128, 512, 16), (8, 32, 8, 128, 1024, 64)]
 
 
 @pytest.mark.parametrize("merge", ["owner", "ticket"])
