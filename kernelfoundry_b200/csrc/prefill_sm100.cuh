@@ -336,7 +336,17 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         return r * G + ((r & 1) ? G - 1 - c : c);
     };
 
+    // Key-half units (short calls, one or two items per CTA): the producer skips the
+    // set-up barrier of the TMEM allocation, which it does not use, and its tensor maps
+    // (kernel parameters) start loading at entry.  (Measured: C1 +2 %; no gain for the
+    // long-unit kernels, whose prologue runs once per CTA: they keep the plain set-up.)
+    constexpr bool EARLY = KVH;
     if (threadIdx.x == 0) {
+        if constexpr (EARLY) {
+            tma_prefetch_desc(&tmQ);
+            tma_prefetch_desc(&tmK);
+            tma_prefetch_desc(&tmV);
+        }
         for (int t = 0; t < NQ; ++t) {
             mbar_init(&q_full[t], 1);
             mbar_init(&s_full[t], 1);
@@ -364,18 +374,33 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             reinterpret_cast<uint4*>(sQ)[i] = make_uint4(0, 0, 0, 0);
         fence_proxy_async_smem();
     }
+    if constexpr (EARLY) __syncthreads();    // barrier inits (and zero fill) seen by every thread
     // Set-up above touches shared memory only.  Global memory, and TMEM (which a CTA of
     // the previous launch on this SM may still hold), come after the previous launch on
     // the stream has completed.
     grid_dep_wait();
     grid_dep_launch_dependents();
-    if (warp == 1) {
-        tmem_alloc(tmem_slot, C::TMEM_COLS);
-        tmem_relinquish();
+    if constexpr (EARLY) {
+        // The producer (warp 0) starts at once; the other warps wait for the TMEM
+        // allocation on named barrier 1.
+        if (warp != 0) {
+            if (warp == 1) {
+                tmem_alloc(tmem_slot, C::TMEM_COLS);
+                tmem_relinquish();
+            }
+            tc_fence_before();
+            named_bar_sync(1, C::THREADS - 32);
+            tc_fence_after();
+        }
+    } else {
+        if (warp == 1) {
+            tmem_alloc(tmem_slot, C::TMEM_COLS);
+            tmem_relinquish();
+        }
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
     }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
     // The TMEM base is read from shared memory inside each role (after its setmaxnreg),
     // not held in a register across the register reallocation.
     auto tmem_base = [&]() { return *reinterpret_cast<volatile uint32_t*>(tmem_slot); };
@@ -384,9 +409,11 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         // ------------------------------------------------------------ TMA producer
         if constexpr (C::REBALANCE) setmaxnreg_dec<C::REG_CTRL>();
         if (lane == 0) {
-            tma_prefetch_desc(&tmQ);
-            tma_prefetch_desc(&tmK);
-            tma_prefetch_desc(&tmV);
+            if constexpr (!EARLY) {
+                tma_prefetch_desc(&tmQ);
+                tma_prefetch_desc(&tmK);
+                tma_prefetch_desc(&tmV);
+            }
             const uint32_t q_bytes = NSPAN * p.q_box * SWB;
             const uint32_t kv_bytes = NSPAN * p.kv_box * SWB;
             int pos = 0;                          // ring position of the next K/V load
