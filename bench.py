@@ -833,8 +833,12 @@ def run_ours(args):
     achieved = flops_rank / (kern_ms * 1e-3) / 1e12
     traffic = profile_traffic("prefill_sm100_C2.md")
     from kernelfoundry_b200 import plan
-    split = plan(1, H_Q, H_KV, S, S, D)["ctas"] > plan(1, H_Q, H_KV, S, S, D, workspace_bytes=0)["ctas"]
-    kernel_name = f"kf::prefill_fwd_kernel<128, false, {'true' if split else 'false'}>"
+    unsplit_ctas = plan(1, H_Q, H_KV, S, S, D, workspace_bytes=0)["ctas"]
+    split = plan(1, H_Q, H_KV, S, S, D)["ctas"] > unsplit_ctas
+    # One-tile units with an even count of 128-key tiles run as key-half units (KVH).
+    kvh = unsplit_ctas == H_Q * ((S + 127) // 128) and ((S + 127) // 128) % 2 == 0
+    tf = lambda x: "true" if x else "false"  # noqa: E731
+    kernel_name = f"kf::prefill_fwd_kernel<128, false, {tf(split)}, {tf(kvh)}>"
 
     roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"],
                 "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": traffic,

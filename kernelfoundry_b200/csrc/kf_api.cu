@@ -1442,6 +1442,26 @@ int kf_fill_normal_f16(uint16_t* dst, long long n, unsigned long long seed, long
     return e == cudaSuccess ? KF_OK : cuda_fail(e);
 }
 
+#ifdef KF_PREFILL_TRACE
+// Developer builds only (python -m kernelfoundry_b200.phase_trace): the prefill kernels'
+// per-CTA phase stamps (kf::PrefillTracePoint slots of kf::kTrSlots words per CTA, global
+// timer ns, 0 = phase not reached).  Not declared in include/: the shipped library lacks them.
+int kf_prefill_trace_read(unsigned long long* host, int n_ctas) {
+    if (!host || n_ctas <= 0 || n_ctas > kf::kTraceCtas) return KF_ERR_INVALID_ARG;
+    cudaError_t e = cudaMemcpyFromSymbol(host, kf::g_kf_prefill_trace,
+                                         static_cast<size_t>(n_ctas) * kf::kTrSlots * sizeof(unsigned long long));
+    return e == cudaSuccess ? KF_OK : cuda_fail(e);
+}
+
+int kf_prefill_trace_clear(void) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, kf::g_kf_prefill_trace);
+    if (e == cudaSuccess) e = cudaMemset(ptr, 0, sizeof(kf::g_kf_prefill_trace));
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    return e == cudaSuccess ? KF_OK : cuda_fail(e);
+}
+#endif
+
 int kf_selftest_wait_timeout(unsigned long long timeout_ns, void* stream) {
     DeviceInfo* di = nullptr;
     int rc = device_info(&di);

@@ -37,6 +37,34 @@
 
 namespace kf {
 
+// Phase trace (developer builds only: -DKF_PREFILL_TRACE, see phase_trace.py): one
+// global-timer stamp per phase and CTA, for the CTA's last item.  Without the macro every
+// KF_TRACE is empty and the kernels are unchanged.
+enum PrefillTracePoint {
+    kTrEntry, kTrSetup, kTrProdQ, kTrMmaQ, kTrMmaK0, kTrFirstS0, kTrFirstS1, kTrOFull0, kTrOFull1,
+    kTrHalvesMet, kTrHalvesMerged, kTrOwnerWaited, kTrPartialWritten, kTrTicket, kTrItemEnd0,
+    kTrItemEnd1, kTrExit, kTrProdRegs, kTrProdItem, kTrPassBuilt0, kTrPassStored0, kTrPassBuilt1,
+    kTrPassStored1, kTrSmid, kTrSlots = 32
+};
+constexpr int kTraceCtas = 1024;
+#ifdef KF_PREFILL_TRACE
+__device__ unsigned long long g_kf_prefill_trace[kTraceCtas * kTrSlots];
+#define KF_TRACE(i)                                                                                   \
+    do {                                                                                              \
+        if (blockIdx.x < kTraceCtas) g_kf_prefill_trace[blockIdx.x * kTrSlots + (i)] = global_timer_ns(); \
+    } while (0)
+#define KF_TRACE_SMID()                                                                               \
+    do {                                                                                              \
+        unsigned smid_;                                                                               \
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid_));                                            \
+        KF_TRACE(kTrEntry);                                                                           \
+        if (blockIdx.x < kTraceCtas) g_kf_prefill_trace[blockIdx.x * kTrSlots + kTrSmid] = smid_;     \
+    } while (0)
+#else
+#define KF_TRACE(i) do { } while (0)
+#define KF_TRACE_SMID() do { } while (0)
+#endif
+
 template <int D>
 struct PrefillCfg {
     static constexpr int BM = 128;                     // query rows per tile (UMMA M)
@@ -275,6 +303,7 @@ __device__ __forceinline__ void stage_store_tile(uint8_t* slot, uint32_t tO, int
                 }
             }
         }
+        if (row == 0) KF_TRACE(kTrPassBuilt0 + 2 * (ps & 1));
         fence_proxy_async_smem();
         named_bar_sync(bar, 128);
         const bool overlap = slot2 != nullptr && ps == 0 && n_pass > 1;    // pass 1 goes to slot2
@@ -282,6 +311,7 @@ __device__ __forceinline__ void stage_store_tile(uint8_t* slot, uint32_t tO, int
             for (int k = 0; k < k_end; ++k) tma_store_3d(map, sl + k * SPAN, (ps * SPP + k) * cols, c1, c2);
             bulk_commit_group();
             if (!overlap) bulk_wait_group_read0();
+            KF_TRACE(kTrPassStored0 + 2 * (ps & 1));
         }
         if (!overlap && ps + 1 < n_pass) named_bar_sync(bar, 128);    // slots read: next pass may write
     }
@@ -329,6 +359,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) KF_TRACE_SMID();
     // Item of round r of this CTA: rounds alternate direction over the CTAs (snake
     // order), so with items sorted heaviest first (causal) every CTA's total balances.
     auto prefill_item_index = [](int r) {
@@ -401,6 +432,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         __syncthreads();
         tc_fence_after();
     }
+    if (threadIdx.x == 32) KF_TRACE(kTrSetup);         // the MMA warp, past the set-up barrier
     // The TMEM base is read from shared memory inside each role (after its setmaxnreg),
     // not held in a register across the register reallocation.
     auto tmem_base = [&]() { return *reinterpret_cast<volatile uint32_t*>(tmem_slot); };
@@ -408,6 +440,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
         if constexpr (C::REBALANCE) setmaxnreg_dec<C::REG_CTRL>();
+        if (lane == 0) KF_TRACE(kTrProdRegs);
         if (lane == 0) {
             if constexpr (!EARLY) {
                 tma_prefetch_desc(&tmQ);
@@ -429,6 +462,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 const PrefillItem it = prefill_item<D, CAUSAL, SPLIT, KVH>(p, item);
                 const int bh_q = it.b * p.H_q + it.h;
                 const int bh_kv = it.b * p.H_kv + it.h_kv;
+                if (n_done == 0) KF_TRACE(kTrProdItem);
                 // Q of this item once the previous item's QK MMAs stopped reading Q.
                 if (n_done > 0 && !mbar_wait_bounded(q_empty, (n_done - 1) & 1, abort_flag, p.timeout_ns)) {
                     atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_MMA); ok = false; break;
@@ -441,6 +475,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                         tma_load_3d(sQ + t * C::Q_BYTES + s * BM * SWB, &tmQ, &q_full[t], s * SWE,
                                     it.q_row0 + t * BM, bh_q);
                     ++q_cnt[t];
+                    if (n_done == 0) KF_TRACE(kTrProdQ);
                 }
                 for (int i = 0; i < (KVH ? 4 : 2) * it.n_kv; ++i, ++pos) {
                     const int slot = pos % NSLOT;
@@ -536,6 +571,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     ++q_cnt[t];
                 }
                 if (!ok) { atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_TMA); break; }
+                KF_TRACE(kTrMmaQ);
                 if constexpr (KVH) {
                     // Two key halves of one query tile: step j reads K_t(j) at ring position
                     // ring + 4j + t and V_t(j - 1) at ring + 4(j - 1) + 2 + t; both tiles' QK use
@@ -558,6 +594,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                         }
                         if (!ok) { atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_TMA); break; }
                         tc_fence_after();
+                        if (j == 0) KF_TRACE(kTrMmaK0);
 #pragma unroll
                         for (int t = 0; t < 2; ++t) {
                             const uint32_t tS = tmem + t * BC;
@@ -719,6 +756,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 ok = mbar_wait_bounded(&s_full[t], (sst + j) & 1, abort_flag, p.timeout_ns);
                 ok = __all_sync(0xffffffffu, ok);
                 if (!ok) { atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_MMA); break; }
+                if (j == 0 && row == 0) KF_TRACE(kTrFirstS0 + t);
                 tc_fence_after();
                 uint32_t sr[BC];
 #pragma unroll
@@ -841,6 +879,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                 if (!ok) atomicOr(&g_kf_dev_error, KF_DEVERR_TIMEOUT_MMA);
             }
             ++o_cnt;
+            if (row == 0) KF_TRACE(kTrOFull0 + t);
             // Rebase to the true row max: O_t * f and l * f are relative to m_true.
             float f = ex2_approx((m_ref - m_true) * c);
             float l_true = l * f;
@@ -882,6 +921,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     tc_fence_before();
                 }
                 ok = named_bar_and(4, 256, ok);
+                if (row == 0 && t == 0) KF_TRACE(kTrHalvesMet);
                 if (t == 0) {
                     tc_fence_after();
                     const float4 ob = xch[row];
@@ -904,6 +944,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                             tmem_st_chunk<RCH>(tO + dc * RCH, oa);
                         }
                         tmem_wait_st();
+                        if (row == 0) KF_TRACE(kTrHalvesMerged);
                         if (split) {
                             // A split chunk: the merged tile goes on to the split epilogue below
                             // as this chunk's tile 0 (O relative to M, sum L).
@@ -987,6 +1028,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                         }
                         if (got) *counter = 0u;          // every donor has added: zero for the next call
                         *flag = got;
+                        KF_TRACE(kTrOwnerWaited);
                     }
                     named_bar_sync(2 + t, 128);
                     owner_merge = *flag != 0;
@@ -1079,6 +1121,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                                                 __uint_as_float(o[kk + 2]) * f, __uint_as_float(o[kk + 3]) * f);
                         }
                         *ml_part(chunk) = make_float2(m_true, l_true);
+                        if (row == 0) KF_TRACE(kTrPartialWritten);
                         if constexpr (C::TMA_STORE) {
                             if (row == 0) {                    // the staging slots were not used
                                 mbar_arrive(&stage_free[t]);
@@ -1092,6 +1135,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                         int last = 0;
                         if (!*abort_flag) last = atomicAdd(counter, 1u) == static_cast<unsigned>(k - 1);
                         *flag = last;
+                        KF_TRACE(kTrTicket);
                     }
                     named_bar_sync(2 + t, 128);
                     const bool last = *flag != 0;
@@ -1167,10 +1211,12 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                     }
                 }
             }
+            if (row == 0) KF_TRACE(kTrItemEnd0 + t);
             tc_fence_before();
         }
     }
     __syncthreads();
+    if (threadIdx.x == 0) KF_TRACE(kTrExit);
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base(), C::TMEM_COLS);
