@@ -356,6 +356,8 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* ticket_last = abort_flag + 1;     // one flag per tile
+    PrefillItem* first_item = reinterpret_cast<PrefillItem*>(const_cast<int*>(ticket_last) + 2);   // EARLY
+    static_assert((6 * NQ + 2 * NSLOT + 2) * 8 + 16 + sizeof(PrefillItem) <= C::BAR_BYTES, "barrier area");
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -377,6 +379,10 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             tma_prefetch_desc(&tmQ);
             tma_prefetch_desc(&tmK);
             tma_prefetch_desc(&tmV);
+            // The producer's first item, decoded now (kernel parameters only) and parked in
+            // shared memory: its Q load then issues as soon as the producer starts.
+            if (static_cast<int>(blockIdx.x) < p.n_items)
+                *first_item = prefill_item<D, CAUSAL, SPLIT, KVH>(p, static_cast<int>(blockIdx.x));
         }
         for (int t = 0; t < NQ; ++t) {
             mbar_init(&q_full[t], 1);
@@ -459,7 +465,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
             for (int rnd = 0; rnd * static_cast<int>(gridDim.x) < p.n_items && ok; ++rnd) {
                 const int item = prefill_item_index(rnd);
                 if (item >= p.n_items) continue;
-                const PrefillItem it = prefill_item<D, CAUSAL, SPLIT, KVH>(p, item);
+                const PrefillItem it = (EARLY && rnd == 0) ? *first_item : prefill_item<D, CAUSAL, SPLIT, KVH>(p, item);
                 const int bh_q = it.b * p.H_q + it.h;
                 const int bh_kv = it.b * p.H_kv + it.h_kv;
                 if (n_done == 0) KF_TRACE(kTrProdItem);
