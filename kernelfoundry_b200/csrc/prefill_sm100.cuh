@@ -369,7 +369,7 @@ prefill_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         return r * G + ((r & 1) ? G - 1 - c : c);
     };
 
-    // Key-half units (short calls, one or two items per CTA): the producer skips the
+    // Key-half units (short calls, few items per CTA): the producer skips the
     // set-up barrier of the TMEM allocation, which it does not use, and its tensor maps
     // (kernel parameters) start loading at entry.  (Measured: C1 +2 %; no gain for the
     // long-unit kernels, whose prologue runs once per CTA: they keep the plain set-up.)
